@@ -1,0 +1,27 @@
+"""Loads the committed golden fixtures and rebuilds their inputs."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+
+from miniserve_b200 import workloads
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sampler_golden.json")
+
+
+def load():
+    with open(GOLDEN) as f:
+        return json.load(f)
+
+
+def expected_token(t):
+    """Reference token, or -1 where the reference raised ZeroDivisionError."""
+    return -1 if t == "ZeroDivisionError" else int(t)
+
+
+def config_batch(entry):
+    g = dict(entry["gen"])
+    fn = getattr(workloads, g.pop("fn"))
+    return fn(**g)
