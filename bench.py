@@ -1,0 +1,343 @@
+"""Benchmark: logits rows sampled/sec at 512 x 151936 (heterogeneous top-k/top-p).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one batched sampling call over the 512-row fp32 batch of the
+heterogeneous configuration (Zipf-like logits; per-row top_k in
+{0,1,20,50,200}, top_p ~ U(0.5,1], temperature ~ U(0.2,1.5); seeded
+synthetic data).  The 311 MB batch is larger than the 126 MB L2, so no flush
+is needed between steps.
+
+`value` is device-resident throughput (inputs already in HBM), timed with CUDA
+events on the launching stream.  `e2e` goes through the public
+``Sampler.sample_batch`` API from pinned host memory: every step copies the
+logits and per-row parameters host->device and reads tokens, probabilities and
+statuses back, inside the timed region.  Under torchrun each rank samples its
+own batch (rows are independent; no collective on the data path), timing is
+the max over ranks and `value` the total rows of all ranks over that time.
+
+`--impl reference` times the reference algorithm on the host cores instead:
+the float64 Python restatement of miniserve's Sampler.sample (oracle/, the
+reference is Python) over a bounded sample of the same rows, one process per
+core.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "logits rows sampled/sec at 512x151936 top-k/top-p; % of B200 HBM roofline"
+WORKLOAD = "config3: 512x151936 fp32, heterogeneous per-row top_k/top_p/temperature"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ----------------------------------------------------------------- CPU side
+def _ref_rows(args):
+    """Worker: the reference algorithm (Python float64 restatement) on rows."""
+    logits, T, K, P, U = args
+    from oracle import sampler_oracle as so
+    out = []
+    for b in range(len(T)):
+        out.append(so.sample_row(logits[b].tolist(), float(T[b]), int(K[b]), float(P[b]), float(U[b])).token)
+    return out
+
+
+def cpu_reference_rate(batch, rows, pool, cores):
+    """rows/s of the reference algorithm on `rows`, spread over `cores` processes."""
+    chunks = [rows[i::cores] for i in range(cores)]
+    chunks = [c for c in chunks if len(c)]
+    jobs = [(batch.logits[c], batch.temperature[c], batch.top_k[c], batch.top_p[c], batch.uniforms[c])
+            for c in chunks]
+    t0 = time.perf_counter()
+    pool.map(_ref_rows, jobs)
+    dt = time.perf_counter() - t0
+    return len(rows) / dt, dt
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ----------------------------------------------------------------- GPU side
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from miniserve_b200 import Sampler, _lib, workloads
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cores = os.cpu_count() or 1
+    pool = None
+    if rank == 0 and not args.no_cpu_baseline:
+        pool = mp.get_context("spawn").Pool(cores)  # started before GPU work
+        pool.map(int, range(cores))
+    batch = workloads.config3(3 + rank)
+    B, V = batch.B, batch.V
+    sampler = Sampler()
+    L = _lib.lib()
+    x = torch.from_numpy(batch.logits).to(dev)
+    T = torch.from_numpy(batch.temperature).to(dev)
+    K = torch.from_numpy(batch.top_k).to(dev)
+    P = torch.from_numpy(batch.top_p).to(dev)
+    U = torch.from_numpy(batch.uniforms).to(dev)
+    tok = torch.empty(B, dtype=torch.int64, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    def step():
+        rc = L.ms_sample(x.data_ptr(), 0, B, V, V, T.data_ptr(), K.data_ptr(), P.data_ptr(), U.data_ptr(),
+                         None, 0, tok.data_ptr(), prob.data_ptr(), st.data_ptr(), sptr)
+        if rc != 0:
+            _lib.check(rc, "ms_sample")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local_rank) as clocks:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    per_launch = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    elapsed_ms = evs[0].elapsed_time(evs[-1])
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_step = max_ms / args.steps
+    value = world * B * args.steps / (max_ms / 1e3)
+
+    # correctness spot check of the timed outputs against the pinned oracle
+    # is done by the tests; here only the row statuses are checked
+    assert int((st != 0).sum().item()) == 0
+
+    # ------------------------------------------------------------ e2e (host buffers)
+    pin = lambda a: torch.from_numpy(a).pin_memory()
+    hx, hT, hK, hP, hU = (pin(batch.logits), pin(batch.temperature), pin(batch.top_k),
+                          pin(batch.top_p), pin(batch.uniforms))
+    otok = torch.empty(B, dtype=torch.int64).pin_memory()
+    oprob = torch.empty(B, dtype=torch.float32).pin_memory()
+    ost = torch.empty(B, dtype=torch.int32).pin_memory()
+    dx = torch.empty_like(x)
+    dT, dK, dP, dU = (torch.empty_like(T), torch.empty_like(K), torch.empty_like(P), torch.empty_like(U))
+    h2d = sum(a.numel() * a.element_size() for a in (hx, hT, hK, hP, hU))
+    d2h = sum(a.numel() * a.element_size() for a in (otok, oprob, ost))
+
+    def e2e_step():
+        for d, h in ((dx, hx), (dT, hT), (dK, hK), (dP, hP), (dU, hU)):
+            d.copy_(h, non_blocking=True)
+        t_, p_, s_ = sampler.sample_batch(dx, dT, dK, dP, uniforms=dU, out=(tok, prob, st))
+        otok.copy_(t_, non_blocking=True)
+        oprob.copy_(p_, non_blocking=True)
+        ost.copy_(s_, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 10))
+    for _ in range(min(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * e2e_steps / (float(te.item()) / 1e3)
+    assert np.array_equal(otok.numpy(), tok.cpu().numpy())
+
+    if rank != 0:
+        return None
+    # roofline of the sampling kernel: algorithmic bytes per launch / launch time
+    alg_bytes = B * (V * 4 + 8 + 4 + 8 + 8 + 8 + 4 + 4)
+    avg_launch_ms = sum(per_launch) / len(per_launch)
+    achieved = alg_bytes / (avg_launch_ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    cpu = None
+    if pool is not None:
+        sample_rows = list(range(min(B, max(2 * cores, 16))))
+        rate, dt = cpu_reference_rate(batch, sample_rows, pool, cores)
+        cpu = {"value": round(rate, 3), "unit": "rows/s", "cores": cores, "kind": "port",
+               "sample": f"{len(sample_rows)} rows of the same batch, reference float64 Python "
+                         f"restatement, {cores} processes, {dt:.1f}s"}
+        pool.close()
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Zipf-like logits, no dataset exists for this path)",
+        "config": {"workload": WORKLOAD, "batch_rows": B, "vocab": V, "global_batch": B * world,
+                   "parallelism": f"dp{world} (independent rows per rank)",
+                   "l2": "inputs (311 MB) larger than L2 (126 MB); no flush"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                     "alg_bytes_per_launch": alg_bytes, "avg_launch_us": round(avg_launch_ms * 1e3, 2)},
+        "e2e": {"value": round(e2e_value, 1), "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * launches_per_call(),
+        "clocks": clocks.summary(),
+    }
+
+
+def launches_per_call():
+    return 1
+
+
+def run_reference(args, rank):
+    """Reference arm: the reference algorithm on host cores, bounded sample per step."""
+    from miniserve_b200 import workloads
+    if rank != 0:
+        return None
+    cores = os.cpu_count() or 1
+    pool = mp.get_context("spawn").Pool(cores)
+    batch = workloads.config3(3)
+    n = min(batch.B, max(cores, 8))
+    rows = list(range(n))
+    for _ in range(args.warmup):
+        cpu_reference_rate(batch, rows[: min(n, cores)], pool, cores)
+    times = []
+    for s in range(args.steps):
+        rr = [(r + s * n) % batch.B for r in rows]
+        t0 = time.perf_counter()
+        cpu_reference_rate(batch, rr, pool, cores)
+        times.append(time.perf_counter() - t0)
+    pool.close()
+    total = sum(times)
+    value = n * args.steps / total
+    sample = (f"{n} rows per step of the 512-row batch, float64 Python restatement of "
+              f"miniserve Sampler.sample, {cores} processes")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded Zipf-like logits)",
+        "config": {"workload": WORKLOAD, "batch_rows": batch.B, "vocab": batch.V},
+        "cpu_baseline": {"value": round(value, 3), "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        out = run_reference(args, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        out = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

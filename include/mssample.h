@@ -1,0 +1,95 @@
+/*
+ * mssample.h -- C ABI of the B200 token-sampling library (libmssample.so).
+ *
+ * Drop-in boundary for miniserve's sampling hot path.  Each entry point
+ * replaces one reference interface, cited below by file:line of the
+ * miniserve project:
+ *
+ *   ms_sample            Sampler.sample (miniserve/sampler.py:23-68), batched:
+ *                        one token per row of a [B, V] logits matrix, with
+ *                        per-row temperature / top_k / top_p and a
+ *                        caller-supplied uniform per row (the value
+ *                        random.Random(seed).random() the reference draws at
+ *                        miniserve/sampler.py:32,62).  With a mask it also
+ *                        applies the logits-processor hook's -inf convention
+ *                        (miniserve/model_runner.py:214-216) before sampling.
+ *                        Serves the sample_fn(out, plan) -> List[int] seam of
+ *                        OverlapEngine (miniserve/overlap.py:109-112).
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer owned by the caller.
+ *   - Launches are asynchronous on `stream`; nothing is synchronised.
+ *   - Return value: MS_OK, or a negative MS_E_* for argument or launch errors
+ *     detected on the host before/at launch.
+ *   - Per-row conditions are reported in row_status (MS_ROW_* bits); a row
+ *     with a non-zero status other than MS_ROW_NONFINITE gets token -1.
+ *   - No global mutable state: calls from several host threads on different
+ *     streams are safe.
+ */
+#ifndef MSSAMPLE_H
+#define MSSAMPLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ms_stream_t; /* == cudaStream_t */
+
+enum {
+  MS_OK = 0,
+  MS_E_INVALID = -1,     /* null pointer, B < 0, V < 1, ld < V, V >= 2^31 ... */
+  MS_E_DTYPE = -2,       /* dtype not MS_DTYPE_F32 / MS_DTYPE_BF16 */
+  MS_E_CUDA = -3,        /* a CUDA call failed (see ms_last_cuda_error) */
+  MS_E_UNSUPPORTED = -4  /* valid request outside what this build handles */
+};
+
+enum { MS_DTYPE_F32 = 0, MS_DTYPE_BF16 = 1 };
+
+/* row_status bits */
+enum {
+  MS_ROW_OK = 0,
+  MS_ROW_ALL_MASKED = 1,      /* temperature > 0 and every logit is -inf/masked:
+                                 the reference raises ZeroDivisionError
+                                 (miniserve/sampler.py:46-47) */
+  MS_ROW_BAD_TEMPERATURE = 2, /* temperature < 0, NaN or infinite */
+  MS_ROW_NONFINITE = 4        /* a NaN or +inf logit was present; NaN is read
+                                 as -inf (the reference's result is arbitrary) */
+};
+
+/*
+ * Sample one token per row.
+ *
+ *   logits       [B, ld] row-major, fp32 (dtype 0) or bf16 (dtype 1); the
+ *                first V entries of each row are the vocabulary.
+ *   temperature  [B] f64; 0 selects greedy argmax (first maximal index).
+ *   top_k        [B] i32; <= 0 or >= V disables (miniserve/sampler.py:37).
+ *   top_p        [B] f64; >= 1 (or NaN) disables (miniserve/sampler.py:49).
+ *   uniforms     [B] f64 in [0, 1).
+ *   mask         optional [B, mask_ld] u32 bitmask, bit (i & 31) of word
+ *                (i >> 5) set = token i allowed; NULL = all allowed.
+ *   tokens       [B] i64 out; probs [B] f32 out (final renormalised
+ *                probability of the returned token, 1 for greedy);
+ *   row_status   [B] i32 out.
+ */
+int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+              const double *temperature, const int32_t *top_k, const double *top_p,
+              const double *uniforms, const uint32_t *mask, int64_t mask_ld, int64_t *tokens,
+              float *probs, int32_t *row_status, ms_stream_t stream);
+
+/* Human-readable text for an MS_E_* code. */
+const char *ms_error_string(int code);
+
+/* cudaError_t of the most recent failed CUDA call in this thread (0 if none). */
+int ms_last_cuda_error(void);
+
+/* Library version, e.g. 100 for 0.1.0. */
+int ms_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSSAMPLE_H */

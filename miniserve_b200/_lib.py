@@ -1,0 +1,69 @@
+"""ctypes binding of libmssample.so (the C ABI in include/mssample.h).
+
+There is no fallback: if the library is missing or no CUDA device is
+present, every sampling call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmssample.so")
+
+MS_OK = 0
+MS_DTYPE_F32 = 0
+MS_DTYPE_BF16 = 1
+MS_ROW_OK = 0
+MS_ROW_ALL_MASKED = 1
+MS_ROW_BAD_TEMPERATURE = 2
+MS_ROW_NONFINITE = 4
+
+_lock = threading.Lock()
+_lib = None
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+
+# name -> (restype, argtypes); every function include/mssample.h declares
+SIGNATURES = {
+    "ms_sample": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64,
+                                 _P, _P, _P, _P]),
+    "ms_error_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "ms_last_cuda_error": (ctypes.c_int, []),
+    "ms_version": (ctypes.c_int, []),
+}
+
+
+class SamplerLibraryError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load libmssample.so once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise SamplerLibraryError(
+                    f"{LIB_PATH} is missing: build it with `python -m miniserve_b200.build` "
+                    "(there is no CPU fallback)")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != MS_OK:
+        L = lib()
+        msg = L.ms_error_string(rc).decode()
+        if rc == -3:
+            msg += f" (cudaError {L.ms_last_cuda_error()})"
+        raise SamplerLibraryError(f"{what} failed: {msg}")

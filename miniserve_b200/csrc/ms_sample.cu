@@ -1,0 +1,70 @@
+// libmssample.so -- C ABI of the B200 token sampler (declared in include/mssample.h).
+//
+// Reference semantics (miniserve/sampler.py, Sampler.sample):
+//   :33-34  temperature == 0 -> first maximal index
+//   :35     scaled = logit / T                     (here: exp((l - max) / T) in f64)
+//   :37-42  top_k > 0: stable descending sort, first k kept, the rest -inf
+//   :44-47  softmax over what is left (zero total -> ZeroDivisionError)
+//   :49-60  top_p < 1: stable sort of probabilities, running sum, the element
+//           that reaches top_p is kept, renormalise
+//   :62-68  r = Random(seed).random(); first index (index order) whose running
+//           probability reaches r; V-1 when none does
+// The mask path applies the logits-processor hook's -inf convention
+// (miniserve/model_runner.py:214) before all of the above.
+
+#include <cuda_runtime.h>
+
+#include "ms_common.cuh"
+#include "ms_generic.cuh"
+
+namespace {
+thread_local int g_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  return MS_E_CUDA;
+}
+}  // namespace
+
+extern "C" {
+
+int ms_version(void) { return 100; }
+
+int ms_last_cuda_error(void) { return g_last_cuda_error; }
+
+const char *ms_error_string(int code) {
+  switch (code) {
+    case MS_OK: return "ok";
+    case MS_E_INVALID: return "invalid argument (null pointer, B < 0, V < 1, V >= 2^31, ld < V or mask_ld too small)";
+    case MS_E_DTYPE: return "unsupported dtype (expected MS_DTYPE_F32 or MS_DTYPE_BF16)";
+    case MS_E_CUDA: return "CUDA error (see ms_last_cuda_error)";
+    case MS_E_UNSUPPORTED: return "request outside what this build supports";
+    default: return "unknown error";
+  }
+}
+
+int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+              const double *temperature, const int32_t *top_k, const double *top_p,
+              const double *uniforms, const uint32_t *mask, int64_t mask_ld, int64_t *tokens,
+              float *probs, int32_t *row_status, ms_stream_t stream) {
+  if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
+  if (B < 0 || V < 1 || V > 0x7FFFFFFFll - 4096 || ld < V) return MS_E_INVALID;
+  if (B > 0x7FFFFFFFll) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!logits || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
+    return MS_E_INVALID;
+  if (mask && mask_ld < (V + 31) / 32) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ms::SampleArgs a{logits, ld, (int)V, temperature, top_k, top_p, uniforms,
+                   mask, mask_ld, tokens, probs, row_status};
+  dim3 grid((unsigned)B), block(ms::kGenThreads);
+  if (dtype == MS_DTYPE_F32)
+    ms::ms_generic_kernel<MS_DTYPE_F32><<<grid, block, 0, s>>>(a, nullptr, nullptr);
+  else
+    ms::ms_generic_kernel<MS_DTYPE_BF16><<<grid, block, 0, s>>>(a, nullptr, nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
+}
+
+}  // extern "C"
