@@ -74,42 +74,56 @@ def cpu_reference_rate(batch, rows, pool, cores):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while running."""
+    """nvidia-smi samples of SM clock and throttle reasons, read on a thread.
+
+    Started before the timed region; `wait_first()` blocks until the first
+    sample arrives so the timed region is covered from its start."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_ms: int = 20):
         self.gpu = gpu_index
+        self.interval = interval_ms
         self.proc = None
+        self.lines = []
+        self._first = threading.Event()
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
+                self._first.set()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._reader, daemon=True).start()
         except Exception:
             self.proc = None
         return self
 
+    def wait_first(self, timeout=5.0):
+        self._first.wait(timeout)
+        self.start_count = len(self.lines)
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
         return False
 
     def summary(self):
         sms, maxes, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
+        for line in self.lines[getattr(self, "start_count", 0):]:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -124,7 +138,7 @@ class ClockSampler:
         if not sms:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(sms)}
+                "samples": len(sms), "window": "device-timed and e2e regions"}
 
 
 # ----------------------------------------------------------------- GPU side
@@ -169,12 +183,16 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(local_rank) as clocks:
-        evs[0].record(stream)
-        for i in range(args.steps):
-            step()
-            evs[i + 1].record(stream)
-        torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank).__enter__()
+    clocks.wait_first()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    evs[0].record(stream)
+    for i in range(args.steps):
+        step()
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -227,6 +245,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = world * B * e2e_steps / (float(te.item()) / 1e3)
+    clocks.__exit__(None, None, None)
     assert np.array_equal(otok.numpy(), tok.cpu().numpy())
 
     if rank != 0:
@@ -265,7 +284,8 @@ def run_ours(args, rank, world, local_rank):
 
 
 def launches_per_call():
-    return 1
+    """ms_sample launches the cluster kernel and the pending-row pass."""
+    return 2
 
 
 def run_reference(args, rank):
@@ -308,8 +328,8 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

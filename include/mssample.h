@@ -79,6 +79,18 @@ int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
               const double *uniforms, const uint32_t *mask, int64_t mask_ld, int64_t *tokens,
               float *probs, int32_t *row_status, ms_stream_t stream);
 
+/*
+ * Same contract and results as ms_sample, always through the multi-pass
+ * kernel that re-reads each row from global memory (one CTA per row) instead
+ * of the cluster-resident single-read path.  It has no vocabulary-size limit
+ * and serves as the cross-check of the fast path.  Same reference interface
+ * as ms_sample (miniserve/sampler.py:23-68).
+ */
+int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+                      const double *temperature, const int32_t *top_k, const double *top_p,
+                      const double *uniforms, const uint32_t *mask, int64_t mask_ld,
+                      int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);
+
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);
 

@@ -30,6 +30,8 @@ _I64 = ctypes.c_int64
 SIGNATURES = {
     "ms_sample": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64,
                                  _P, _P, _P, _P]),
+    "ms_sample_generic": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _P, _P, _P, _P,
+                                         _I64, _P, _P, _P, _P]),
     "ms_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ms_last_cuda_error": (ctypes.c_int, []),
     "ms_version": (ctypes.c_int, []),

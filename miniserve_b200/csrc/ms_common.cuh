@@ -13,6 +13,7 @@ constexpr uint32_t kNegInfBits = 0xFF800000u;
 constexpr uint32_t kPosInfBits = 0x7F800000u;
 constexpr uint32_t kNegInfKey = 0x007FFFFFu;  // key of -inf: every valid key is larger
 constexpr int kNoCut = 0x7FFFFFFF;            // "all ties kept"
+constexpr int32_t kRowPending = 1 << 30;      // internal status: row left for the generic kernel
 
 // fp32 bit pattern -> uint32 whose unsigned order is the float order.
 __device__ __forceinline__ uint32_t bits_to_key(uint32_t u) {

@@ -1,0 +1,752 @@
+// Cluster-resident sampling kernel: one thread-block cluster of C CTAs per
+// logits row.  Each CTA pulls its contiguous vocab slice from HBM exactly
+// once (one cp.async.bulk TMA copy into shared memory) and every later pass
+// -- max/argmax, temperature-scaled float64 exponentials, the top-k count
+// select, the top-p mass select and the index-order draw -- reads that
+// on-chip copy.  Cross-CTA steps (max, sums, histograms, candidate gathers)
+// go through distributed shared memory between cluster barriers.
+//
+// Rows the on-chip path cannot finish exactly (a candidate set above kCap,
+// a top-k/top-p cut beyond the 40-units-of-x grid) are marked
+// kRowPending in row_status and finished by ms_generic_kernel.
+//
+// Control flow: every decision taken after a cluster barrier is computed by
+// all CTAs from the same published values, so all CTAs of a cluster execute
+// the same sequence of barriers.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "ms_common.cuh"
+#include "ms_generic.cuh"
+
+namespace ms {
+
+namespace cg = cooperative_groups;
+
+constexpr int kFastThreads = 512;
+constexpr int kFastWarps = kFastThreads / 32;
+constexpr int kCap = 1024;                 // on-chip candidate capacity of the leader CTA
+constexpr int kXBins = 2048;               // x-grid bins over [0, 40) units of (max - x)
+constexpr float kXRange = 40.0f;           // exp(-40) ~ 4e-18: past it a token's weight is noise
+constexpr double kQScale = 17592186044416.0;  // 2^44 fixed-point weight scale
+
+enum FastMode : int { kModeDone = 0, kModeFull = 1, kModeTopK = 2, kModeNucleus = 3 };
+
+struct FastCtl {
+  uint32_t max_key;
+  int max_idx;
+  uint32_t nvalid;
+  uint32_t flags;
+  double sum;                 // float64 sum of this CTA's kept weights
+  uint32_t rcnt;              // totals of this CTA's reduced bin range
+  unsigned long long rq;
+  int ncand;
+  uint32_t cut_key;           // written by the leader into every CTA
+  int cut_idx;
+  int go;
+};
+
+struct FastScratch {
+  double redd[33];
+  uint32_t redu[33];
+  int redi[33];
+  int bi[16];
+  double bd[8];
+  int tma_timeout;
+};
+
+// Dynamic shared memory layout (byte offsets); all sections 16-byte aligned.
+struct FastLayout {
+  int keys;      // S stored keys
+  int work;      // histogram / candidate union
+  int red;       // reduced bin range of this CTA
+  int ctl;
+  int scratch;
+  int mbar;
+  int total;
+};
+
+constexpr int kWorkBytes = kXBins * 4 + kXBins * 8;  // 24 KB: u32 counts + u64 fixed-point weights
+static_assert(kCap * 20 <= kWorkBytes, "candidate arrays must fit the histogram region");
+
+__host__ __device__ inline int align16(int x) { return (x + 15) & ~15; }
+
+__host__ __device__ inline FastLayout fast_layout(int S, int key_bytes, int C) {
+  FastLayout L;
+  L.keys = 0;
+  L.work = align16(S * key_bytes);
+  L.red = L.work + kWorkBytes;
+  L.ctl = L.red + align16((kXBins / C) * 12);
+  L.scratch = L.ctl + align16((int)sizeof(FastCtl));
+  L.mbar = L.scratch + align16((int)sizeof(FastScratch));
+  L.total = L.mbar + 16;
+  return L;
+}
+
+template <int DT>
+struct KeyStore;
+template <>
+struct KeyStore<MS_DTYPE_F32> {
+  using T = uint32_t;
+  static __device__ __forceinline__ uint32_t full(T k) { return k; }
+  static __device__ __forceinline__ T pack(uint32_t key) { return key; }
+};
+template <>
+struct KeyStore<MS_DTYPE_BF16> {
+  using T = uint16_t;
+  static __device__ __forceinline__ uint32_t full(T k) {
+    uint32_t k32 = (uint32_t)k << 16;
+    return (k & 0x8000u) ? k32 : (k32 | 0xFFFFu);
+  }
+  static __device__ __forceinline__ T pack(uint32_t key) { return (T)(key >> 16); }
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Bin of a kept element on the x grid: 0 holds the row maximum; kXBins
+// means "past the grid".  Monotone non-increasing in the logit, so every
+// bin is a contiguous range of the descending key order.
+__device__ __forceinline__ int xbin(float v, float vmax, float scale) {
+  float t = (vmax - v) * scale;
+  return t < (float)kXBins ? (int)t : kXBins;
+}
+
+__device__ __forceinline__ unsigned long long qweight(double w) {
+  return (unsigned long long)(w * kQScale);
+}
+
+template <int C, int DT>
+__global__ void __launch_bounds__(kFastThreads, 2)
+    ms_fast_kernel(SampleArgs a, int S, int R) {
+  using KS = KeyStore<DT>;
+  using KT = typename KS::T;
+  extern __shared__ __align__(128) unsigned char smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int row = blockIdx.x / C;
+  const int tid = threadIdx.x;
+  const FastLayout L = fast_layout(S, (int)sizeof(KT), C);
+  KT *keys = reinterpret_cast<KT *>(smem + L.keys);
+  uint32_t *hcnt = reinterpret_cast<uint32_t *>(smem + L.work);
+  unsigned long long *hq = reinterpret_cast<unsigned long long *>(smem + L.work + kXBins * 4);
+  uint32_t *ckey = reinterpret_cast<uint32_t *>(smem + L.work);
+  int *cidx = reinterpret_cast<int *>(smem + L.work + kCap * 4);
+  int *crank = reinterpret_cast<int *>(smem + L.work + kCap * 8);
+  uint32_t *skey = reinterpret_cast<uint32_t *>(smem + L.work + kCap * 12);
+  int *sidx = reinterpret_cast<int *>(smem + L.work + kCap * 16);
+  constexpr int NBR = kXBins / C;  // bins this CTA reduces across the cluster
+  uint32_t *rcnt = reinterpret_cast<uint32_t *>(smem + L.red);
+  unsigned long long *rq = reinterpret_cast<unsigned long long *>(smem + L.red + NBR * 4);
+  FastCtl &ctl = *reinterpret_cast<FastCtl *>(smem + L.ctl);
+  FastScratch &sc = *reinterpret_cast<FastScratch *>(smem + L.scratch);
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.mbar);
+
+  const int V = a.V;
+  const int lo = rank * S;
+  const int n = max(0, min(V, lo + S) - lo);  // elements in this CTA's slice
+  const char *grow = reinterpret_cast<const char *>(a.logits) +
+                     ((int64_t)row * a.ld + lo) * (DT == MS_DTYPE_F32 ? 4 : 2);
+  const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_ld : nullptr;
+  const int esz = DT == MS_DTYPE_F32 ? 4 : 2;
+
+  // ------------------------------------------------------------ load slice
+  const bool tma_ok = ((reinterpret_cast<uintptr_t>(grow) & 15u) == 0);
+  const int tma_elems = tma_ok ? ((n * esz) & ~15) / esz : 0;
+  if (tid == 0) {
+    sc.tma_timeout = 0;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t bytes = (uint32_t)(tma_elems * esz);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mbar)),
+                 "r"(bytes)
+                 : "memory");
+    if (bytes)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(keys)),
+          "l"(grow), "r"(bytes), "r"(smem_u32(mbar))
+          : "memory");
+  }
+  for (int i = tma_elems + tid; i < n; i += kFastThreads) {
+    if (DT == MS_DTYPE_F32)
+      reinterpret_cast<uint32_t *>(keys)[i] = __ldg(reinterpret_cast<const unsigned int *>(grow) + i);
+    else
+      reinterpret_cast<uint16_t *>(keys)[i] = __ldg(reinterpret_cast<const unsigned short *>(grow) + i);
+  }
+  // zero the histogram while the copy is in flight
+  for (int b = tid; b < kXBins; b += kFastThreads) {
+    hcnt[b] = 0u;
+    hq[b] = 0ull;
+  }
+  {
+    // bounded wait for the bulk copy (phase 0)
+    uint32_t done = 0;
+    for (long it = 0; it < (1l << 26) && !done; ++it) {
+      asm volatile(
+          "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
+          : "=r"(done)
+          : "r"(smem_u32(mbar))
+          : "memory");
+    }
+    if (!done) sc.tma_timeout = 1;  // the row is handed to the generic kernel below
+  }
+  __syncthreads();
+
+  // ------------------------------------------ clean + keys + local max/argmax
+  const int t0 = tid * R;
+  const int t1 = min(n, t0 + R);
+  uint32_t flags = 0, bk = 0u, nvalid = 0;
+  int bi = 0x7FFFFFFF;
+  for (int i = t0; i < t1; ++i) {
+    const int gi = lo + i;
+    uint32_t raw = DT == MS_DTYPE_F32 ? reinterpret_cast<uint32_t *>(keys)[i]
+                                      : ((uint32_t)reinterpret_cast<uint16_t *>(keys)[i] << 16);
+    uint32_t key = bits_to_key(clean_bits(raw, mask_allows(mrow, gi), flags));
+    keys[i] = KS::pack(key);
+    key = KS::full(keys[i]);
+    if (key > bk) {
+      bk = key;
+      bi = gi;
+    }
+    nvalid += key > kNegInfKey ? 1u : 0u;
+  }
+  if (bi == 0x7FFFFFFF) bk = 0u;
+  warp_argmax(bk, bi);
+  flags = __reduce_or_sync(0xFFFFFFFFu, flags);
+  nvalid = warp_sum_u32(nvalid);
+  if ((tid & 31) == 0) {
+    sc.redu[tid >> 5] = bk;
+    sc.redi[tid >> 5] = bi;
+    sc.bi[tid >> 5] = (int)nvalid;
+    reinterpret_cast<uint32_t *>(sc.redd)[tid >> 5] = flags;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    uint32_t k2 = tid < kFastWarps ? sc.redu[tid] : 0u;
+    int i2 = tid < kFastWarps ? sc.redi[tid] : 0x7FFFFFFF;
+    uint32_t f2 = tid < kFastWarps ? reinterpret_cast<uint32_t *>(sc.redd)[tid] : 0u;
+    uint32_t nv = tid < kFastWarps ? (uint32_t)sc.bi[tid] : 0u;
+    warp_argmax(k2, i2);
+    f2 = __reduce_or_sync(0xFFFFFFFFu, f2);
+    nv = warp_sum_u32(nv);
+    if (tid == 0) {
+      ctl.max_key = k2;
+      ctl.max_idx = i2;
+      ctl.nvalid = nv;
+      ctl.flags = f2 | (sc.tma_timeout ? (uint32_t)kRowPending : 0u);
+    }
+  }
+  cluster.sync();  // ---------------------------------------------------- S1
+  uint32_t M_key = 0u, nval = 0u, rflags = 0u;
+  int M_idx = 0x7FFFFFFF;
+  for (int q = 0; q < C; ++q) {
+    const FastCtl *rc = cluster.map_shared_rank(&ctl, q);
+    uint32_t k2 = rc->max_key;
+    int i2 = rc->max_idx;
+    if (k2 > M_key || (k2 == M_key && i2 < M_idx)) {
+      M_key = k2;
+      M_idx = i2;
+    }
+    nval += rc->nvalid;
+    rflags |= rc->flags;
+  }
+  const double T = a.temperature[row];
+  const int kk = a.top_k[row];
+  const double P = a.top_p[row];
+  const double U = a.uniforms[row];
+  const bool leader = rank == 0;
+
+  // --------------------------------------------------------- row decisions
+  int mode = kModeDone;
+  const uint32_t fl = rflags & ~(uint32_t)kRowPending;
+  if (rflags & (uint32_t)kRowPending) {
+    if (leader && tid == 0) a.status[row] = kRowPending;
+  } else if (T == 0.0) {
+    if (leader && tid == 0) write_row(a, row, M_idx, 1.0f, (int32_t)fl);
+  } else if (!(T > 0.0) || isinf(T)) {
+    if (leader && tid == 0) write_row(a, row, -1, 0.0f, (int32_t)(fl | MS_ROW_BAD_TEMPERATURE));
+  } else if (nval == 0u) {
+    if (leader && tid == 0) write_row(a, row, -1, 0.0f, (int32_t)(fl | MS_ROW_ALL_MASKED));
+  } else if (M_key == bits_to_key(kPosInfBits)) {
+    if (leader && tid == 0) write_row(a, row, M_idx, 1.0f, (int32_t)fl);
+  } else {
+    const int keff = (kk > 0 && (uint32_t)kk < nval) ? kk : 0;
+    if (keff == 1) {
+      if (leader && tid == 0) {
+        if (U > 0.0)
+          write_row(a, row, M_idx, 1.0f, (int32_t)fl);
+        else
+          write_row(a, row, 0, M_idx == 0 ? 1.0f : 0.0f, (int32_t)fl);
+      }
+    } else if (keff > 1) {
+      mode = keff <= kCap ? kModeTopK : kModeDone;
+      if (mode == kModeDone && leader && tid == 0) a.status[row] = kRowPending;
+    } else if (P < 1.0) {
+      mode = kModeNucleus;
+    } else {
+      mode = kModeFull;
+    }
+  }
+  if (mode == kModeDone) {
+    cluster.sync();  // nobody may leave while others read its control block
+    return;
+  }
+  const int keff = (kk > 0 && (uint32_t)kk < nval) ? kk : 0;
+  const float vmax = key_to_float(M_key);
+  const double dmax = (double)vmax;
+  const double inv_t = 1.0 / T;
+  const float xscale = (float)((double)kXBins / ((double)kXRange * T));
+
+  // The draw over a kept set (FULL, or after a top-p cut): cut describes it.
+  Cut cut = cut_all();
+  double my_sum = 0.0;  // this thread's run weight over the kept set
+
+  if (mode == kModeTopK || mode == kModeNucleus) {
+    // ------------------------------------------------ histogram on the x grid
+    for (int i = t0; i < t1; ++i) {
+      uint32_t key = KS::full(keys[i]);
+      if (key <= kNegInfKey) continue;
+      float v = key_to_float(key);
+      int b = xbin(v, vmax, xscale);
+      if (mode == kModeNucleus) {
+        double w = exp(((double)v - dmax) * inv_t);
+        my_sum += w;
+        if (b < kXBins) {
+          atomicAdd(&hcnt[b], 1u);
+          atomicAdd(&hq[b], qweight(w));
+        }
+      } else if (b < kXBins) {
+        atomicAdd(&hcnt[b], 1u);
+      }
+    }
+    if (mode == kModeNucleus) {
+      double s = block_sum<kFastThreads>(my_sum, sc.redd);
+      if (tid == 0) ctl.sum = s;
+    }
+    cluster.sync();  // -------------------------------------------------- S2
+    // reduce bins [rank*NBR, (rank+1)*NBR) over the cluster
+    uint32_t rc_local = 0;
+    unsigned long long rq_local = 0;
+    for (int j = tid; j < NBR; j += kFastThreads) {
+      const int b = rank * NBR + j;
+      uint32_t c = 0;
+      unsigned long long q = 0;
+      for (int r2 = 0; r2 < C; ++r2) {
+        c += cluster.map_shared_rank(hcnt, r2)[b];
+        if (mode == kModeNucleus) q += cluster.map_shared_rank(hq, r2)[b];
+      }
+      rcnt[j] = c;
+      rq[j] = q;
+      rc_local += c;
+      rq_local += q;
+    }
+    {
+      uint32_t tc = block_sum_u32<kFastThreads>(rc_local, sc.redu);
+      // 64-bit integer block sum via two 32-bit halves would overflow partial
+      // sums; reduce with a warp tree on unsigned long long instead
+      unsigned long long v = rq_local;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+      unsigned long long *wq = reinterpret_cast<unsigned long long *>(sc.redd);
+      if ((tid & 31) == 0) wq[tid >> 5] = v;
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long t = 0;
+        for (int w = 0; w < kFastWarps; ++w) t += wq[w];
+        ctl.rcnt = tc;
+        ctl.rq = t;
+      }
+    }
+    cluster.sync();  // -------------------------------------------------- S3
+    // every CTA: total weight, threshold, crossing range and bin
+    double total = 0.0;
+    unsigned long long qtot = 0;
+    uint32_t ctot = 0;
+    uint32_t rc_all[C];
+    unsigned long long rq_all[C];
+    for (int q = 0; q < C; ++q) {
+      const FastCtl *rc = cluster.map_shared_rank(&ctl, q);
+      rc_all[q] = rc->rcnt;
+      rq_all[q] = rc->rq;
+      qtot += rq_all[q];
+      ctot += rc_all[q];
+      if (mode == kModeNucleus) total += rc->sum;
+    }
+    const double thr = mode == kModeTopK ? (double)keff : P * (double)qtot;
+    int crange = -1;
+    double acc = 0.0, range_before = 0.0;
+    for (int q = 0; q < C; ++q) {
+      double w = mode == kModeTopK ? (double)rc_all[q] : (double)rq_all[q];
+      if (rc_all[q] > 0u && acc + w >= thr) {
+        crange = q;
+        range_before = acc;
+        break;
+      }
+      acc += w;
+    }
+    int gather = 0;  // 0: none, 1: bins <= b*, 2: bin b* only
+    int bstar = kXBins;
+    uint32_t above_cnt = 0, in_cnt = 0;
+    unsigned long long above_q = 0;
+    if (crange >= 0) {
+      // leader thread of each CTA scans the owner's reduced range
+      if (tid == 0) {
+        const uint32_t *orc = cluster.map_shared_rank(rcnt, crange);
+        const unsigned long long *orq = cluster.map_shared_rank(rq, crange);
+        double acc2 = range_before;
+        uint32_t cb = 0;
+        unsigned long long qb = 0;
+        for (int q = 0; q < crange; ++q) {
+          cb += rc_all[q];
+          qb += rq_all[q];
+        }
+        int found = -1;
+        for (int j = 0; j < NBR; ++j) {
+          uint32_t c = orc[j];
+          unsigned long long qq = orq[j];
+          double w = mode == kModeTopK ? (double)c : (double)qq;
+          if (c > 0u && acc2 + w >= thr) {
+            found = j;
+            sc.bi[0] = crange * NBR + j;
+            sc.bi[1] = (int)cb;
+            sc.bi[2] = (int)c;
+            sc.bd[0] = __longlong_as_double((long long)qb);
+            break;
+          }
+          acc2 += w;
+          cb += c;
+          qb += qq;
+        }
+        if (found < 0) sc.bi[0] = kXBins;  // rounding: treat as not found
+      }
+      __syncthreads();
+      bstar = sc.bi[0];
+      above_cnt = (uint32_t)sc.bi[1];
+      in_cnt = (uint32_t)sc.bi[2];
+      above_q = (unsigned long long)__double_as_longlong(sc.bd[0]);
+      __syncthreads();
+    }
+    if (bstar < kXBins) {
+      if (above_cnt + in_cnt <= (uint32_t)kCap)
+        gather = 1;
+      else if (mode == kModeNucleus && in_cnt <= (uint32_t)kCap)
+        gather = 2;
+    }
+    if (gather == 0) {
+      // NUCLEUS whose threshold was never reached keeps every valid token
+      // (the reference's loop ran out); anything else goes to the generic path
+      if (mode == kModeNucleus && crange < 0) {
+        mode = kModeFull;  // reuse my_sum and total below
+      } else {
+        if (leader && tid == 0) a.status[row] = kRowPending;
+        cluster.sync();
+        return;
+      }
+    }
+    if (gather) {
+      // ---------------------------------------- compact candidates locally
+      int mine = 0;
+      for (int i = t0; i < t1; ++i) {
+        uint32_t key = KS::full(keys[i]);
+        if (key <= kNegInfKey) continue;
+        int b = xbin(key_to_float(key), vmax, xscale);
+        mine += (gather == 1 ? b <= bstar : b == bstar) ? 1 : 0;
+      }
+      int ex, inc, tot;
+      block_scan<kFastThreads, int>(mine, ex, inc, tot, sc.redi);
+      if (tot <= kCap) {
+        int pos = ex;
+        for (int i = t0; i < t1 && pos < inc; ++i) {
+          uint32_t key = KS::full(keys[i]);
+          if (key <= kNegInfKey) continue;
+          int b = xbin(key_to_float(key), vmax, xscale);
+          if (gather == 1 ? b <= bstar : b == bstar) {
+            ckey[pos] = key;
+            cidx[pos] = lo + i;
+            ++pos;
+          }
+        }
+      }
+      if (tid == 0) ctl.ncand = tot;
+      cluster.sync();  // ------------------------------------------------ S4
+      int offs[C + 1];
+      offs[0] = 0;
+      for (int q = 0; q < C; ++q) offs[q + 1] = offs[q] + cluster.map_shared_rank(&ctl, q)->ncand;
+      const int ntot = offs[C];
+      if (ntot > kCap) {  // cannot happen (counts are exact); stay safe
+        if (leader && tid == 0) a.status[row] = kRowPending;
+        cluster.sync();
+        return;
+      }
+      if (leader) {
+        for (int q = 1; q < C; ++q) {
+          const uint32_t *rk = cluster.map_shared_rank(ckey, q);
+          const int *ri = cluster.map_shared_rank(cidx, q);
+          for (int j = tid; j < offs[q + 1] - offs[q]; j += kFastThreads) {
+            ckey[offs[q] + j] = rk[j];
+            cidx[offs[q] + j] = ri[j];
+          }
+        }
+      }
+      cluster.sync();  // ------------------------------------------------ S5
+      if (gather == 1) {
+        if (!leader) return;
+        // ---------------------------------------- leader: exact finish
+        __syncthreads();
+        // rank of each candidate in (key desc, index asc) order
+        for (int i = tid; i < ntot; i += kFastThreads) {
+          const uint32_t ki = ckey[i];
+          int r2 = 0;
+          for (int j = 0; j < ntot; ++j) {
+            const uint32_t kj = ckey[j];
+            r2 += (kj > ki || (kj == ki && j < i)) ? 1 : 0;
+          }
+          crank[i] = r2;
+        }
+        __syncthreads();
+        const int m = mode == kModeTopK ? keff : ntot;  // kept before top-p
+        for (int i = tid; i < ntot; i += kFastThreads) {
+          if (crank[i] < m) {
+            skey[crank[i]] = ckey[i];
+            sidx[crank[i]] = cidx[i];
+          }
+        }
+        __syncthreads();
+        // softmax normaliser over the kept set
+        double tot_m;
+        if (mode == kModeTopK) {
+          double s = 0.0;
+          for (int r2 = tid; r2 < m; r2 += kFastThreads)
+            s += exp(((double)key_to_float(skey[r2]) - dmax) * inv_t);
+          tot_m = block_sum<kFastThreads>(s, sc.redd);
+        } else {
+          tot_m = total;
+        }
+        int nkeep = m;
+        if (P < 1.0) {
+          // running sum in sorted order; first position reaching P * tot_m
+          const int per = (m + kFastThreads - 1) / kFastThreads;
+          const int p0 = tid * per, p1 = min(m, p0 + per);
+          double s = 0.0;
+          for (int r2 = p0; r2 < p1; ++r2) s += exp(((double)key_to_float(skey[r2]) - dmax) * inv_t);
+          double ex2, inc2, tot2;
+          block_scan<kFastThreads, double>(s, ex2, inc2, tot2, sc.redd);
+          const double target = P * tot_m;
+          int cand = 0x7FFFFFFF;
+          if (p0 < p1 && inc2 >= target) {
+            double acc3 = ex2;
+            for (int r2 = p0; r2 < p1; ++r2) {
+              acc3 += exp(((double)key_to_float(skey[r2]) - dmax) * inv_t);
+              if (acc3 >= target) {
+                cand = r2;
+                break;
+              }
+            }
+            if (cand == 0x7FFFFFFF) cand = p1 - 1;
+          }
+          int first = block_min_i<kFastThreads>(cand, sc.redi);
+          if (first != 0x7FFFFFFF) nkeep = first + 1;
+        }
+        // index-order draw over candidates with rank < nkeep
+        const int per = (ntot + kFastThreads - 1) / kFastThreads;
+        const int p0 = tid * per, p1 = min(ntot, p0 + per);
+        double s = 0.0;
+        for (int i = p0; i < p1; ++i)
+          if (crank[i] < nkeep) s += exp(((double)key_to_float(ckey[i]) - dmax) * inv_t);
+        double ex3, inc3, tot3;
+        block_scan<kFastThreads, double>(s, ex3, inc3, tot3, sc.redd);
+        const double tot_p = tot3;
+        if (!(U > 0.0)) {
+          if (tid == 0) {
+            double w0 = (ntot > 0 && cidx[0] == 0 && crank[0] < nkeep)
+                            ? exp(((double)key_to_float(ckey[0]) - dmax) * inv_t)
+                            : 0.0;
+            write_row(a, row, 0, (float)(w0 / tot_p), (int32_t)fl);
+          }
+          return;
+        }
+        const double target = U * tot_p;
+        int cand = (s > 0.0 && inc3 >= target) ? tid : 0x7FFFFFFF;
+        int who = block_min_i<kFastThreads>(cand, sc.redi);
+        if (who == 0x7FFFFFFF) {
+          if (tid == 0) {
+            // the reference's loop ran past the end: V-1
+            double wl = (ntot > 0 && cidx[ntot - 1] == V - 1 && crank[ntot - 1] < nkeep)
+                            ? exp(((double)key_to_float(ckey[ntot - 1]) - dmax) * inv_t)
+                            : 0.0;
+            write_row(a, row, V - 1, (float)(wl / tot_p), (int32_t)fl);
+          }
+          return;
+        }
+        if (tid == who) {
+          double acc3 = ex3;
+          int tok = -1, last = -1;
+          double wt = 0.0, wl = 0.0;
+          for (int i = p0; i < p1; ++i) {
+            if (crank[i] >= nkeep) continue;
+            double w = exp(((double)key_to_float(ckey[i]) - dmax) * inv_t);
+            acc3 += w;
+            last = cidx[i];
+            wl = w;
+            if (acc3 >= target) {
+              tok = cidx[i];
+              wt = w;
+              break;
+            }
+          }
+          if (tok < 0) {
+            tok = last;
+            wt = wl;
+          }
+          write_row(a, row, tok, (float)(wt / tot_p), (int32_t)fl);
+        }
+        return;
+      }
+      // gather == 2: the leader places the top-p cut inside bin b*
+      if (leader) {
+        for (int i = tid; i < ntot; i += kFastThreads) {
+          const uint32_t ki = ckey[i];
+          int r2 = 0;
+          for (int j = 0; j < ntot; ++j) {
+            const uint32_t kj = ckey[j];
+            r2 += (kj > ki || (kj == ki && j < i)) ? 1 : 0;
+          }
+          skey[r2] = ki;
+          sidx[r2] = cidx[i];
+        }
+        __syncthreads();
+        // same fixed-point weights as the histogram, so the cut agrees with it
+        const int per = (ntot + kFastThreads - 1) / kFastThreads;
+        const int p0 = tid * per, p1 = min(ntot, p0 + per);
+        unsigned long long qs = 0;
+        for (int r2 = p0; r2 < p1; ++r2)
+          qs += qweight(exp(((double)key_to_float(skey[r2]) - dmax) * inv_t));
+        unsigned long long qex, qin, qtt;
+        block_scan<kFastThreads, unsigned long long>(qs, qex, qin, qtt,
+                                                     reinterpret_cast<unsigned long long *>(sc.redd));
+        int cand = 0x7FFFFFFF;
+        if (p0 < p1 && (double)(above_q + qin) >= thr) {
+          unsigned long long accq = above_q + qex;
+          for (int r2 = p0; r2 < p1; ++r2) {
+            accq += qweight(exp(((double)key_to_float(skey[r2]) - dmax) * inv_t));
+            if ((double)accq >= thr) {
+              cand = r2;
+              break;
+            }
+          }
+          if (cand == 0x7FFFFFFF) cand = p1 - 1;
+        }
+        int r_cut = block_min_i<kFastThreads>(cand, sc.redi);
+        if (r_cut == 0x7FFFFFFF) r_cut = ntot - 1;
+        if (tid < C) {
+          FastCtl *rc = cluster.map_shared_rank(&ctl, tid);
+          rc->cut_key = skey[r_cut];
+          rc->cut_idx = sidx[r_cut];
+        }
+      }
+      cluster.sync();  // ------------------------------------------------ S6
+      cut.key = ctl.cut_key;
+      cut.cut = ctl.cut_idx;
+      // weights of the kept set in my run
+      my_sum = 0.0;
+      for (int i = t0; i < t1; ++i) {
+        uint32_t key = KS::full(keys[i]);
+        if (key > kNegInfKey && kept(cut, key, lo + i))
+          my_sum += exp(((double)key_to_float(key) - dmax) * inv_t);
+      }
+      double s = block_sum<kFastThreads>(my_sum, sc.redd);
+      if (tid == 0) ctl.sum = s;
+      cluster.sync();  // ------------------------------------------------ S7
+      mode = kModeFull;
+    }
+  } else {
+    // FULL: every valid token is kept
+    for (int i = t0; i < t1; ++i) {
+      uint32_t key = KS::full(keys[i]);
+      if (key > kNegInfKey) my_sum += exp(((double)key_to_float(key) - dmax) * inv_t);
+    }
+    double s = block_sum<kFastThreads>(my_sum, sc.redd);
+    if (tid == 0) ctl.sum = s;
+    cluster.sync();  // ---------------------------------------------------- S2
+  }
+
+  // ------------------------------------------------- index-order draw (FULL)
+  {
+    double sums[C];
+    double total = 0.0;
+    for (int q = 0; q < C; ++q) {
+      sums[q] = cluster.map_shared_rank(&ctl, q)->sum;
+      total += sums[q];
+    }
+    auto wt = [&](int i) -> double {  // i: slice-local index
+      uint32_t key = KS::full(keys[i]);
+      return (key > kNegInfKey && kept(cut, key, lo + i))
+                 ? exp(((double)key_to_float(key) - dmax) * inv_t)
+                 : 0.0;
+    };
+    if (!(U > 0.0)) {
+      if (rank == 0 && tid == 0) write_row(a, row, 0, (float)(wt(0) / total), (int32_t)fl);
+    } else {
+      const double target = U * total;
+      int cstar = -1;
+      double before = 0.0, acc = 0.0;
+      for (int q = 0; q < C; ++q) {
+        if (sums[q] > 0.0 && acc + sums[q] >= target) {
+          cstar = q;
+          before = acc;
+          break;
+        }
+        acc += sums[q];
+      }
+      if (cstar < 0) {
+        const int owner = (V - 1) / S;
+        if (rank == owner && tid == 0)
+          write_row(a, row, V - 1, (float)(wt(V - 1 - lo) / total), (int32_t)fl);
+      } else if (rank == cstar) {
+        double ex, inc, tot;
+        block_scan<kFastThreads, double>(my_sum, ex, inc, tot, sc.redd);
+        int cand = (my_sum > 0.0 && before + inc >= target) ? tid : 0x7FFFFFFF;
+        int who = block_min_i<kFastThreads>(cand, sc.redi);
+        if (who == 0x7FFFFFFF) {
+          // rounding left the crossing past this CTA's partial sums: take
+          // the last kept element of the CTA
+          int lastt = my_sum > 0.0 ? tid : -1;
+          lastt = -block_min_i<kFastThreads>(-lastt, sc.redi);
+          who = lastt;
+        }
+        if (tid == who) {
+          double cum = before + ex;
+          int tok = -1, last = -1;
+          double wtk = 0.0, wl = 0.0;
+          for (int i = t0; i < t1; ++i) {
+            double w = wt(i);
+            if (w <= 0.0) continue;
+            cum += w;
+            last = lo + i;
+            wl = w;
+            if (cum >= target) {
+              tok = lo + i;
+              wtk = w;
+              break;
+            }
+          }
+          if (tok < 0) {
+            tok = last;
+            wtk = wl;
+          }
+          write_row(a, row, tok, (float)(wtk / total), (int32_t)fl);
+        }
+      }
+    }
+  }
+  cluster.sync();  // keep every slice alive until all remote reads are done
+}
+
+}  // namespace ms

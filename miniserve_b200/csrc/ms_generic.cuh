@@ -358,4 +358,16 @@ __global__ void __launch_bounds__(kGenThreads, 1)
   gen_row<DT>(a, r, sh);
 }
 
+// Finishes the rows the cluster kernel left with status kRowPending; a
+// grid-stride loop, so the grid can stay one CTA per SM whatever B is.
+template <int DT>
+__global__ void __launch_bounds__(kGenThreads, 1) ms_generic_pending_kernel(SampleArgs a, int B) {
+  __shared__ GenShared sh;
+  for (int r = blockIdx.x; r < B; r += gridDim.x) {
+    if (a.status[r] != kRowPending) continue;
+    gen_row<DT>(a, r, sh);
+    __syncthreads();
+  }
+}
+
 }  // namespace ms

@@ -14,7 +14,10 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "ms_common.cuh"
+#include "ms_fast.cuh"
 #include "ms_generic.cuh"
 
 namespace {
@@ -23,6 +26,90 @@ thread_local int g_last_cuda_error = 0;
 int cuda_fail(cudaError_t e) {
   g_last_cuda_error = (int)e;
   return MS_E_CUDA;
+}
+
+constexpr int kMaxDevices = 64;
+constexpr int kFastMaxV = 1 << 19;          // fixed-point weight sums stay below 2^63
+constexpr int kTwoPerSmBytes = 110 * 1024;  // two CTAs per SM
+constexpr int kOnePerSmBytes = 227 * 1024;
+
+struct FastPlan {
+  int C = 0;   // cluster size; 0 = no on-chip path
+  int S = 0;   // slice length (elements), multiple of 16
+  int R = 0;   // per-thread run length (odd: conflict-free shared-memory strides)
+  int smem = 0;
+};
+
+FastPlan plan_fast(int64_t V, int dtype) {
+  FastPlan p;
+  if (V > kFastMaxV) return p;
+  const int kb = dtype == MS_DTYPE_F32 ? 4 : 2;
+  for (int limit : {kTwoPerSmBytes, kOnePerSmBytes}) {
+    for (int C : {4, 8, 16}) {
+      int S = (int)((V + C - 1) / C);
+      S = (S + 15) & ~15;
+      int smem = ms::fast_layout(S, kb, C).total;
+      if (smem <= limit) {
+        p.C = C;
+        p.S = S;
+        p.R = ((S + ms::kFastThreads - 1) / ms::kFastThreads) | 1;
+        p.smem = smem;
+        return p;
+      }
+    }
+  }
+  return p;
+}
+
+// cudaFuncSetAttribute once per (kernel, device).
+template <int C, int DT>
+cudaError_t prepare_fast(int dev) {
+  static std::atomic<int> ready[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (ready[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  auto kern = ms::ms_fast_kernel<C, DT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kOnePerSmBytes);
+  if (e == cudaSuccess && C > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) ready[dev].store(1, std::memory_order_release);
+  return e;
+}
+
+template <int C, int DT>
+cudaError_t launch_fast(const ms::SampleArgs &a, int B, const FastPlan &p, cudaStream_t s, int dev) {
+  cudaError_t e = prepare_fast<C, DT>(dev);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(B * C));
+  cfg.blockDim = dim3(ms::kFastThreads);
+  cfg.dynamicSmemBytes = (size_t)p.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, ms::ms_fast_kernel<C, DT>, a, p.S, p.R);
+}
+
+template <int DT>
+cudaError_t launch_all(const ms::SampleArgs &a, int B, const FastPlan &p, cudaStream_t s, int dev) {
+  cudaError_t e;
+  switch (p.C) {
+    case 4: e = launch_fast<4, DT>(a, B, p, s, dev); break;
+    case 8: e = launch_fast<8, DT>(a, B, p, s, dev); break;
+    case 16: e = launch_fast<16, DT>(a, B, p, s, dev); break;
+    default:
+      ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
+      return cudaGetLastError();
+  }
+  if (e != cudaSuccess) return e;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = B < sms ? B : sms;
+  ms::ms_generic_pending_kernel<DT><<<dim3((unsigned)grid), dim3(ms::kGenThreads), 0, s>>>(a, B);
+  return cudaGetLastError();
 }
 }  // namespace
 
@@ -43,10 +130,11 @@ const char *ms_error_string(int code) {
   }
 }
 
-int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
-              const double *temperature, const int32_t *top_k, const double *top_p,
-              const double *uniforms, const uint32_t *mask, int64_t mask_ld, int64_t *tokens,
-              float *probs, int32_t *row_status, ms_stream_t stream) {
+static int sample_impl(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+                       const double *temperature, const int32_t *top_k, const double *top_p,
+                       const double *uniforms, const uint32_t *mask, int64_t mask_ld,
+                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream,
+                       bool generic_only) {
   if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
   if (B < 0 || V < 1 || V > 0x7FFFFFFFll - 4096 || ld < V) return MS_E_INVALID;
   if (B > 0x7FFFFFFFll) return MS_E_INVALID;
@@ -57,14 +145,30 @@ int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   ms::SampleArgs a{logits, ld, (int)V, temperature, top_k, top_p, uniforms,
                    mask, mask_ld, tokens, probs, row_status};
-  dim3 grid((unsigned)B), block(ms::kGenThreads);
-  if (dtype == MS_DTYPE_F32)
-    ms::ms_generic_kernel<MS_DTYPE_F32><<<grid, block, 0, s>>>(a, nullptr, nullptr);
-  else
-    ms::ms_generic_kernel<MS_DTYPE_BF16><<<grid, block, 0, s>>>(a, nullptr, nullptr);
-  cudaError_t e = cudaGetLastError();
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const FastPlan p = generic_only ? FastPlan{} : plan_fast(V, dtype);
+  e = dtype == MS_DTYPE_F32 ? launch_all<MS_DTYPE_F32>(a, (int)B, p, s, dev)
+                            : launch_all<MS_DTYPE_BF16>(a, (int)B, p, s, dev);
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;
+}
+
+int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+              const double *temperature, const int32_t *top_k, const double *top_p,
+              const double *uniforms, const uint32_t *mask, int64_t mask_ld, int64_t *tokens,
+              float *probs, int32_t *row_status, ms_stream_t stream) {
+  return sample_impl(logits, dtype, B, V, ld, temperature, top_k, top_p, uniforms, mask, mask_ld,
+                     tokens, probs, row_status, stream, false);
+}
+
+int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
+                      const double *temperature, const int32_t *top_k, const double *top_p,
+                      const double *uniforms, const uint32_t *mask, int64_t mask_ld,
+                      int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
+  return sample_impl(logits, dtype, B, V, ld, temperature, top_k, top_p, uniforms, mask, mask_ld,
+                     tokens, probs, row_status, stream, true);
 }
 
 }  // extern "C"

@@ -53,7 +53,18 @@ def _param(x, B: int, dtype, device):
 
 
 class Sampler:
-    """Convert logit scores to token ids on the GPU (miniserve/sampler.py:20-68)."""
+    """Convert logit scores to token ids on the GPU (miniserve/sampler.py:20-68).
+
+    ``path="fast"`` (default) uses the cluster-resident kernel that reads each
+    row from HBM once; ``path="generic"`` forces the multi-pass kernel (no
+    vocabulary limit; the cross-check of the fast path).  Both give the same
+    results.
+    """
+
+    def __init__(self, path: str = "fast") -> None:
+        if path not in ("fast", "generic"):
+            raise ValueError("path must be 'fast' or 'generic'")
+        self.path = path
 
     def sample(self, logits, *, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0,
                seed: Optional[int] = None) -> int:
@@ -134,7 +145,8 @@ class Sampler:
             tokens, probs, status = out
         with torch.cuda.device(dev):
             stream = torch.cuda.current_stream(dev).cuda_stream
-            rc = _lib.lib().ms_sample(logits.data_ptr(), dtype, B, V, logits.stride(0), T.data_ptr(),
+            fn = _lib.lib().ms_sample if self.path == "fast" else _lib.lib().ms_sample_generic
+            rc = fn(logits.data_ptr(), dtype, B, V, logits.stride(0), T.data_ptr(),
                                       K.data_ptr(), P.data_ptr(), U.data_ptr(), mask_ptr, mask_ld,
                                       tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
         _lib.check(rc, "ms_sample")

@@ -10,13 +10,13 @@ from parity import compare, gpu_sample
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def sampler():
+@pytest.fixture(scope="module", params=["fast", "generic"])
+def sampler(request):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
         pytest.fail("CUDA device required for -m gpu tests")
     from miniserve_b200 import Sampler
-    return Sampler()
+    return Sampler(request.param)
 
 
 def test_kat(sampler):
