@@ -380,58 +380,59 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       if (mode == kModeNucleus) total += rc->sum;
     }
     const double thr = mode == kModeTopK ? (double)keff : P * (double)qtot;
+    // running totals are exact integers (counts, or 2^-44 fixed-point weights)
+    auto reached = [&](unsigned long long cum_c, unsigned long long cum_q) -> bool {
+      return mode == kModeTopK ? (double)cum_c >= thr : (double)cum_q >= thr;
+    };
     int crange = -1;
-    double acc = 0.0, range_before = 0.0;
-    for (int q = 0; q < C; ++q) {
-      double w = mode == kModeTopK ? (double)rc_all[q] : (double)rq_all[q];
-      if (rc_all[q] > 0u && acc + w >= thr) {
-        crange = q;
-        range_before = acc;
-        break;
+    {
+      unsigned long long ac = 0, aq = 0;
+      for (int q = 0; q < C; ++q) {
+        if (rc_all[q] > 0u && reached(ac + rc_all[q], aq + rq_all[q])) {
+          crange = q;
+          break;
+        }
+        ac += rc_all[q];
+        aq += rq_all[q];
       }
-      acc += w;
     }
     int gather = 0;  // 0: none, 1: bins <= b*, 2: bin b* only
     int bstar = kXBins;
     uint32_t above_cnt = 0, in_cnt = 0;
     unsigned long long above_q = 0;
     if (crange >= 0) {
-      // leader thread of each CTA scans the owner's reduced range
-      if (tid == 0) {
-        const uint32_t *orc = cluster.map_shared_rank(rcnt, crange);
-        const unsigned long long *orq = cluster.map_shared_rank(rq, crange);
-        double acc2 = range_before;
-        uint32_t cb = 0;
-        unsigned long long qb = 0;
-        for (int q = 0; q < crange; ++q) {
-          cb += rc_all[q];
-          qb += rq_all[q];
-        }
-        int found = -1;
-        for (int j = 0; j < NBR; ++j) {
-          uint32_t c = orc[j];
-          unsigned long long qq = orq[j];
-          double w = mode == kModeTopK ? (double)c : (double)qq;
-          if (c > 0u && acc2 + w >= thr) {
-            found = j;
-            sc.bi[0] = crange * NBR + j;
-            sc.bi[1] = (int)cb;
-            sc.bi[2] = (int)c;
-            sc.bd[0] = __longlong_as_double((long long)qb);
-            break;
-          }
-          acc2 += w;
-          cb += c;
-          qb += qq;
-        }
-        if (found < 0) sc.bi[0] = kXBins;  // rounding: treat as not found
+      // one thread per bin of the owner's reduced range; a block scan finds
+      // the first non-empty bin whose running total reaches thr
+      unsigned long long cb = 0, qb = 0;
+      for (int q = 0; q < crange; ++q) {
+        cb += rc_all[q];
+        qb += rq_all[q];
       }
-      __syncthreads();
-      bstar = sc.bi[0];
-      above_cnt = (uint32_t)sc.bi[1];
-      in_cnt = (uint32_t)sc.bi[2];
-      above_q = (unsigned long long)__double_as_longlong(sc.bd[0]);
-      __syncthreads();
+      const uint32_t *orc = cluster.map_shared_rank(rcnt, crange);
+      const unsigned long long *orq = cluster.map_shared_rank(rq, crange);
+      const unsigned long long c = tid < NBR ? (unsigned long long)orc[tid] : 0ull;
+      const unsigned long long qq = (tid < NBR && mode == kModeNucleus) ? orq[tid] : 0ull;
+      unsigned long long cex, cin, ctt, qex, qin, qtt;
+      block_scan<kFastThreads, unsigned long long>(c, cex, cin, ctt,
+                                                   reinterpret_cast<unsigned long long *>(sc.redd));
+      block_scan<kFastThreads, unsigned long long>(qq, qex, qin, qtt,
+                                                   reinterpret_cast<unsigned long long *>(sc.redd));
+      const bool hit = tid < NBR && c > 0ull && reached(cb + cin, qb + qin);
+      const int j = block_min_i<kFastThreads>(hit ? tid : 0x7FFFFFFF, sc.redi);
+      if (j != 0x7FFFFFFF) {
+        if (tid == j) {
+          sc.bi[0] = crange * NBR + j;
+          sc.bi[1] = (int)(cb + cex);
+          sc.bi[2] = (int)c;
+          sc.bd[0] = __longlong_as_double((long long)(qb + qex));
+        }
+        __syncthreads();
+        bstar = sc.bi[0];
+        above_cnt = (uint32_t)sc.bi[1];
+        in_cnt = (uint32_t)sc.bi[2];
+        above_q = (unsigned long long)__double_as_longlong(sc.bd[0]);
+        __syncthreads();
+      }
     }
     if (bstar < kXBins) {
       if (above_cnt + in_cnt <= (uint32_t)kCap)
