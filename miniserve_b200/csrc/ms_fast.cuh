@@ -102,6 +102,50 @@ struct KeyStore<MS_DTYPE_BF16> {
   static __device__ __forceinline__ T pack(uint32_t key) { return (T)(key >> 16); }
 };
 
+// Canonical order key of a finite-or-(-inf) value: -0 and +0 share a key,
+// as the reference compares values, not bit patterns.
+__device__ __forceinline__ uint32_t fkey(float v) {
+  uint32_t u = __float_as_uint(v);
+  if (u == 0x80000000u) u = 0u;
+  return bits_to_key(u);
+}
+
+// Kept-set predicate on values: above the cut value, or equal to it with an
+// index at or below the cut index (ties taken in index order).
+struct FCut {
+  float v;
+  int idx;
+};
+__device__ __forceinline__ bool fkept(const FCut &c, float v, int idx) {
+  return v > c.v || (v == c.v && idx <= c.idx);
+}
+
+// Raw slice values in shared memory: fp32 as is, bf16 widened exactly.
+template <int DT>
+__device__ __forceinline__ float fv(const void *vals, int i) {
+  if (DT == MS_DTYPE_F32) return reinterpret_cast<const float *>(vals)[i];
+  return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(vals)[i] << 16);
+}
+// Four consecutive values starting at a multiple of 4 (one 16- or 8-byte load).
+template <int DT>
+__device__ __forceinline__ void load4(const void *vals, int i, float x[4]) {
+  if (DT == MS_DTYPE_F32) {
+    const float4 f = reinterpret_cast<const float4 *>(vals)[i >> 2];
+    x[0] = f.x;
+    x[1] = f.y;
+    x[2] = f.z;
+    x[3] = f.w;
+  } else {
+    const uint2 h = reinterpret_cast<const uint2 *>(vals)[i >> 2];
+    x[0] = __uint_as_float(h.x << 16);
+    x[1] = __uint_as_float(h.x & 0xFFFF0000u);
+    x[2] = __uint_as_float(h.y << 16);
+    x[3] = __uint_as_float(h.y & 0xFFFF0000u);
+  }
+}
+
+constexpr uint32_t kHasNegInf = 1u << 29;  // flag: a -inf logit in an unmasked row
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -199,25 +243,83 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   }
   __syncthreads();
 
-  // ------------------------------------------ clean + keys + local max/argmax
+  // ---------------------------------------------- mask pass (masked rows)
+  // The slice keeps raw values; a disallowed token becomes -inf in place
+  // (the logits-processor hook's convention, miniserve/model_runner.py:214).
   const int t0 = tid * R;
   const int t1 = min(n, t0 + R);
-  uint32_t flags = 0, bk = 0u, nvalid = 0;
-  int bi = 0x7FFFFFFF;
-  for (int i = t0; i < t1; ++i) {
-    const int gi = lo + i;
-    uint32_t raw = DT == MS_DTYPE_F32 ? reinterpret_cast<uint32_t *>(keys)[i]
-                                      : ((uint32_t)reinterpret_cast<uint16_t *>(keys)[i] << 16);
-    uint32_t key = bits_to_key(clean_bits(raw, mask_allows(mrow, gi), flags));
-    keys[i] = KS::pack(key);
-    key = KS::full(keys[i]);
-    if (key > bk) {
-      bk = key;
-      bi = gi;
+  uint32_t nvalid = 0;
+  if (mrow) {
+    for (int i = t0; i < t1; ++i) {
+      const int gi = lo + i;
+      if (!((__ldg(mrow + (gi >> 5)) >> (gi & 31)) & 1u)) {
+        if (DT == MS_DTYPE_F32)
+          reinterpret_cast<uint32_t *>(keys)[i] = kNegInfBits;
+        else
+          reinterpret_cast<uint16_t *>(keys)[i] = (uint16_t)(kNegInfBits >> 16);
+      }
     }
-    nvalid += key > kNegInfKey ? 1u : 0u;
+    // counted after the writes so that every element is read once more here
+    for (int i = t0; i < t1; ++i) nvalid += fv<DT>(keys, i) > -INFINITY ? 1u : 0u;
   }
-  if (bi == 0x7FFFFFFF) bk = 0u;
+  // ----------------------------------------- local max (first index if needed)
+  // Rows that need the argmax (greedy, top_k == 1) track the first index of
+  // the maximum; the others only need its value.  The float sum detects NaN
+  // and +inf, whose rows go to the generic kernel.
+  const double T0 = a.temperature[row];
+  const int k0 = a.top_k[row];
+  const bool need_idx = T0 == 0.0 || k0 == 1;
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  int i4[4] = {0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF};
+  float vsum = 0.0f;
+  {
+    const int tv = t0 + ((t1 - t0) & ~3);  // end of whole groups of 4
+    if (need_idx) {
+      for (int i = t0; i < tv; i += 4) {
+        float x[4];
+        load4<DT>(keys, i, x);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          vsum += x[e];
+          if (x[e] > m4[e]) {
+            m4[e] = x[e];
+            i4[e] = lo + i + e;
+          }
+        }
+      }
+    } else {
+      for (int i = t0; i < tv; i += 4) {
+        float x[4];
+        load4<DT>(keys, i, x);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) m4[e] = fmaxf(m4[e], x[e]);
+        vsum += (x[0] + x[1]) + (x[2] + x[3]);
+      }
+    }
+    for (int i = tv; i < t1; ++i) {
+      const float x = fv<DT>(keys, i);
+      vsum += x;
+      if (x > m4[0]) {
+        m4[0] = x;
+        i4[0] = lo + i;
+      }
+    }
+  }
+  float tmax = m4[0];
+  int tidx = i4[0];
+#pragma unroll
+  for (int e = 1; e < 4; ++e) {
+    if (m4[e] > tmax || (m4[e] == tmax && i4[e] < tidx)) {
+      tmax = m4[e];
+      tidx = i4[e];
+    }
+  }
+  uint32_t flags = 0;
+  if (isnan(vsum) || vsum == INFINITY) flags |= MS_ROW_NONFINITE;
+  if (vsum == -INFINITY && !mrow) flags |= kHasNegInf;
+  uint32_t bk = tmax > -INFINITY ? fkey(tmax) : kNegInfKey;
+  int bi = tmax > -INFINITY ? tidx : 0x7FFFFFFF;
+  if (!need_idx) bi = 0;
   warp_argmax(bk, bi);
   flags = __reduce_or_sync(0xFFFFFFFFu, flags);
   nvalid = warp_sum_u32(nvalid);
@@ -265,17 +367,18 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 
   // --------------------------------------------------------- row decisions
   int mode = kModeDone;
-  const uint32_t fl = rflags & ~(uint32_t)kRowPending;
-  if (rflags & (uint32_t)kRowPending) {
+  if (!mrow) nval = (uint32_t)V;  // unmasked: every token counts unless -inf is present
+  const uint32_t fl = 0u;
+  const bool defer = (rflags & ((uint32_t)kRowPending | MS_ROW_NONFINITE)) != 0u ||
+                     ((rflags & kHasNegInf) && T > 0.0 && kk > 1);
+  if (defer) {
     if (leader && tid == 0) a.status[row] = kRowPending;
-  } else if (T == 0.0) {
-    if (leader && tid == 0) write_row(a, row, M_idx, 1.0f, (int32_t)fl);
+  } else if (T == 0.0) {  // all -inf: the first index is the (tied) maximum
+    if (leader && tid == 0) write_row(a, row, M_key == kNegInfKey ? 0 : M_idx, 1.0f, (int32_t)fl);
   } else if (!(T > 0.0) || isinf(T)) {
     if (leader && tid == 0) write_row(a, row, -1, 0.0f, (int32_t)(fl | MS_ROW_BAD_TEMPERATURE));
-  } else if (nval == 0u) {
+  } else if (M_key == kNegInfKey) {  // every token is -inf: zero total (sampler.py:46-47)
     if (leader && tid == 0) write_row(a, row, -1, 0.0f, (int32_t)(fl | MS_ROW_ALL_MASKED));
-  } else if (M_key == bits_to_key(kPosInfBits)) {
-    if (leader && tid == 0) write_row(a, row, M_idx, 1.0f, (int32_t)fl);
   } else {
     const int keff = (kk > 0 && (uint32_t)kk < nval) ? kk : 0;
     if (keff == 1) {
@@ -305,15 +408,14 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   const float xscale = (float)((double)kXBins / ((double)kXRange * T));
 
   // The draw over a kept set (FULL, or after a top-p cut): cut describes it.
-  Cut cut = cut_all();
+  FCut cut{-INFINITY, -1};
   double my_sum = 0.0;  // this thread's run weight over the kept set
 
   if (mode == kModeTopK || mode == kModeNucleus) {
     // ------------------------------------------------ histogram on the x grid
     for (int i = t0; i < t1; ++i) {
-      uint32_t key = KS::full(keys[i]);
-      if (key <= kNegInfKey) continue;
-      float v = key_to_float(key);
+      const float v = fv<DT>(keys, i);
+      if (!(v > -INFINITY)) continue;
       int b = xbin(v, vmax, xscale);
       if (mode == kModeNucleus) {
         double w = exp(((double)v - dmax) * inv_t);
@@ -455,9 +557,9 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       // ---------------------------------------- compact candidates locally
       int mine = 0;
       for (int i = t0; i < t1; ++i) {
-        uint32_t key = KS::full(keys[i]);
-        if (key <= kNegInfKey) continue;
-        int b = xbin(key_to_float(key), vmax, xscale);
+        const float v = fv<DT>(keys, i);
+        if (!(v > -INFINITY)) continue;
+        int b = xbin(v, vmax, xscale);
         mine += (gather == 1 ? b <= bstar : b == bstar) ? 1 : 0;
       }
       int ex, inc, tot;
@@ -465,11 +567,11 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       if (tot <= kCap) {
         int pos = ex;
         for (int i = t0; i < t1 && pos < inc; ++i) {
-          uint32_t key = KS::full(keys[i]);
-          if (key <= kNegInfKey) continue;
-          int b = xbin(key_to_float(key), vmax, xscale);
+          const float v = fv<DT>(keys, i);
+          if (!(v > -INFINITY)) continue;
+          int b = xbin(v, vmax, xscale);
           if (gather == 1 ? b <= bstar : b == bstar) {
-            ckey[pos] = key;
+            ckey[pos] = fkey(v);
             cidx[pos] = lo + i;
             ++pos;
           }
@@ -653,14 +755,13 @@ __global__ void __launch_bounds__(kFastThreads, 2)
         }
       }
       cluster.sync();  // ------------------------------------------------ S6
-      cut.key = ctl.cut_key;
-      cut.cut = ctl.cut_idx;
+      cut.v = key_to_float(ctl.cut_key);
+      cut.idx = ctl.cut_idx;
       // weights of the kept set in my run
       my_sum = 0.0;
       for (int i = t0; i < t1; ++i) {
-        uint32_t key = KS::full(keys[i]);
-        if (key > kNegInfKey && kept(cut, key, lo + i))
-          my_sum += exp(((double)key_to_float(key) - dmax) * inv_t);
+        const float v = fv<DT>(keys, i);
+        if (v > -INFINITY && fkept(cut, v, lo + i)) my_sum += exp(((double)v - dmax) * inv_t);
       }
       double s = block_sum<kFastThreads>(my_sum, sc.redd);
       if (tid == 0) ctl.sum = s;
@@ -670,8 +771,8 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   } else {
     // FULL: every valid token is kept
     for (int i = t0; i < t1; ++i) {
-      uint32_t key = KS::full(keys[i]);
-      if (key > kNegInfKey) my_sum += exp(((double)key_to_float(key) - dmax) * inv_t);
+      const float v = fv<DT>(keys, i);
+      if (v > -INFINITY) my_sum += exp(((double)v - dmax) * inv_t);
     }
     double s = block_sum<kFastThreads>(my_sum, sc.redd);
     if (tid == 0) ctl.sum = s;
@@ -687,10 +788,8 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       total += sums[q];
     }
     auto wt = [&](int i) -> double {  // i: slice-local index
-      uint32_t key = KS::full(keys[i]);
-      return (key > kNegInfKey && kept(cut, key, lo + i))
-                 ? exp(((double)key_to_float(key) - dmax) * inv_t)
-                 : 0.0;
+      const float v = fv<DT>(keys, i);
+      return (v > -INFINITY && fkept(cut, v, lo + i)) ? exp(((double)v - dmax) * inv_t) : 0.0;
     };
     if (!(U > 0.0)) {
       if (rank == 0 && tid == 0) write_row(a, row, 0, (float)(wt(0) / total), (int32_t)fl);

@@ -36,7 +36,7 @@ constexpr int kOnePerSmBytes = 227 * 1024;
 struct FastPlan {
   int C = 0;   // cluster size; 0 = no on-chip path
   int S = 0;   // slice length (elements), multiple of 16
-  int R = 0;   // per-thread run length (odd: conflict-free shared-memory strides)
+  int R = 0;   // per-thread run length (a multiple of 4 with an odd quarter)
   int smem = 0;
 };
 
@@ -52,7 +52,11 @@ FastPlan plan_fast(int64_t V, int dtype) {
       if (smem <= limit) {
         p.C = C;
         p.S = S;
-        p.R = ((S + ms::kFastThreads - 1) / ms::kFastThreads) | 1;
+        // per-thread run: a multiple of 4 (vector loads) whose quarter is odd
+        // (conflict-free 8- and 16-byte shared-memory accesses across a warp)
+        int q4 = ((S + ms::kFastThreads - 1) / ms::kFastThreads + 3) / 4;
+        if ((q4 & 1) == 0) ++q4;
+        p.R = 4 * q4;
         p.smem = smem;
         return p;
       }
