@@ -26,6 +26,7 @@ namespace cg = cooperative_groups;
 
 constexpr int kFastThreads = 512;
 constexpr int kFastWarps = kFastThreads / 32;
+constexpr int kMaxCluster = 16;
 constexpr int kCap = 1024;                 // on-chip candidate capacity of the leader CTA
 constexpr int kXBins = 2048;               // x-grid bins over [0, 40) units of (max - x)
 constexpr float kXRange = 40.0f;           // exp(-40) ~ 4e-18: past it a token's weight is noise
@@ -62,6 +63,7 @@ struct FastLayout {
   int work;      // histogram / candidate union
   int red;       // reduced bin range of this CTA
   int ctl;
+  int lctl;   // local copies of every CTA's control block
   int scratch;
   int mbar;
   int total;
@@ -78,7 +80,8 @@ __host__ __device__ inline FastLayout fast_layout(int S, int key_bytes, int C) {
   L.work = align16(S * key_bytes);
   L.red = L.work + kWorkBytes;
   L.ctl = L.red + align16((kXBins / C) * 12);
-  L.scratch = L.ctl + align16((int)sizeof(FastCtl));
+  L.lctl = L.ctl + align16((int)sizeof(FastCtl));
+  L.scratch = L.lctl + align16(kMaxCluster * (int)sizeof(FastCtl));
   L.mbar = L.scratch + align16((int)sizeof(FastScratch));
   L.total = L.mbar + 16;
   return L;
@@ -146,6 +149,25 @@ __device__ __forceinline__ void load4(const void *vals, int i, float x[4]) {
 
 constexpr uint32_t kHasNegInf = 1u << 29;  // flag: a -inf logit in an unmasked row
 
+// After a cluster barrier: C threads copy the C control blocks into local
+// shared memory, so the rest of the CTA reads them locally.
+template <int C>
+__device__ __forceinline__ void pull_ctl(cg::cluster_group &cluster, FastCtl &ctl, FastCtl *lctl) {
+  if (threadIdx.x < C) {
+    const FastCtl *r = cluster.map_shared_rank(&ctl, (int)threadIdx.x);
+    FastCtl &d = lctl[threadIdx.x];
+    d.max_key = r->max_key;
+    d.max_idx = r->max_idx;
+    d.nvalid = r->nvalid;
+    d.flags = r->flags;
+    d.sum = r->sum;
+    d.rcnt = r->rcnt;
+    d.rq = r->rq;
+    d.ncand = r->ncand;
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -185,6 +207,7 @@ __global__ void __launch_bounds__(kFastThreads, 2)
   uint32_t *rcnt = reinterpret_cast<uint32_t *>(smem + L.red);
   unsigned long long *rq = reinterpret_cast<unsigned long long *>(smem + L.red + NBR * 4);
   FastCtl &ctl = *reinterpret_cast<FastCtl *>(smem + L.ctl);
+  FastCtl *lctl = reinterpret_cast<FastCtl *>(smem + L.lctl);
   FastScratch &sc = *reinterpret_cast<FastScratch *>(smem + L.scratch);
   uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.mbar);
 
@@ -346,10 +369,11 @@ __global__ void __launch_bounds__(kFastThreads, 2)
     }
   }
   cluster.sync();  // ---------------------------------------------------- S1
+  pull_ctl<C>(cluster, ctl, lctl);
   uint32_t M_key = 0u, nval = 0u, rflags = 0u;
   int M_idx = 0x7FFFFFFF;
   for (int q = 0; q < C; ++q) {
-    const FastCtl *rc = cluster.map_shared_rank(&ctl, q);
+    const FastCtl *rc = &lctl[q];
     uint32_t k2 = rc->max_key;
     int i2 = rc->max_idx;
     if (k2 > M_key || (k2 == M_key && i2 < M_idx)) {
@@ -467,6 +491,7 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       }
     }
     cluster.sync();  // -------------------------------------------------- S3
+    pull_ctl<C>(cluster, ctl, lctl);
     // every CTA: total weight, threshold, crossing range and bin
     double total = 0.0;
     unsigned long long qtot = 0;
@@ -474,7 +499,7 @@ __global__ void __launch_bounds__(kFastThreads, 2)
     uint32_t rc_all[C];
     unsigned long long rq_all[C];
     for (int q = 0; q < C; ++q) {
-      const FastCtl *rc = cluster.map_shared_rank(&ctl, q);
+      const FastCtl *rc = &lctl[q];
       rc_all[q] = rc->rcnt;
       rq_all[q] = rc->rq;
       qtot += rq_all[q];
@@ -581,7 +606,8 @@ __global__ void __launch_bounds__(kFastThreads, 2)
       cluster.sync();  // ------------------------------------------------ S4
       int offs[C + 1];
       offs[0] = 0;
-      for (int q = 0; q < C; ++q) offs[q + 1] = offs[q] + cluster.map_shared_rank(&ctl, q)->ncand;
+      pull_ctl<C>(cluster, ctl, lctl);
+      for (int q = 0; q < C; ++q) offs[q + 1] = offs[q] + lctl[q].ncand;
       const int ntot = offs[C];
       if (ntot > kCap) {  // cannot happen (counts are exact); stay safe
         if (leader && tid == 0) a.status[row] = kRowPending;
@@ -781,10 +807,11 @@ __global__ void __launch_bounds__(kFastThreads, 2)
 
   // ------------------------------------------------- index-order draw (FULL)
   {
+    pull_ctl<C>(cluster, ctl, lctl);
     double sums[C];
     double total = 0.0;
     for (int q = 0; q < C; ++q) {
-      sums[q] = cluster.map_shared_rank(&ctl, q)->sum;
+      sums[q] = lctl[q].sum;
       total += sums[q];
     }
     auto wt = [&](int i) -> double {  // i: slice-local index
