@@ -23,6 +23,14 @@ __device__ __forceinline__ float key_to_float(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
 }
 
+// Order key of a finite-or-(-inf) float; -0 and +0 share a key, since the
+// reference compares values, not bit patterns.
+__device__ __forceinline__ uint32_t fkey(float v) {
+  uint32_t u = __float_as_uint(v);
+  if (u == 0x80000000u) u = 0u;
+  return bits_to_key(u);
+}
+
 // Raw fp32 bits of logit i (bf16 widened exactly).
 template <int DT>
 __device__ __forceinline__ uint32_t raw_bits(const void *row, int i) {
@@ -143,6 +151,26 @@ __device__ __forceinline__ int block_min_i(int v, int *red) {
   }
   __syncthreads();
   int t = red[32];
+  __syncthreads();
+  return t;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max_f(float v, float *red) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = lane < NW ? red[lane] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xFFFFFFFFu, t, o));
+    if (lane == 0) red[32] = t;
+  }
+  __syncthreads();
+  const float t = red[32];
   __syncthreads();
   return t;
 }

@@ -17,8 +17,8 @@
 #include <atomic>
 
 #include "ms_common.cuh"
-#include "ms_fast.cuh"
 #include "ms_generic.cuh"
+#include "ms_stream.cuh"
 
 namespace {
 thread_local int g_last_cuda_error = 0;
@@ -29,85 +29,26 @@ int cuda_fail(cudaError_t e) {
 }
 
 constexpr int kMaxDevices = 64;
-constexpr int kFastMaxV = 1 << 19;          // fixed-point weight sums stay below 2^63
-constexpr int kTwoPerSmBytes = 110 * 1024;  // two CTAs per SM
-constexpr int kOnePerSmBytes = 227 * 1024;
+constexpr int kStreamMaxV = ms::kMaxSubs / 2 * ms::kChunk;  // per-sub-chunk totals fit
 
-struct FastPlan {
-  int C = 0;   // cluster size; 0 = no on-chip path
-  int S = 0;   // slice length (elements), multiple of 16
-  int R = 0;   // per-thread run length (a multiple of 4 with an odd quarter)
-  int smem = 0;
-};
-
-FastPlan plan_fast(int64_t V, int dtype) {
-  FastPlan p;
-  if (V > kFastMaxV) return p;
-  const int kb = dtype == MS_DTYPE_F32 ? 4 : 2;
-  for (int limit : {kTwoPerSmBytes, kOnePerSmBytes}) {
-    for (int C : {4, 8, 16}) {
-      int S = (int)((V + C - 1) / C);
-      S = (S + 15) & ~15;
-      int smem = ms::fast_layout(S, kb, C).total;
-      if (smem <= limit) {
-        p.C = C;
-        p.S = S;
-        // per-thread run: a multiple of 4 (vector loads) whose quarter is odd
-        // (conflict-free 8- and 16-byte shared-memory accesses across a warp)
-        int q4 = ((S + ms::kFastThreads - 1) / ms::kFastThreads + 3) / 4;
-        if ((q4 & 1) == 0) ++q4;
-        p.R = 4 * q4;
-        p.smem = smem;
-        return p;
-      }
-    }
+// The streaming kernel (one CTA per row) for every row it can finish, then
+// the generic kernel for the rows it marked pending.
+template <int DT>
+cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, bool generic_only) {
+  if (generic_only || a.V > kStreamMaxV) {
+    ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
+    return cudaGetLastError();
   }
-  return p;
-}
-
-// cudaFuncSetAttribute once per (kernel, device).
-template <int C, int DT>
-cudaError_t prepare_fast(int dev) {
   static std::atomic<int> ready[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  if (ready[dev].load(std::memory_order_acquire)) return cudaSuccess;
-  auto kern = ms::ms_fast_kernel<C, DT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kOnePerSmBytes);
-  if (e == cudaSuccess && C > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess) ready[dev].store(1, std::memory_order_release);
-  return e;
-}
-
-template <int C, int DT>
-cudaError_t launch_fast(const ms::SampleArgs &a, int B, const FastPlan &p, cudaStream_t s, int dev) {
-  cudaError_t e = prepare_fast<C, DT>(dev);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(B * C));
-  cfg.blockDim = dim3(ms::kFastThreads);
-  cfg.dynamicSmemBytes = (size_t)p.smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, ms::ms_fast_kernel<C, DT>, a, p.S, p.R);
-}
-
-template <int DT>
-cudaError_t launch_all(const ms::SampleArgs &a, int B, const FastPlan &p, cudaStream_t s, int dev) {
-  cudaError_t e;
-  switch (p.C) {
-    case 4: e = launch_fast<4, DT>(a, B, p, s, dev); break;
-    case 8: e = launch_fast<8, DT>(a, B, p, s, dev); break;
-    case 16: e = launch_fast<16, DT>(a, B, p, s, dev); break;
-    default:
-      ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
-      return cudaGetLastError();
+  if (!ready[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(ms::ms_stream_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(ms::StShared));
+    if (e != cudaSuccess) return e;
+    ready[dev].store(1, std::memory_order_release);
   }
+  ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -152,9 +93,8 @@ static int sample_impl(const void *logits, int dtype, int64_t B, int64_t V, int6
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
-  const FastPlan p = generic_only ? FastPlan{} : plan_fast(V, dtype);
-  e = dtype == MS_DTYPE_F32 ? launch_all<MS_DTYPE_F32>(a, (int)B, p, s, dev)
-                            : launch_all<MS_DTYPE_BF16>(a, (int)B, p, s, dev);
+  e = dtype == MS_DTYPE_F32 ? launch_all<MS_DTYPE_F32>(a, (int)B, s, dev, generic_only)
+                            : launch_all<MS_DTYPE_BF16>(a, (int)B, s, dev, generic_only);
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;
 }
