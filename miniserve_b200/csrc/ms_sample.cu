@@ -29,13 +29,12 @@ int cuda_fail(cudaError_t e) {
 }
 
 constexpr int kMaxDevices = 64;
-constexpr int kStreamMaxV = ms::kMaxSubs / 2 * ms::kChunk;  // per-sub-chunk totals fit
 
 // The streaming kernel (one CTA per row) for every row it can finish, then
 // the generic kernel for the rows it marked pending.
 template <int DT>
 cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, bool generic_only) {
-  if (generic_only || a.V > kStreamMaxV) {
+  if (generic_only || a.V > ms::kStreamMaxV) {
     ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
     return cudaGetLastError();
   }

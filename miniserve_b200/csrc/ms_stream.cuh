@@ -1,22 +1,35 @@
 // Streaming sampling kernel: one 512-thread CTA per logits row, two CTAs per
 // SM.  The row streams from HBM through a ring of shared-memory stages filled
 // by cp.async.bulk (TMA) copies, so a CTA never holds more than three 4096-
-// element chunks and every synchronisation is CTA-local.
+// element chunks and every synchronisation is CTA-local.  Each warp owns one
+// "unit" of every chunk: 256 consecutive elements.
 //
 //   argmax rows (temperature 0, or top_k == 1)  one pass: per-thread first
 //                                                maximum, block argmax
 //   top-k rows (2 <= top_k <= kStTopK)          one pass: adaptive threshold
 //                                                + candidate buffer, exact
 //                                                finish on <= top_k entries
-//   top-p-only / full-softmax rows              pass 1 (HBM) for the maximum;
-//                                                later passes re-read the row
-//                                                from L2 (it is loaded with
-//                                                an L2 evict-last hint)
+//   full-softmax rows (no top-k, top_p >= 1)    one pass: per-unit maximum and
+//                                                weight sum; the draw re-reads
+//                                                one unit
+//   top-p-only rows                             pass 1 as above (L2 evict-last
+//                                                hint), pass 2 an integer x-grid
+//                                                histogram that brackets the
+//                                                top-p crossing, pass 3 gathers
+//                                                the bracket and the per-unit
+//                                                mass above it; exact cut and
+//                                                a one-unit draw
+//
+// Every weight of a softmax row is the same function of (logit, unit):
+// W_u(v) * f_u with W_u(v) = 2^((v - m_u) log2(e) / T) in fp32 (m_u the unit
+// maximum) and f_u = 2^((m_u - max) log2(e) / T), so totals, cuts and draws
+// agree with each other to the last bit of each term.
 //
 // Semantics follow miniserve/sampler.py:23-68 (see ms_sample.cu).  Rows
 // outside what this kernel finishes exactly (NaN or +inf logits, top_k above
-// kStTopK that may still cut, candidate buffers overflowing on heavy ties)
-// get status kRowPending and are finished by ms_generic_pending_kernel.
+// kStTopK that may still cut, candidate buffers overflowing on heavy ties,
+// temperatures below 1e-30) get status kRowPending and are finished by
+// ms_generic_pending_kernel.
 #pragma once
 
 #include "ms_common.cuh"
@@ -26,14 +39,21 @@ namespace ms {
 
 constexpr int kStThreads = 512;
 constexpr int kStWarps = kStThreads / 32;
-constexpr int kSub = kStThreads * 4;  // elements per sub-chunk: 4 consecutive per thread
-constexpr int kChunk = 2 * kSub;      // elements per chunk (one TMA copy)
+constexpr int kUnit = 256;                      // elements per unit: one warp's share of a chunk
+constexpr int kChunk = kStWarps * kUnit;        // elements per chunk (one TMA copy)
 constexpr int kStages = 3;
-constexpr int kCandCap = 4096;        // candidate buffer entries
-constexpr int kStTopK = 256;          // largest top_k resolved by the streaming pass
-constexpr int kSBins = 2048;          // x-grid bins (top-p)
-constexpr float kSXRange = 40.0f;     // grid depth, units of x = logit / T
-constexpr int kMaxSubs = 1024;        // sub-chunk totals kept per row (V <= 2^21)
+constexpr int kCandCap = 6144;                  // top-k candidate buffer entries
+constexpr int kSortCap = 4096;                  // largest set st_sort handles
+constexpr int kRankCap = 1024;                  // largest set sorted by rank counting
+constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
+constexpr int kMaxUnits = 1024;                 // per-unit summaries kept per row
+constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
+constexpr int kSBins = 2048;                    // x-grid bins (top-p)
+constexpr float kSXRange = 40.0f;               // grid depth, units of x = (max - logit) / T
+constexpr float kQScale = 65536.0f;             // fixed-point scale of in-bin weights
+constexpr uint32_t kBinCntMax = 65535u;         // a bin with more entries may wrap its mass sum
+constexpr double kHistTol = 4e-5;               // bound on the histogram's running-mass error / total
+constexpr double kMinTemperature = 1e-30;       // fp32 weights need a finite log2(e)/T
 
 struct StShared {
   alignas(128) unsigned char stage[kStages][kChunk * 4];
@@ -41,14 +61,25 @@ struct StShared {
     struct {
       uint32_t key[kCandCap];
       int idx[kCandCap];
-    } c;
+    } c;  // top-k candidates
     struct {
-      uint32_t cnt[kSBins];
-      float mass[kSBins];
-    } h;
+      float m[kMaxUnits];  // unit maxima
+      float s[kMaxUnits];  // unit weight sums; after pass 3 the mass above the bracket
+      float f[kMaxUnits];  // unit scales
+      union {
+        struct {
+          uint32_t cnt[kSBins];
+          uint32_t q[kSBins];
+        } h;  // x-grid histogram
+        struct {
+          uint32_t key[kSortCap];
+          int idx[kSortCap];
+        } g;  // the bracket's elements
+      } x;
+    } n;
   } w;
-  uint32_t tmaxk[kStThreads];  // per-thread maxima as keys (top-k bound)
-  double subsum[kMaxSubs];
+  uint32_t wbound[kStWarps];
+  int wcnt[2][kStWarps];  // per-warp insert counts of the last two chunks
   uint32_t hist256[256];
   unsigned long long full[kStages];
   double redd[33];
@@ -180,10 +211,23 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
   }
 }
 
-// One pass over the row.  `body(x[4], gidx0, sub)` sees this thread's 4
-// consecutive values of each sub-chunk (gidx0 = global index of x[0]; sub =
-// sub-chunk number, index order).  Returns false when a copy timed out
-// (after draining).  `ph` carries the stages' phase parities across passes.
+// This thread's 8 elements of chunk c (in stage s): x[0..3] at chunk offset
+// warp*kUnit + lane*4, x[4..7] 128 further on, so a warp's 256 values are one
+// unit.  Returns the global index of x[0].
+template <int DT>
+__device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
+  const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
+  st_get4<DT>(sh, r, c, s, j, x);
+  st_get4<DT>(sh, r, c, s, j + 128, x + 4);
+  return c * kChunk + j;
+}
+// global index of x[e] given that of x[0]
+__device__ __forceinline__ int st_gidx(int g0, int e) { return e < 4 ? g0 + e : g0 + 124 + e; }
+
+// One pass over the row.  `body(x[8], g0, u)` sees this thread's 8 values of
+// each chunk (st_get8 layout; u = the warp's unit number, index order).
+// Returns false when a copy timed out.  `ph` carries the stages' phase
+// parities across passes.
 template <int DT, class Body>
 __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph, Body body) {
   const int tid = threadIdx.x;
@@ -195,13 +239,9 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
     const int s = c % kStages;
     if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
     ph ^= 1u << s;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float x[4];
-      const int j = h * kSub + tid * 4;
-      st_get4<DT>(sh, r, c, s, j, x);
-      body(x, c * kChunk + j, c * 2 + h);
-    }
+    float x[8];
+    const int g0 = st_get8<DT>(sh, r, c, s, x);
+    body(x, g0, c * kStWarps + (tid >> 5));
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && c + kStages < r.nchunks) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -209,6 +249,12 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
     }
   }
   return __syncthreads_and(ok) != 0;
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
 }
 
 // --------------------------------------------------------- block selection
@@ -223,10 +269,17 @@ __device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int
     const int shift = 24 - 8 * d;
     for (int b = tid; b < 256; b += kStThreads) sh.hist256[b] = 0u;
     __syncthreads();
-    for (int i = tid; i < n; i += kStThreads) {
-      const uint32_t key = keys[i];
-      if (d > 0 && (key >> (shift + 8)) != prefix) continue;
-      atomicAdd(&sh.hist256[(key >> shift) & 255u], 1u);
+    // keys share leading digits heavily: one atomic per distinct digit per warp
+    for (int i0 = 0; i0 < n; i0 += kStThreads) {
+      const int i = i0 + tid;
+      const uint32_t key = i < n ? keys[i] : 0u;
+      const bool in = i < n && (d == 0 || (key >> (shift + 8)) == prefix);
+      const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
+      if (in) {
+        const uint32_t digit = (key >> shift) & 255u;
+        const unsigned same = __match_any_sync(act, digit);
+        if ((tid & 31) == __ffs(same) - 1) atomicAdd(&sh.hist256[digit], (uint32_t)__popc(same));
+      }
     }
     __syncthreads();
     // digit whose running count from the top reaches rem
@@ -276,7 +329,7 @@ __device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int
 }
 
 // ------------------------------------------------------------ bitonic sort
-// Sort n <= cap entries (key, idx) in shared memory into (key desc, index asc)
+// Sort n <= kSortCap entries (key, idx) in shared memory into (key desc, index asc)
 // order, or by index ascending when by_index.  Pads to a power of two with
 // entries that sort last.  All threads.
 __device__ void st_sort(uint32_t *key, int *idx, int n, bool by_index) {
@@ -360,69 +413,162 @@ __device__ void st_draw_sorted(StShared &sh, const SampleArgs &a, int row, const
   }
 }
 
-// Exact finish over a candidate set that contains the top-k (or nucleus) set:
-// entries (key, idx) in sh.w.c, n of them.  m_keep0 = entries kept before
-// top-p (top_k, or all); total0 = the softmax normaliser over that set when
-// known (<= 0: compute it over the m_keep0 best entries).  float64 weights
-// exp(l/T - max/T) as in miniserve/sampler.py:35,45; top-p in sorted order
-// (sampler.py:50-57); index-order draw (sampler.py:62-68).
-__device__ void st_finish_set(StShared &sh, const SampleArgs &a, int row, int n, int m_keep0,
-                              double total0, double T, double P, double U, float vmax) {
+// Sort n <= kRankCap entries (key, idx) into (key desc, idx asc) order, or
+// into index order when by_index (keys carried along), by counting for each
+// entry the entries that precede it.  Stage 0 (idle) holds the composites.
+// All threads.
+__device__ void st_rank_sort(StShared &sh, uint32_t *key, int *idx, int n, bool by_index) {
   const int tid = threadIdx.x;
-  uint32_t *key = sh.w.c.key;
-  int *idx = sh.w.c.idx;
-  st_sort(key, idx, n, false);
-  const int m = min(m_keep0, n);
-  const double xmax = (double)vmax / T;
-  auto wk = [&](uint32_t k) -> double { return exp((double)key_to_float(k) / T - xmax); };
-  double total = total0;
-  if (!(total > 0.0)) {
-    double s = 0.0;
-    for (int i = tid; i < m; i += kStThreads) s += wk(key[i]);
-    total = block_sum<kStThreads>(s, sh.redd);
+  unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
+  // larger composite = earlier in the target order; all distinct (indices are)
+  for (int i = tid; i < n; i += kStThreads) {
+    const unsigned long long ni = (unsigned long long)(~(uint32_t)idx[i]);
+    comp[i] = by_index ? ((ni << 32) | key[i]) : (((unsigned long long)key[i] << 32) | ni);
   }
-  int nkeep = m;
-  if (P < 1.0) {
-    const int per = (m + kStThreads - 1) / kStThreads;
-    const int p0 = tid * per, p1 = min(m, p0 + per);
-    double s = 0.0;
-    for (int i = p0; i < p1; ++i) s += wk(key[i]);
-    double ex, inc, tot;
-    block_scan<kStThreads, double>(s, ex, inc, tot, sh.redd);
-    const double target = P * total;
-    int cand = 0x7FFFFFFF;
-    if (p0 < p1 && inc >= target) {
-      double acc = ex;
-      for (int i = p0; i < p1; ++i) {
-        acc += wk(key[i]);
-        if (acc >= target) {
-          cand = i;
-          break;
-        }
-      }
-      if (cand == 0x7FFFFFFF) cand = p1 - 1;
+  if (tid == 0) comp[n] = 0ull;  // pad for the paired reads
+  __syncthreads();
+  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(comp);
+  const int npair = (n + 1) >> 1;
+  for (int i = tid; i < n; i += kStThreads) {
+    const unsigned long long ci = comp[i];
+    int rank = 0;
+    for (int j = 0; j < npair; ++j) {
+      const ulonglong2 q = c2[j];
+      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
     }
-    const int first = block_min_i<kStThreads>(cand, sh.redi);
+    if (by_index) {
+      key[rank] = (uint32_t)ci;
+      idx[rank] = (int)~(uint32_t)(ci >> 32);
+    } else {
+      key[rank] = (uint32_t)(ci >> 32);
+      idx[rank] = (int)~(uint32_t)ci;
+    }
+  }
+  __syncthreads();
+}
+
+// jw-th largest of the warp's running maxima, as a key (0 for -inf).
+__device__ __forceinline__ uint32_t warp_kth_key(float rmax, int jw) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key = rmax > -INFINITY ? fkey(rmax) : 0u;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {  // bitonic sort, ascending
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const uint32_t o = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
+      const bool asc = (lane & size) == 0 || size == 32;
+      const bool low = (lane & stride) == 0;
+      key = (low == asc) ? min(key, o) : max(key, o);
+    }
+  }
+  return __shfl_sync(0xFFFFFFFFu, key, 32 - jw);
+}
+
+// Lower bound on the k-th largest value of the row, as a key: each warp takes
+// the jw-th largest (jw = ceil(k/16)) of its lanes' running maxima; the
+// minimum over the 16 warps has at least 16*jw >= k maxima, each a distinct
+// element, at or above it.  0 when some warp holds fewer than jw finite
+// maxima.  All threads; one barrier.
+__device__ __forceinline__ uint32_t st_topk_bound(StShared &sh, float rmax, int jw) {
+  const uint32_t bw = warp_kth_key(rmax, jw);
+  if ((threadIdx.x & 31) == 0) sh.wbound[threadIdx.x >> 5] = bw;
+  __syncthreads();
+  uint32_t bmin = 0xFFFFFFFFu;
+#pragma unroll
+  for (int q = 0; q < kStWarps; ++q) bmin = min(bmin, sh.wbound[q]);
+  return bmin;
+}
+
+// The same bound without a barrier: each warp publishes its own (it only
+// grows, running maxima only grow) and takes the minimum of what the others
+// last published, which is still a valid bound.  Per warp.
+__device__ __forceinline__ uint32_t st_topk_bound_nb(StShared &sh, float rmax, int jw) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t bw = warp_kth_key(rmax, jw);
+  volatile uint32_t *wb = sh.wbound;
+  if (lane == 0) wb[threadIdx.x >> 5] = bw;
+  __syncwarp();
+  return __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? wb[lane] : 0xFFFFFFFFu);
+}
+
+// Exact top-k finish over a candidate buffer of n <= kRankCap unordered
+// entries (sh.w.c) holding every member of the row's top-k set, ranked by
+// value descending then index ascending (the stable sort of
+// miniserve/sampler.py:37-44).  Keys below thr cannot rank in that set.
+// float64 weights exp(l/T - max/T) (sampler.py:35,45), top-p in rank order
+// (sampler.py:49-58), index-order draw (sampler.py:60-68).  The idle transfer
+// stages hold scratch.  All threads.
+__device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int n, int k, uint32_t thr,
+                                double T, double P, double U, float vmax) {
+  const int tid = threadIdx.x;
+  unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
+  // (key, ~index) composites: larger = earlier in rank order, all distinct
+  auto compose = [&](int i) -> unsigned long long {
+    return ((unsigned long long)sh.w.c.key[i] << 32) | (unsigned long long)(~(uint32_t)sh.w.c.idx[i]);
+  };
+  const int i1 = tid + kStThreads;
+  const int f0 = (tid < n && sh.w.c.key[tid] >= thr) ? 1 : 0;
+  const int f1 = (i1 < n && sh.w.c.key[i1] >= thr) ? 1 : 0;
+  const unsigned long long c0 = f0 ? compose(tid) : 0ull, c1 = f1 ? compose(i1) : 0ull;
+  int ex, inc, n2;
+  block_scan<kStThreads, int>(f0 + f1, ex, inc, n2, sh.redi);
+  if (f0) comp[ex] = c0;
+  if (f1) comp[ex + f0] = c1;
+  if (tid == 0) comp[n2] = 0ull;  // pad for the paired reads
+  __syncthreads();
+  const int m = min(n2, k);
+  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(comp);
+  const int npair = (n2 + 1) >> 1;
+  for (int i = tid; i < n2; i += kStThreads) {
+    const unsigned long long ci = comp[i];
+    int rank = 0;
+    for (int j = 0; j < npair; ++j) {
+      const ulonglong2 q = c2[j];
+      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
+    }
+    if (rank < m) {
+      sh.w.c.key[rank] = (uint32_t)(ci >> 32);
+      sh.w.c.idx[rank] = (int)~(uint32_t)ci;
+    }
+  }
+  __syncthreads();
+  // thread r holds rank r
+  const double xmax = (double)vmax / T;
+  const double w = tid < m ? exp((double)key_to_float(sh.w.c.key[tid]) / T - xmax) : 0.0;
+  double wex, winc, total;
+  block_scan<kStThreads, double>(w, wex, winc, total, sh.redd);
+  int nkeep = m;
+  if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept
+    const int first = block_min_i<kStThreads>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
     if (first != 0x7FFFFFFF) nkeep = first + 1;
   }
-  // the kept entries, by index
-  st_sort(key, idx, nkeep, true);
-  double s = 0.0;
-  for (int i = tid; i < nkeep; i += kStThreads) s += wk(key[i]);
-  const double tot_keep = block_sum<kStThreads>(s, sh.redd);
-  st_draw_sorted(sh, a, row, idx, nkeep, tot_keep, U, [&](int i) { return wk(key[i]); });
+  // kept entries in index order: position = kept entries of smaller index
+  double *dw = reinterpret_cast<double *>(sh.stage[1]);
+  int *didx = sh.w.c.idx + kStTopK;
+  if (tid < nkeep) {
+    const int my = sh.w.c.idx[tid];
+    int pos = 0;
+    for (int j = 0; j < nkeep; ++j) pos += sh.w.c.idx[j] < my ? 1 : 0;
+    didx[pos] = my;
+    dw[pos] = w;
+  }
+  const double tot_keep = block_sum<kStThreads>(tid < nkeep ? w : 0.0, sh.redd);
+  st_draw_sorted(sh, a, row, didx, nkeep, tot_keep, U, [&](int i) { return dw[i]; });
 }
 
 // fp32 weight 2^((v - M) * log2(e) / T) from two FMAs and one ex2.approx:
 // c = c_hi + c_lo and M*c = mc_hi + mc_lo carry the constants to ~2^-48, so
 // the only roundings are the final sum (|z| * 2^-24) and ex2 (~2^-22).
+// set_t once per row, set_m per reference maximum M.
 struct StW {
   float c_hi, c_lo, mc_hi, mc_lo;
-  __device__ __forceinline__ void init(float M, double T) {
+  __device__ __forceinline__ void set_t(double T) {
     const double c = 1.4426950408889634 / T;  // log2(e) / T
     c_hi = (float)c;
     c_lo = (float)(c - (double)c_hi);
-    const double mc = (double)M * (double)c_hi;
+  }
+  __device__ __forceinline__ void set_m(float M) {
+    const double mc = (double)M * (double)c_hi;  // exact: 24 x 24 bits
     mc_hi = (float)mc;
     mc_lo = (float)(mc - (double)mc_hi) + (float)((double)M * (double)c_lo);
   }
@@ -434,27 +580,56 @@ struct StW {
   }
 };
 
-struct FCutS {
-  float v;
-  int idx;
-};
-
-// Four consecutive elements of the row from global memory (L2), masked
-// tokens and positions past the row as -inf.
+// Element gi of the row from global memory (L2), masked tokens as -inf.
 template <int DT>
-__device__ __forceinline__ void st_load4_global(const StRow &r, int g0, float x[4]) {
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int gi = g0 + e;
-    if (gi >= r.V) {
-      x[e] = -INFINITY;
-      continue;
-    }
-    x[e] = DT == MS_DTYPE_F32
-               ? __ldg(reinterpret_cast<const float *>(r.g) + gi)
-               : __uint_as_float((uint32_t)__ldg(reinterpret_cast<const unsigned short *>(r.g) + gi) << 16);
-    if (r.mask && !((__ldg(r.mask + (gi >> 5)) >> (gi & 31)) & 1u)) x[e] = -INFINITY;
+__device__ __forceinline__ float st_load1(const StRow &r, int gi) {
+  float v = DT == MS_DTYPE_F32
+                ? __ldg(reinterpret_cast<const float *>(r.g) + gi)
+                : __uint_as_float((uint32_t)__ldg(reinterpret_cast<const unsigned short *>(r.g) + gi) << 16);
+  if (r.mask && !((__ldg(r.mask + (gi >> 5)) >> (gi & 31)) & 1u)) v = -INFINITY;
+  return v;
+}
+
+// Index-order inverse CDF (miniserve/sampler.py:60-68) over a row whose kept
+// mass per unit is kept[0..nu) (sum `total`): the crossing unit from a block
+// scan, then that unit's 256 elements re-read with keptw(v, gi), the same
+// float64 weights the unit sums were made of.  Writes the row.  All threads.
+template <int DT, class KW>
+__device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r, int row, int nu,
+                              const double *kept, double total, double U, KW keptw) {
+  const int tid = threadIdx.x;
+  if (!(U > 0.0)) {  // r == 0 stops at index 0 (sampler.py:66)
+    if (tid == 0) write_row(a, row, 0, (float)(keptw(st_load1<DT>(r, 0), 0) / total), 0);
+    return;
   }
+  const double target = U * total;
+  const int u0 = 2 * tid;
+  const double k0 = u0 < nu ? kept[u0] : 0.0, k1 = u0 + 1 < nu ? kept[u0 + 1] : 0.0;
+  double ex, inc, tt;
+  block_scan<kStThreads, double>(k0 + k1, ex, inc, tt, sh.redd);
+  int cand = 0x7FFFFFFF;
+  if (k0 + k1 > 0.0 && inc >= target) cand = (k0 > 0.0 && ex + k0 >= target) ? u0 : u0 + 1;
+  const int us = block_min_i<kStThreads>(cand, sh.redi);
+  if (us == 0x7FFFFFFF) {  // ran past the end (sampler.py:68)
+    if (tid == 0) write_row(a, row, a.V - 1, (float)(keptw(st_load1<DT>(r, a.V - 1), a.V - 1) / total), 0);
+    return;
+  }
+  if (tid == (us >> 1)) sh.bcast_d[1] = (us == u0) ? ex : ex + k0;
+  __syncthreads();
+  const double before = sh.bcast_d[1];
+  const int gi = us * kUnit + tid;
+  const double w = (tid < kUnit && gi < a.V) ? keptw(st_load1<DT>(r, gi), gi) : 0.0;
+  double wex, winc, wtot;
+  block_scan<kStThreads, double>(w, wex, winc, wtot, sh.redd);
+  int who = block_min_i<kStThreads>((w > 0.0 && before + winc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  if (who == 0x7FFFFFFF) {  // rounding left the target past the unit: its last kept element
+    who = -block_min_i<kStThreads>(w > 0.0 ? -tid : 1, sh.redi);
+  }
+  if (who < 0) {  // no kept element in the unit (cannot happen for consistent sums)
+    if (tid == 0) a.status[row] = kRowPending;
+    return;
+  }
+  if (tid == who) write_row(a, row, gi, (float)(w / total), 0);
 }
 
 enum StMode : int { kStArgmax = 0, kStTopKMode = 1, kStFull = 2, kStNucleus = 3 };
@@ -465,6 +640,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   StShared &sh = *reinterpret_cast<StShared *>(st_raw);
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   const double T = a.temperature[row];
   const int k = a.top_k[row];
   const double P = a.top_p[row];
@@ -478,13 +654,15 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   if (T == 0.0 || k == 1) {
     mode = kStArgmax;
   } else if (k >= 2 && k < V) {
-    if (k > kStTopK) {  // may still cut: the generic kernel finishes it
-      if (tid == 0) a.status[row] = kRowPending;
-      return;
-    }
     mode = kStTopKMode;
   } else {
     mode = P < 1.0 ? kStNucleus : kStFull;
+  }
+  // top_k above what the streaming buffer resolves, or a temperature too small
+  // for fp32 weights: the generic kernel finishes the row
+  if ((mode == kStTopKMode && k > kStTopK) || (mode != kStArgmax && !(T >= kMinTemperature))) {
+    if (tid == 0) a.status[row] = kRowPending;
+    return;
   }
   StRow r;
   r.esz = DT == MS_DTYPE_F32 ? 4 : 2;
@@ -496,6 +674,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   if (tid < kStages) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
   }
+  if (tid < kStWarps) sh.wbound[tid] = 0u;
   if (tid == 0) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -512,13 +691,15 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     float mv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     int mi[4] = {0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF};
     float vsum = 0.0f;
+    // slot e & 3 sees its elements in increasing index order: strict > keeps
+    // the first maximum
     ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 8; ++e) {
         vsum += x[e];
-        if (x[e] > mv[e]) {
-          mv[e] = x[e];
-          mi[e] = g0 + e;
+        if (x[e] > mv[e & 3]) {
+          mv[e & 3] = x[e];
+          mi[e & 3] = st_gidx(g0, e);
         }
       }
     });
@@ -534,7 +715,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     uint32_t bk = tm > -INFINITY ? fkey(tm) : 0u;
     int bi = tm > -INFINITY ? ti : 0x7FFFFFFF;
     warp_argmax(bk, bi);
-    if ((tid & 31) == 0) {
+    if (lane == 0) {
       sh.redu[tid >> 5] = bk;
       sh.redi[tid >> 5] = bi;
     }
@@ -562,438 +743,454 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 
   // ================================================================= top-k
   if (mode == kStTopKMode) {
-    __shared__ float s_tau;  // candidates are values >= s_tau (> when s_strict)
-    __shared__ int s_strict, s_cc;
-    if (tid == 0) {
-      s_tau = -INFINITY;
-      s_strict = 0;
-      s_cc = 0;
-    }
-    float vmax_t = -INFINITY, vsum = 0.0f;
-    const int lane = tid & 31;
+    // Candidates are values >= tau (> when strict).  tau rises to lower
+    // bounds of the row's k-th largest value (st_topk_bound: with a barrier on
+    // chunk 0, barrier-free every 4th chunk after); ties at tau stay
+    // candidates.  A warp with no value at or above tau skips the insert.
+    float tau = -INFINITY;
+    bool strict = false;
+    float rmax = -INFINITY, vsum = 0.0f;
+    const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
+    int ncand = 0;  // exact buffer size, identical in every thread
     if (tid == 0) {
       for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_stream);
     }
-    __syncthreads();
     int c = 0;
-    for (; c < r.nchunks && !over; ++c) {
+    for (; c < r.nchunks; ++c) {
       const int s = c % kStages;
       if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
       ph ^= 1u << s;
       float x[8];
-      st_get4<DT>(sh, r, c, s, tid * 4, x);
-      st_get4<DT>(sh, r, c, s, kSub + tid * 4, x + 4);
-      const int g0 = c * kChunk + tid * 4, g1 = g0 + kSub;
-      float cm = -INFINITY;
+      const int g0 = st_get8<DT>(sh, r, c, s, x);
+      float cm = x[0];
+      vsum += x[0];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 1; e < 8; ++e) {
         vsum += x[e];
         cm = fmaxf(cm, x[e]);
       }
-      vmax_t = fmaxf(vmax_t, cm);
-      // Insert this chunk's values >= tau.  When they would not fit: shrink
-      // the buffer to its top-k, or raise tau to the k-th largest of this
-      // chunk's thread maxima (k distinct threads hold k values >= it, so
-      // the row's k-th largest is not below it).
-      for (int attempt = 0; attempt < 4; ++attempt) {
-        const float tau = s_tau;
-        const bool strict = s_strict != 0;
+      rmax = fmaxf(rmax, cm);
+      if ((c & 3) == 0) {
+        const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
+        if (bmin != 0u && key_to_float(bmin) > tau) {
+          tau = key_to_float(bmin);
+          strict = false;
+        }
+      }
+      // insert: one shared atomic per warp with candidates.  The buffer holds
+      // at most kCandCap - kChunk entries before each chunk, so it cannot
+      // overflow here.
+      int wt = 0;
+      if (__any_sync(0xFFFFFFFFu, strict ? cm > tau : cm >= tau)) {
         int cnt = 0;
 #pragma unroll
         for (int e = 0; e < 8; ++e) cnt += (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) ? 1 : 0;
-        if (!__syncthreads_or(cnt > 0)) break;  // common case: nothing to insert
-        int incl = cnt;
+        wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+        if (wt > 0) {
+          int incl = cnt;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        int wbase = 0;
-        if (lane == 31) wbase = atomicAdd(&s_cc, incl);
-        wbase = __shfl_sync(0xFFFFFFFFu, wbase, 31);
-        __syncthreads();
-        const int total = s_cc;
-        const int n0 = sh.ncand;
-        // the first chunk always starts from the thread-maxima bound
-        const bool fits = n0 + total <= kCandCap && !(c == 0 && attempt == 0 && total > k);
-        if (fits) {
-          int pos = n0 + wbase + incl - cnt;
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&sh.ncand, wt);  // positions only
+          base = __shfl_sync(0xFFFFFFFFu, base, 0);
+          int pos = base + incl - cnt;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             if (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) {
               sh.w.c.key[pos] = fkey(x[e]);
-              sh.w.c.idx[pos] = e < 4 ? g0 + e : g1 + e - 4;
+              sh.w.c.idx[pos] = st_gidx(g0, e);
               ++pos;
             }
           }
         }
-        __syncthreads();
-        if (tid == 0) {
-          if (fits) sh.ncand = n0 + total;
-          s_cc = 0;
-        }
-        __syncthreads();
-        if (fits) break;
-        if (attempt == 3) {
-          over = true;  // heavy ties: the generic kernel finishes the row
-          break;
-        }
-        if (n0 > k && attempt == 0) {
-          // keep the buffer's entries >= its k-th largest key (ties kept)
-          int above;
-          const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
-          uint32_t kv[kCandCap / kStThreads];
-          int iv[kCandCap / kStThreads];
-          int nk = 0;
-          for (int i = tid; i < n0; i += kStThreads) {
-            if (sh.w.c.key[i] >= kk) {
-              kv[nk] = sh.w.c.key[i];
-              iv[nk] = sh.w.c.idx[i];
-              ++nk;
-            }
-          }
-          int kex, kin, ktot;
-          block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
-          for (int q = 0; q < nk; ++q) {
-            sh.w.c.key[kex + q] = kv[q];
-            sh.w.c.idx[kex + q] = iv[q];
-          }
-          __syncthreads();
-          if (tid == 0) {
-            sh.ncand = ktot;
-            s_tau = key_to_float(kk);
-            s_strict = 1;  // >= k entries >= kk held: a later equal value ranks below them
-          }
-          __syncthreads();
-          continue;
-        }
-        sh.tmaxk[tid] = cm > -INFINITY ? fkey(cm) : 0u;
-        __syncthreads();
-        int above2;
-        const uint32_t bk = st_select_kth(sh, sh.tmaxk, kStThreads, k, &above2);
-        if (tid == 0 && bk != 0u && key_to_float(bk) > s_tau) {
-          s_tau = key_to_float(bk);
-          s_strict = 0;
-        }
-        __syncthreads();
       }
-      __syncthreads();  // stage s is free
-      if (tid == 0 && !over && c + kStages < r.nchunks) {
+      if (lane == 0) sh.wcnt[c & 1][tid >> 5] = wt;
+      __syncthreads();  // stage s is free; the buffer is settled
+      // exact count from the per-warp slots (slot c&1 is rewritten two chunks
+      // on, after a barrier every thread has passed)
+      ncand += __reduce_add_sync(0xFFFFFFFFu, lane < kStWarps ? sh.wcnt[c & 1][lane] : 0);
+      if (ncand > kCandCap - kChunk) {
+        // shrink to the entries >= the buffer's k-th largest (ties kept)
+        const int n0 = ncand;
+        int above;
+        const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
+        uint32_t kv[kCandCap / kStThreads];
+        int iv[kCandCap / kStThreads];
+        int nk = 0;
+        for (int i = tid; i < n0; i += kStThreads) {
+          if (sh.w.c.key[i] >= kk) {
+            kv[nk] = sh.w.c.key[i];
+            iv[nk] = sh.w.c.idx[i];
+            ++nk;
+          }
+        }
+        int kex, kin, ktot;
+        block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
+        for (int q = 0; q < nk; ++q) {
+          sh.w.c.key[kex + q] = kv[q];
+          sh.w.c.idx[kex + q] = iv[q];
+        }
+        if (tid == 0) sh.ncand = ktot;
+        __syncthreads();
+        ncand = ktot;
+        tau = key_to_float(kk);
+        strict = true;  // >= k entries >= kk are held: a later equal value ranks below
+        if (ktot > kCandCap - kChunk) over = true;  // heavy ties
+      }
+      if (over) break;
+      if (tid == 0 && c + kStages < r.nchunks) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         st_issue(sh, r, c + kStages, s, pol_stream);
       }
     }
-    // copies issued past the last consumed chunk (early stop) must land
-    // before this CTA's shared memory is released
-    for (int c2 = c; c2 < r.nchunks && c2 < c - 1 + kStages; ++c2) {
-      const int s = c2 % kStages;
-      if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
-      ph ^= 1u << s;
+    if (over) {
+      // copies of chunks c+1 .. c+kStages-1 are in flight: let them land
+      // before this CTA's shared memory is released
+      for (int c2 = c + 1; c2 < r.nchunks && c2 < c + kStages; ++c2) {
+        const int s2 = c2 % kStages;
+        if (!st_wait(sh, s2, (ph >> s2) & 1u)) ok = false;
+        ph ^= 1u << s2;
+      }
     }
     const bool bad = isnan(vsum) || vsum == INFINITY;
     if (__syncthreads_or(bad || !ok || over)) {
       if (tid == 0) a.status[row] = kRowPending;
       return;
     }
-    const float vmax = block_max_f<kStThreads>(vmax_t, sh.redf);
+    const float vmax = block_max_f<kStThreads>(rmax, sh.redf);
     if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
       if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
       return;
     }
-    // fewer valid tokens than top_k: the buffer holds all of them (top-k off)
-    const int n = sh.ncand;
-    int m = n;
-    if (n > k) {
-      st_sort(sh.w.c.key, sh.w.c.idx, n, false);  // (key desc, index asc)
-      m = k;
+    // exact top-k of the buffer; fewer valid tokens than top_k keep all
+    int n = ncand;
+    if (n > kRankCap) {
+      int above;
+      const uint32_t kk = st_select_kth(sh, sh.w.c.key, n, k, &above);
+      uint32_t kv[kCandCap / kStThreads];
+      int iv[kCandCap / kStThreads];
+      int nk = 0;
+      for (int i = tid; i < n; i += kStThreads) {
+        if (sh.w.c.key[i] >= kk) {
+          kv[nk] = sh.w.c.key[i];
+          iv[nk] = sh.w.c.idx[i];
+          ++nk;
+        }
+      }
+      int kex, kin, ktot;
+      block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
+      for (int q = 0; q < nk; ++q) {
+        sh.w.c.key[kex + q] = kv[q];
+        sh.w.c.idx[kex + q] = iv[q];
+      }
+      __syncthreads();
+      n = ktot;
     }
-    st_finish_set(sh, a, row, m, m, 0.0, T, P, U, vmax);
+    if (n > kRankCap) {  // a tie block larger than the rank sort: generic kernel
+      if (tid == 0) a.status[row] = kRowPending;
+      return;
+    }
+    st_finish_small(sh, a, row, n, k, st_topk_bound(sh, rmax, jw), T, P, U, vmax);
     return;
   }
 
-  // ===================================================== top-p / full softmax
+  // ====================================================== softmax over all
+  const bool nucleus = mode == kStNucleus;
+  StW W;
+  W.set_t(T);
   float vmax_t = -INFINITY, vsum = 0.0f;
-  ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int, int) {
+  // pass 1 (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
+  ok = st_pass<DT>(sh, r, nucleus ? pol_keep : pol_stream, ph, [&](const float *x, int, int u) {
+    float cm = x[0];
+    vsum += x[0];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 1; e < 8; ++e) {
       vsum += x[e];
-      vmax_t = fmaxf(vmax_t, x[e]);
+      cm = fmaxf(cm, x[e]);
+    }
+    vmax_t = fmaxf(vmax_t, cm);
+    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
+    float mu = -INFINITY, su = 0.0f;
+    if (km != 0u) {  // warp-uniform
+      mu = key_to_float(km);
+      StW Wu = W;
+      Wu.set_m(mu);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (x[e] > -INFINITY) su += Wu(x[e]);
+      su = warp_sum_f(su);
+    }
+    if (lane == 0) {
+      sh.w.n.m[u] = mu;
+      sh.w.n.s[u] = su;
     }
   });
-  const bool bad = isnan(vsum) || vsum == INFINITY;
-  if (__syncthreads_or(bad || !ok)) {
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
+  {
+    const bool bad = isnan(vsum) || vsum == INFINITY;
+    if (__syncthreads_or(bad || !ok)) {
+      if (tid == 0) a.status[row] = kRowPending;
+      return;
+    }
   }
   const float vmax = block_max_f<kStThreads>(vmax_t, sh.redf);
   if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
     if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
     return;
   }
-  StW W;
-  W.init(vmax, T);
-  const float xscale = (float)((double)kSBins / ((double)kSXRange * T));
-  const bool nucleus = mode == kStNucleus;
-  const int nsubs = 2 * r.nchunks;
-  for (int q = tid; q < nsubs; q += kStThreads) sh.subsum[q] = 0.0;
-  if (nucleus)
-    for (int b = tid; b < kSBins; b += kStThreads) {
-      sh.w.h.cnt[b] = 0u;
-      sh.w.h.mass[b] = 0.0f;
-    }
-  __syncthreads();
-  auto bin_of = [&](float v) -> int {
-    const float t = (vmax - v) * xscale;
-    return t < (float)kSBins ? (int)t : kSBins;
-  };
-  // pass 2 (L2): weights, per-sub-chunk totals, histogram
-  ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int, int sub) {
-    float ws = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (x[e] > -INFINITY) {
-        const float w = W(x[e]);
-        ws += w;
-        if (nucleus) {
-          const int b = bin_of(x[e]);
-          if (b < kSBins) {
-            atomicAdd(&sh.w.h.cnt[b], 1u);
-            atomicAdd(&sh.w.h.mass[b], w);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xFFFFFFFFu, ws, o);
-    if ((tid & 31) == 0 && ws != 0.0f) atomicAdd(&sh.subsum[sub], (double)ws);
-  });
-  if (!__syncthreads_and(ok)) {
+  const double cl = 1.4426950408889634 / T;
+  if (!(fabs((double)vmax) * cl < 1e37)) {  // max * log2(e)/T beyond fp32 range
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  double total;
-  {
-    double s = 0.0;
-    for (int q = tid; q < nsubs; q += kStThreads) s += sh.subsum[q];
-    total = block_sum<kStThreads>(s, sh.redd);
+  const int nu = r.nchunks * kStWarps;
+  // unit scales f_u and the softmax total
+  double zs = 0.0;
+  for (int u = tid; u < nu; u += kStThreads) {
+    const float mu = sh.w.n.m[u];
+    const float fu = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
+    sh.w.n.f[u] = fu;
+    zs += (double)sh.w.n.s[u] * (double)fu;
   }
-  FCutS cut{-INFINITY, -1};  // the kept set: everything valid
-  if (nucleus) {
-    // crossing bin: first bin (from the top) whose running weight reaches
-    // P * total; thread t owns bins 4t..4t+3
-    const double thr = P * total;
+  const double total = block_sum<kStThreads>(zs, sh.redd);  // ends with a barrier
+  double *kd = reinterpret_cast<double *>(sh.stage[1]);      // per-unit kept mass (stages idle)
+  auto unit_w = [&](float v, int gi) -> double {             // the weight of element gi
+    const int u = gi / kUnit;
+    StW Wu = W;
+    Wu.set_m(sh.w.n.m[u]);
+    return (double)Wu(v) * (double)sh.w.n.f[u];
+  };
+
+  if (!nucleus) {  // full softmax: every valid token kept
+    for (int u = tid; u < nu; u += kStThreads) kd[u] = (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
+    __syncthreads();
+    st_draw_units<DT>(sh, a, r, row, nu, kd, total, U,
+                      [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
+    return;
+  }
+
+  // pass 2 (L2): x-grid histogram, x = (max - v) / T, kSBins bins over
+  // [0, kSXRange): entry count and fixed-point mass relative to the bin's top
+  for (int b = tid; b < kSBins; b += kStThreads) {
+    sh.w.n.x.h.cnt[b] = 0u;
+    sh.w.n.x.h.q[b] = 0u;
+  }
+  __syncthreads();
+  const float xs = (float)((double)kSBins / ((double)kSXRange * T));  // bins per logit unit
+  const float dx = kSXRange / (float)kSBins;                          // x per bin
+  auto bin_of = [&](float v, float &frac) -> int {  // monotone non-increasing in v
+    const float t = (vmax - v) * xs;
+    if (!(t < (float)kSBins)) return kSBins;  // the tail
+    const int b = (int)t;
+    frac = t - (float)b;
+    return b;
+  };
+  uint32_t ntail = 0;
+  ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int, int) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (x[e] > -INFINITY) {
+        float fr = 0.0f;
+        const int b = bin_of(x[e], fr);
+        if (b < kSBins) {
+          const float y = fr * dx;  // x below the bin's top, in [0, dx)
+          const float ey = fmaf(fmaf(fmaf(y, -1.0f / 6.0f, 0.5f), y, -1.0f), y, 1.0f);  // e^-y to y^4/24
+          atomicAdd(&sh.w.n.x.h.cnt[b], 1u);
+          atomicAdd(&sh.w.n.x.h.q[b], __float2uint_rn(ey * kQScale));
+        } else {
+          ++ntail;
+        }
+      }
+    }
+  });
+  if (!ok) {
+    if (tid == 0) a.status[row] = kRowPending;
+    return;
+  }
+  // the bracket [b_lo, b_hi]: bins where the running mass crosses
+  // P*total -/+ kHistTol*total (bin kSBins = the tail)
+  const double pz = P * total;
+  int b_lo, b_hi, nr;
+  bool wrap = false;
+  {
+    double m4[4];
+    uint32_t c4[4];
     double s = 0.0;
-    uint32_t cn = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      s += (double)sh.w.h.mass[tid * 4 + q];
-      cn += sh.w.h.cnt[tid * 4 + q];
+      const int b = tid * 4 + q;
+      c4[q] = sh.w.n.x.h.cnt[b];
+      m4[q] = (double)sh.w.n.x.h.q[b] * (1.0 / (double)kQScale) * exp(-(double)b * (double)dx);
+      s += m4[q];
     }
     double ex, inc, tt;
     block_scan<kStThreads, double>(s, ex, inc, tt, sh.redd);
-    int cex, cin, ctt;
-    block_scan<kStThreads, int>((int)cn, cex, cin, ctt, sh.redi);
-    int cand = 0x7FFFFFFF;
-    if (inc >= thr) {
-      double acc = ex;
-      for (int q = 0; q < 4; ++q) {
-        const int b = tid * 4 + q;
-        const double bm = (double)sh.w.h.mass[b];
-        if (sh.w.h.cnt[b] > 0u && acc + bm >= thr) {
-          cand = b;
-          break;
-        }
-        acc += bm;
-      }
+    const double lo_t = pz - kHistTol * total, hi_t = pz + kHistTol * total;
+    int clo = 0x7FFFFFFF, chi = 0x7FFFFFFF;
+    double acc = ex;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      acc += m4[q];
+      if (clo == 0x7FFFFFFF && acc >= lo_t) clo = tid * 4 + q;
+      if (chi == 0x7FFFFFFF && acc >= hi_t) chi = tid * 4 + q;
     }
-    const int bstar = block_min_i<kStThreads>(cand, sh.redi);
-    if (bstar != 0x7FFFFFFF) {
-      if (tid == bstar / 4) {
-        double acc = ex;
-        int ca = cex;
-        for (int q = 0; q < 4; ++q) {
-          const int b = tid * 4 + q;
-          if (b == bstar) {
-            sh.bcast_d[0] = acc;
-            sh.bcast_i[1] = ca;
-            sh.bcast_i[2] = (int)sh.w.h.cnt[b];
-            break;
-          }
-          acc += (double)sh.w.h.mass[b];
-          ca += (int)sh.w.h.cnt[b];
-        }
-      }
-      __syncthreads();
-      const double above_w = sh.bcast_d[0];
-      const int above_c = sh.bcast_i[1];
-      const int in_c = sh.bcast_i[2];
-      __syncthreads();
-      const bool all_up_to = above_c + in_c <= kCandCap;
-      if (!all_up_to && in_c > kCandCap) {  // a crowded bin: generic kernel
-        if (tid == 0) a.status[row] = kRowPending;
-        return;
-      }
-      // pass 3 (L2): gather bins <= bstar, or bin bstar alone
-      if (tid == 0) sh.ncand = 0;
-      __syncthreads();
-      ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
+    b_lo = block_min_i<kStThreads>(clo, sh.redi);
+    b_hi = block_min_i<kStThreads>(chi, sh.redi);
+    if (b_lo == 0x7FFFFFFF) b_lo = kSBins;
+    if (b_hi == 0x7FFFFFFF) b_hi = kSBins;
+    uint32_t part = 0;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (x[e] > -INFINITY) {
-            const int b = bin_of(x[e]);
-            if (all_up_to ? b <= bstar : b == bstar) {
-              const int pos = atomicAdd(&sh.ncand, 1);
-              sh.w.c.key[pos] = fkey(x[e]);
-              sh.w.c.idx[pos] = g0 + e;
-            }
-          }
-        }
-      });
-      if (!__syncthreads_and(ok)) {
-        if (tid == 0) a.status[row] = kRowPending;
-        return;
-      }
-      const int n = sh.ncand;
-      if (all_up_to) {
-        // the nucleus lies among these: exact finish (total: all valid)
-        st_finish_set(sh, a, row, n, n, total, T, P, U, vmax);
-        return;
-      }
-      // the cut inside bin bstar, with the histogram's own weights
-      st_sort(sh.w.c.key, sh.w.c.idx, n, false);
-      {
-        const int per = (n + kStThreads - 1) / kStThreads;
-        const int p0 = tid * per, p1 = min(n, p0 + per);
-        double s2 = 0.0;
-        for (int i = p0; i < p1; ++i) s2 += (double)W(key_to_float(sh.w.c.key[i]));
-        double e2, i2, t2;
-        block_scan<kStThreads, double>(s2, e2, i2, t2, sh.redd);
-        int cc = 0x7FFFFFFF;
-        if (p0 < p1 && above_w + i2 >= thr) {
-          double acc = above_w + e2;
-          for (int i = p0; i < p1; ++i) {
-            acc += (double)W(key_to_float(sh.w.c.key[i]));
-            if (acc >= thr) {
-              cc = i;
-              break;
-            }
-          }
-          if (cc == 0x7FFFFFFF) cc = p1 - 1;
-        }
-        int rc = block_min_i<kStThreads>(cc, sh.redi);
-        if (rc == 0x7FFFFFFF) rc = n - 1;
-        cut.v = key_to_float(sh.w.c.key[rc]);
-        cut.idx = sh.w.c.idx[rc];
-      }
-      // pass 4 (L2): per-sub-chunk weight of the kept set
-      __syncthreads();
-      for (int q = tid; q < nsubs; q += kStThreads) sh.subsum[q] = 0.0;
-      __syncthreads();
-      ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int sub) {
-        float ws = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (x[e] > -INFINITY && (x[e] > cut.v || (x[e] == cut.v && g0 + e <= cut.idx))) ws += W(x[e]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xFFFFFFFFu, ws, o);
-        if ((tid & 31) == 0 && ws != 0.0f) atomicAdd(&sh.subsum[sub], (double)ws);
-      });
-      if (!__syncthreads_and(ok)) {
-        if (tid == 0) a.status[row] = kRowPending;
-        return;
-      }
-      double s3 = 0.0;
-      for (int q = tid; q < nsubs; q += kStThreads) s3 += sh.subsum[q];
-      total = block_sum<kStThreads>(s3, sh.redd);
+    for (int q = 0; q < 4; ++q) {
+      const int b = tid * 4 + q;
+      if (b >= b_lo && b <= b_hi) part += c4[q];
+      if (b <= b_hi && c4[q] > kBinCntMax) wrap = true;
     }
-    // bstar not found: the running sum never reached top_p; all kept
+    const uint32_t tail = block_sum_u32<kStThreads>(ntail, sh.redu);
+    nr = (int)block_sum_u32<kStThreads>(part, sh.redu) + (b_hi == kSBins ? (int)tail : 0);
   }
-  // ------------------------------- index-order draw over the kept set (FULL)
-  auto keptw = [&](float v, int gi) -> float {
-    return (v > -INFINITY && (v > cut.v || (v == cut.v && gi <= cut.idx))) ? W(v) : 0.0f;
-  };
-  if (!(U > 0.0)) {  // r == 0 stops at index 0 (sampler.py:66)
-    if (tid == 0) {
-      float x4[4];
-      st_load4_global<DT>(r, 0, x4);
-      write_row(a, row, 0, (float)((double)keptw(x4[0], 0) / total), 0);
-    }
+  if (__syncthreads_or(wrap) || nr > kSortCap) {  // crowded bracket: generic kernel
+    if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  const double target = U * total;
-  // crossing sub-chunk: thread t owns subs 2t, 2t+1 (nsubs <= 1024)
-  int qstar;
-  double before;
+  // pass 3 (L2): gather the bracket; per-unit mass above it into s_u
+  if (tid == 0) sh.ncand = 0;
+  __syncthreads();
+  bool gover = false;
+  ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int u) {
+    StW Wu = W;
+    Wu.set_m(sh.w.n.m[u]);
+    float above = 0.0f;
+    bool in[8];
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      in[e] = false;
+      if (x[e] > -INFINITY) {
+        float fr;
+        const int b = bin_of(x[e], fr);
+        if (b < b_lo) {
+          above += Wu(x[e]);
+        } else if (b <= b_hi) {
+          in[e] = true;
+          ++cnt;
+        }
+      }
+    }
+    above = warp_sum_f(above);
+    if (lane == 0) sh.w.n.s[u] = above;
+    const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
+    if (wt > 0) {
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int base = 0;
+      if (lane == 0) base = atomicAdd(&sh.ncand, wt);
+      base = __shfl_sync(0xFFFFFFFFu, base, 0);
+      int pos = base + incl - cnt;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (in[e]) {
+          if (pos < kSortCap) {
+            sh.w.n.x.g.key[pos] = fkey(x[e]);
+            sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
+          } else {
+            gover = true;
+          }
+          ++pos;
+        }
+      }
+    }
+  });
+  const int n = sh.ncand;  // st_pass ended with a barrier
+  if (__syncthreads_or(!ok || gover || n != nr)) {
+    if (tid == 0) a.status[row] = kRowPending;
+    return;
+  }
+  double as = 0.0;
+  for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
+  const double above_tot = block_sum<kStThreads>(as, sh.redd);
+  if (above_tot > 0.0 && above_tot >= pz) {  // the crossing lies above the bracket
+    if (tid == 0) a.status[row] = kRowPending;
+    return;
+  }
+  uint32_t *gk = sh.w.n.x.g.key;
+  int *gi = sh.w.n.x.g.idx;
+  if (n <= kRankCap) {
+    st_rank_sort(sh, gk, gi, n, false);
+  } else {
+    st_sort(gk, gi, n, false);
+  }
+  // the cut: first entry (value desc, index asc) whose running mass reaches
+  // P*total (miniserve/sampler.py:50-57)
+  const double need = pz - above_tot;
+  int rc;
   {
-    double s = 0.0;
-    for (int q = 2 * tid; q < 2 * tid + 2 && q < nsubs; ++q) s += sh.subsum[q];
+    const int per = (n + kStThreads - 1) / kStThreads;
+    const int p0 = tid * per, p1 = min(n, p0 + per);
+    double sw = 0.0;
+    for (int i = p0; i < p1; ++i) sw += unit_w(key_to_float(gk[i]), gi[i]);
     double ex, inc, tt;
-    block_scan<kStThreads, double>(s, ex, inc, tt, sh.redd);
+    block_scan<kStThreads, double>(sw, ex, inc, tt, sh.redd);
     int cand = 0x7FFFFFFF;
-    if (s > 0.0 && inc >= target) {
+    if (p0 < p1 && inc >= need) {
       double acc = ex;
-      for (int q = 2 * tid; q < 2 * tid + 2 && q < nsubs; ++q) {
-        if (sh.subsum[q] > 0.0 && acc + sh.subsum[q] >= target) {
-          cand = q;
+      for (int i = p0; i < p1; ++i) {
+        acc += unit_w(key_to_float(gk[i]), gi[i]);
+        if (acc >= need) {
+          cand = i;
           break;
         }
-        acc += sh.subsum[q];
       }
-      if (cand == 0x7FFFFFFF) cand = min(nsubs - 1, 2 * tid + 1);
+      if (cand == 0x7FFFFFFF) cand = p1 - 1;
     }
-    qstar = block_min_i<kStThreads>(cand, sh.redi);
-    if (qstar != 0x7FFFFFFF && tid == qstar / 2) {
-      double acc = ex;
-      for (int q = 2 * tid; q < qstar; ++q) acc += sh.subsum[q];
-      sh.bcast_d[1] = acc;
-    }
-    __syncthreads();
-    before = sh.bcast_d[1];
+    rc = block_min_i<kStThreads>(cand, sh.redi);
   }
-  if (qstar == 0x7FFFFFFF) {  // ran past the end (sampler.py:68)
-    if (tid == 0) {
-      float x4[4];
-      st_load4_global<DT>(r, V - 1, x4);
-      write_row(a, row, V - 1, (float)((double)keptw(x4[0], V - 1) / total), 0);
-    }
+  if (rc == 0x7FFFFFFF && b_hi < kSBins) {  // the crossing lies below the bracket
+    if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  // the crossing sub-chunk, read back from L2
-  const int gq = (qstar >> 1) * kChunk + (qstar & 1) * kSub + tid * 4;
-  float x[4];
-  st_load4_global<DT>(r, gq, x);
-  float wv[4];
-  double s = 0.0;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    wv[e] = keptw(x[e], gq + e);
-    s += (double)wv[e];
+  // rc == none with the tail bracketed: the running sum never reaches top_p,
+  // every token is kept
+  const float vc = rc == 0x7FFFFFFF ? -INFINITY : key_to_float(gk[rc]);
+  const int ic = rc == 0x7FFFFFFF ? 0x7FFFFFFF : gi[rc];
+  const int nkeep = rc == 0x7FFFFFFF ? n : rc + 1;
+  __syncthreads();
+  // kept bracket entries: keys become their fp32 unit weights, then index order
+  for (int i = tid; i < nkeep; i += kStThreads) {
+    StW Wu = W;
+    Wu.set_m(sh.w.n.m[gi[i] / kUnit]);
+    gk[i] = __float_as_uint(Wu(key_to_float(gk[i])));
   }
-  double ex, inc, tt;
-  block_scan<kStThreads, double>(s, ex, inc, tt, sh.redd);
-  int who = block_min_i<kStThreads>((s > 0.0 && before + inc >= target) ? tid : 0x7FFFFFFF, sh.redi);
-  if (who == 0x7FFFFFFF) who = -block_min_i<kStThreads>(s > 0.0 ? -tid : 1, sh.redi);
-  if (tid == who) {
-    double acc = before + ex;
-    int tok = -1, last = -1;
-    double wt = 0.0, wl = 0.0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (wv[e] <= 0.0f || tok >= 0) continue;
-      acc += (double)wv[e];
-      last = gq + e;
-      wl = wv[e];
-      if (acc >= target) {
-        tok = gq + e;
-        wt = wv[e];
-      }
-    }
-    if (tok < 0) {
-      tok = last;
-      wt = wl;
-    }
-    write_row(a, row, tok, (float)(wt / total), 0);
+  __syncthreads();
+  if (nkeep <= kRankCap) {
+    st_rank_sort(sh, gk, gi, nkeep, true);
+  } else {
+    st_sort(gk, gi, nkeep, true);
   }
+  // kept mass per unit: above the bracket + kept bracket entries of the unit
+  double tk = 0.0;
+  for (int u = tid; u < nu; u += kStThreads) {
+    int lo = 0, hi = nkeep;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (gi[mid] < u * kUnit) lo = mid + 1;
+      else hi = mid;
+    }
+    double e = 0.0;
+    for (int i = lo; i < nkeep && gi[i] < (u + 1) * kUnit; ++i) e += (double)__uint_as_float(gk[i]);
+    kd[u] = ((double)sh.w.n.s[u] + e) * (double)sh.w.n.f[u];
+    tk += kd[u];
+  }
+  const double tot_keep = block_sum<kStThreads>(tk, sh.redd);
+  st_draw_units<DT>(sh, a, r, row, nu, kd, tot_keep, U, [&](float v, int g) -> double {
+    if (!(v > -INFINITY) || !(v > vc || (v == vc && g <= ic))) return 0.0;
+    return unit_w(v, g);
+  });
 }
 }  // namespace ms
