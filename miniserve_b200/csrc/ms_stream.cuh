@@ -217,8 +217,34 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
 template <int DT>
 __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
   const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
-  st_get4<DT>(sh, r, c, s, j, x);
-  st_get4<DT>(sh, r, c, s, j + 128, x + 4);
+  if (!r.mask && tma_elems(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
+    if (DT == MS_DTYPE_F32) {
+      const float4 *p = reinterpret_cast<const float4 *>(sh.stage[s]);
+      const float4 f0 = p[j >> 2], f1 = p[(j + 128) >> 2];
+      x[0] = f0.x;
+      x[1] = f0.y;
+      x[2] = f0.z;
+      x[3] = f0.w;
+      x[4] = f1.x;
+      x[5] = f1.y;
+      x[6] = f1.z;
+      x[7] = f1.w;
+    } else {
+      const uint2 *p = reinterpret_cast<const uint2 *>(sh.stage[s]);
+      const uint2 h0 = p[j >> 2], h1 = p[(j + 128) >> 2];
+      x[0] = __uint_as_float(h0.x << 16);
+      x[1] = __uint_as_float(h0.x & 0xFFFF0000u);
+      x[2] = __uint_as_float(h0.y << 16);
+      x[3] = __uint_as_float(h0.y & 0xFFFF0000u);
+      x[4] = __uint_as_float(h1.x << 16);
+      x[5] = __uint_as_float(h1.x & 0xFFFF0000u);
+      x[6] = __uint_as_float(h1.y << 16);
+      x[7] = __uint_as_float(h1.y & 0xFFFF0000u);
+    }
+  } else {
+    st_get4<DT>(sh, r, c, s, j, x);
+    st_get4<DT>(sh, r, c, s, j + 128, x + 4);
+  }
   return c * kChunk + j;
 }
 // global index of x[e] given that of x[0]
@@ -771,43 +797,29 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         cm = fmaxf(cm, x[e]);
       }
       rmax = fmaxf(rmax, cm);
-      if ((c & 3) == 0) {
+      if (c < 3 || (c & 3) == 0) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
         if (bmin != 0u && key_to_float(bmin) > tau) {
           tau = key_to_float(bmin);
           strict = false;
         }
       }
-      // insert: one shared atomic per warp with candidates.  The buffer holds
-      // at most kCandCap - kChunk entries before each chunk, so it cannot
-      // overflow here.
-      int wt = 0;
-      if (__any_sync(0xFFFFFFFFu, strict ? cm > tau : cm >= tau)) {
-        int cnt = 0;
+      // insert: only lanes holding a candidate, one shared atomic per entry
+      // (u32 shared atomics run at full rate).  The buffer holds at most
+      // kCandCap - kChunk entries before each chunk, so it cannot overflow.
+      int cnt = 0;
+      if (strict ? cm > tau : cm >= tau) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) cnt += (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) ? 1 : 0;
-        wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-        if (wt > 0) {
-          int incl = cnt;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-            if (lane >= o) incl += y;
-          }
-          int base = 0;
-          if (lane == 0) base = atomicAdd(&sh.ncand, wt);  // positions only
-          base = __shfl_sync(0xFFFFFFFFu, base, 0);
-          int pos = base + incl - cnt;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            if (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) {
-              sh.w.c.key[pos] = fkey(x[e]);
-              sh.w.c.idx[pos] = st_gidx(g0, e);
-              ++pos;
-            }
+        for (int e = 0; e < 8; ++e) {
+          if (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) {
+            const int pos = atomicAdd(&sh.ncand, 1);  // positions only
+            sh.w.c.key[pos] = fkey(x[e]);
+            sh.w.c.idx[pos] = st_gidx(g0, e);
+            ++cnt;
           }
         }
       }
+      const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
       if (lane == 0) sh.wcnt[c & 1][tid >> 5] = wt;
       __syncthreads();  // stage s is free; the buffer is settled
       // exact count from the per-warp slots (slot c&1 is rewritten two chunks
