@@ -12,13 +12,16 @@
 //   full-softmax rows (no top-k, top_p >= 1)    one pass: per-unit maximum and
 //                                                weight sum; the draw re-reads
 //                                                one unit
-//   top-p-only rows                             pass 1 as above (L2 evict-last
-//                                                hint), pass 2 an integer x-grid
-//                                                histogram that brackets the
-//                                                top-p crossing, pass 3 gathers
-//                                                the bracket and the per-unit
-//                                                mass above it; exact cut and
-//                                                a one-unit draw
+//   top-p-only rows                             pass 1 (L2 evict-last hint):
+//                                                unit maxima and an integer
+//                                                x-grid histogram anchored at
+//                                                chunk 0's maximum, which
+//                                                brackets the top-p crossing;
+//                                                pass 2 (L2): every weight, the
+//                                                per-unit mass above the
+//                                                bracket and the bracket's
+//                                                elements; exact cut, one-unit
+//                                                draw
 //
 // Every weight of a softmax row is the same function of (logit, unit):
 // W_u(v) * f_u with W_u(v) = 2^((v - m_u) log2(e) / T) in fp32 (m_u the unit
@@ -48,8 +51,11 @@ constexpr int kRankCap = 1024;                  // largest set sorted by rank co
 constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
 constexpr int kMaxUnits = 1024;                 // per-unit summaries kept per row
 constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
-constexpr int kSBins = 2048;                    // x-grid bins (top-p)
-constexpr float kSXRange = 40.0f;               // grid depth, units of x = (max - logit) / T
+constexpr int kXBins = 2048;                    // x-grid bins per kSXRange (top-p)
+constexpr float kSXRange = 40.0f;               // units of x = logit / T
+constexpr int kUpBins = 512;                    // grid bins above the anchor
+constexpr int kSBins = kXBins + kUpBins;        // x-grid bins in all
+constexpr int kHighCap = 256;                   // values above the grid kept exactly
 constexpr float kQScale = 65536.0f;             // fixed-point scale of in-bin weights
 constexpr uint32_t kBinCntMax = 65535u;         // a bin with more entries may wrap its mass sum
 constexpr double kHistTol = 4e-5;               // bound on the histogram's running-mass error / total
@@ -66,6 +72,8 @@ struct StShared {
       float m[kMaxUnits];  // unit maxima
       float s[kMaxUnits];  // unit weight sums; after pass 3 the mass above the bracket
       float f[kMaxUnits];  // unit scales
+      uint32_t hkey[kHighCap];  // values above the x-grid
+      int hidx[kHighCap];
       union {
         struct {
           uint32_t cnt[kSBins];
@@ -80,6 +88,8 @@ struct StShared {
   } w;
   uint32_t wbound[kStWarps];
   int wcnt[2][kStWarps];  // per-warp insert counts of the last two chunks
+  int pick[kStWarps][4];  // row ordering: per-warp class counts
+  int ptot[4];
   uint32_t hist256[256];
   unsigned long long full[kStages];
   double redd[33];
@@ -90,6 +100,7 @@ struct StShared {
   float bcast_f[4];
   double bcast_d[4];
   int ncand;
+  int nhigh;
 };
 
 // ------------------------------------------------------------- the stream
@@ -660,11 +671,90 @@ __device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r,
 
 enum StMode : int { kStArgmax = 0, kStTopKMode = 1, kStFull = 2, kStNucleus = 3 };
 
+// Cost class of row r, longest first: top-p-only 0, top-k 1, full softmax 2,
+// argmax and rows finished without reading the logits 3.
+__device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
+  const double T = a.temperature[r];
+  const int k = a.top_k[r];
+  if (!(T > 0.0) || isinf(T) || k == 1) return 3;
+  if (k >= 2 && k < a.V) return 1;
+  return a.top_p[r] < 1.0 ? 0 : 2;
+}
+
+// The row CTA blockIdx.x takes: rows ordered by (cost class, index), so the
+// CTAs launched first take the longest rows and the batch ends with short
+// ones.  Every CTA computes the same order from the per-row parameters.
+__device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 4) sh.ptot[tid] = 0;
+  __syncthreads();
+  int n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+  for (int r = tid; r < B; r += kStThreads) {
+    const int c = st_row_class(a, r);
+    n0 += c == 0;
+    n1 += c == 1;
+    n2 += c == 2;
+    n3 += c == 3;
+  }
+  n0 = __reduce_add_sync(0xFFFFFFFFu, n0);
+  n1 = __reduce_add_sync(0xFFFFFFFFu, n1);
+  n2 = __reduce_add_sync(0xFFFFFFFFu, n2);
+  n3 = __reduce_add_sync(0xFFFFFFFFu, n3);
+  if (lane == 0) {
+    atomicAdd(&sh.ptot[0], n0);
+    atomicAdd(&sh.ptot[1], n1);
+    atomicAdd(&sh.ptot[2], n2);
+    atomicAdd(&sh.ptot[3], n3);
+  }
+  __syncthreads();
+  if (sh.ptot[0] == B || sh.ptot[1] == B || sh.ptot[2] == B || sh.ptot[3] == B) return blockIdx.x;
+  const int want = blockIdx.x;
+  int base[4];
+  base[0] = 0;
+  base[1] = sh.ptot[0];
+  base[2] = base[1] + sh.ptot[1];
+  base[3] = base[2] + sh.ptot[2];
+  int carry[4] = {0, 0, 0, 0};
+  int found = -1;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int r0 = 0; r0 < B; r0 += kStThreads) {
+    const int r = r0 + tid;
+    const int cls = r < B ? st_row_class(a, r) : -1;
+    int pre = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, cls == c);
+      if (lane == 0) sh.pick[warp][c] = __popc(m);
+      if (cls == c) pre = __popc(m & lt);
+    }
+    __syncthreads();
+    int tot[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int w = 0; w < kStWarps; ++w) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int v = sh.pick[w][c];
+        if (w < warp && c == cls) pre += v;
+        tot[c] += v;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if (c == cls && base[c] + carry[c] + pre == want) found = r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) carry[c] += tot[c];
+    __syncthreads();
+  }
+  if (found >= 0) sh.bcast_i[0] = found;
+  __syncthreads();
+  return sh.bcast_i[0];
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) {
   extern __shared__ __align__(128) unsigned char st_raw[];
   StShared &sh = *reinterpret_cast<StShared *>(st_raw);
-  const int row = blockIdx.x;
+  const int row = st_pick_row(sh, a, (int)gridDim.x);
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const double T = a.temperature[row];
@@ -911,12 +1001,137 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   }
 
   // ====================================================== softmax over all
-  const bool nucleus = mode == kStNucleus;
   StW W;
   W.set_t(T);
+  const double cl = 1.4426950408889634 / T;  // log2(e) / T
+  const int nu = r.nchunks * kStWarps;
+  double *kd = reinterpret_cast<double *>(sh.stage[1]);  // per-unit kept mass (stages idle after the passes)
+  auto unit_w = [&](float v, int gi) -> double {         // float64 weight of element gi, relative to the max
+    const int u = gi / kUnit;
+    StW Wu = W;
+    Wu.set_m(sh.w.n.m[u]);
+    return (double)Wu(v) * (double)sh.w.n.f[u];
+  };
+  // after pass 1: the row maximum, or a status written and false
+  auto finish_max = [&](float vmax_t, float vsum, float &vmax) -> bool {
+    const bool bad = isnan(vsum) || vsum == INFINITY;
+    if (__syncthreads_or(bad || !ok)) {
+      if (tid == 0) a.status[row] = kRowPending;
+      return false;
+    }
+    vmax = block_max_f<kStThreads>(vmax_t, sh.redf);
+    if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
+      if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
+      return false;
+    }
+    if (!(fabs((double)vmax) * cl < 1e37)) {  // max * log2(e)/T beyond fp32 range
+      if (tid == 0) a.status[row] = kRowPending;
+      return false;
+    }
+    return true;
+  };
+
+  if (mode == kStFull) {
+    // one pass (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
+    float vmax_t = -INFINITY, vsum = 0.0f;
+    ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int, int u) {
+      float cm = x[0];
+      vsum += x[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e) {
+        vsum += x[e];
+        cm = fmaxf(cm, x[e]);
+      }
+      vmax_t = fmaxf(vmax_t, cm);
+      const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
+      float mu = -INFINITY, su = 0.0f;
+      if (km != 0u) {  // warp-uniform
+        mu = key_to_float(km);
+        StW Wu = W;
+        Wu.set_m(mu);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (x[e] > -INFINITY) su += Wu(x[e]);
+        su = warp_sum_f(su);
+      }
+      if (lane == 0) {
+        sh.w.n.m[u] = mu;
+        sh.w.n.s[u] = su;
+      }
+    });
+    float vmax;
+    if (!finish_max(vmax_t, vsum, vmax)) return;
+    double zs = 0.0;
+    for (int u = tid; u < nu; u += kStThreads) {
+      const float mu = sh.w.n.m[u];
+      const float fu = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
+      sh.w.n.f[u] = fu;
+      kd[u] = (double)sh.w.n.s[u] * (double)fu;
+      zs += kd[u];
+    }
+    const double total = block_sum<kStThreads>(zs, sh.redd);  // ends with a barrier
+    st_draw_units<DT>(sh, a, r, row, nu, kd, total, U,
+                      [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
+    return;
+  }
+
+  // ============================================================ top-p only
+  // x-grid over t = (G - v) * xs + kUpBins: kXBins bins per kSXRange units of
+  // x = logit / T, anchored at G (the maximum of chunk 0, or the row maximum
+  // on the fallback pass).  Bin -1 holds values more than kUpBins bins above
+  // G (kept exactly in the high list), bin kSBins the tail.
+  const float xs = (float)((double)kXBins / ((double)kSXRange * T));
+  const float dx = kSXRange / (float)kXBins;
+  float G = -INFINITY;
+  auto bin_of = [&](float v, float &frac) -> int {  // monotone non-increasing in v
+    const float t = fmaf(G - v, xs, (float)kUpBins);
+    if (t < 0.0f) return -1;
+    if (!(t < (float)kSBins)) return kSBins;
+    const int b = (int)t;
+    frac = t - (float)b;
+    return b;
+  };
+  uint32_t ntail = 0;
+  auto hist_add = [&](float v, int gidx) {  // v > -inf
+    float fr = 0.0f;
+    const int b = bin_of(v, fr);
+    if (b < 0) {
+      const int pos = atomicAdd(&sh.nhigh, 1);
+      if (pos < kHighCap) {
+        sh.w.n.hkey[pos] = fkey(v);
+        sh.w.n.hidx[pos] = gidx;
+      }
+    } else if (b < kSBins) {
+      const float y = fr * dx;  // x below the bin's top, in [0, dx)
+      const float ey = fmaf(fmaf(fmaf(y, -1.0f / 6.0f, 0.5f), y, -1.0f), y, 1.0f);  // e^-y to y^4/24
+      atomicAdd(&sh.w.n.x.h.cnt[b], 1u);
+      atomicAdd(&sh.w.n.x.h.q[b], __float2uint_rn(ey * kQScale));
+    } else {
+      ++ntail;
+    }
+  };
+  auto hist_clear = [&]() {
+    for (int b = tid; b < kSBins; b += kStThreads) {
+      sh.w.n.x.h.cnt[b] = 0u;
+      sh.w.n.x.h.q[b] = 0u;
+    }
+    if (tid == 0) sh.nhigh = 0;
+    ntail = 0;
+    __syncthreads();
+  };
+
+  // pass 1 (HBM, kept in L2): unit maxima, histogram anchored at chunk 0's max
   float vmax_t = -INFINITY, vsum = 0.0f;
-  // pass 1 (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
-  ok = st_pass<DT>(sh, r, nucleus ? pol_keep : pol_stream, ph, [&](const float *x, int, int u) {
+  hist_clear();
+  if (tid == 0) {
+    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_keep);
+  }
+  for (int c = 0; c < r.nchunks; ++c) {
+    const int s = c % kStages;
+    if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
+    ph ^= 1u << s;
+    float x[8];
+    const int g0 = st_get8<DT>(sh, r, c, s, x);
     float cm = x[0];
     vsum += x[0];
 #pragma unroll
@@ -926,195 +1141,136 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
     vmax_t = fmaxf(vmax_t, cm);
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
-    float mu = -INFINITY, su = 0.0f;
-    if (km != 0u) {  // warp-uniform
-      mu = key_to_float(km);
-      StW Wu = W;
-      Wu.set_m(mu);
+    if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
+    if (c == 0) G = block_max_f<kStThreads>(cm, sh.redf);
+    if (G > -INFINITY) {  // block-uniform
 #pragma unroll
       for (int e = 0; e < 8; ++e)
-        if (x[e] > -INFINITY) su += Wu(x[e]);
-      su = warp_sum_f(su);
+        if (x[e] > -INFINITY) hist_add(x[e], st_gidx(g0, e));
     }
-    if (lane == 0) {
-      sh.w.n.m[u] = mu;
-      sh.w.n.s[u] = su;
+    __syncthreads();  // every thread is done with stage s
+    if (tid == 0 && c + kStages < r.nchunks) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      st_issue(sh, r, c + kStages, s, pol_keep);
     }
-  });
-  {
-    const bool bad = isnan(vsum) || vsum == INFINITY;
-    if (__syncthreads_or(bad || !ok)) {
+  }
+  ok = __syncthreads_and(ok) != 0;
+  float vmax;
+  if (!finish_max(vmax_t, vsum, vmax)) return;
+  for (int u = tid; u < nu; u += kStThreads) {
+    const float mu = sh.w.n.m[u];
+    sh.w.n.f[u] = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
+  }
+  if (!(G > -INFINITY) || sh.nhigh > kHighCap) {
+    // chunk 0 held no finite logit, or many values lie far above its max:
+    // histogram pass (L2) anchored at the row maximum, nothing above it
+    __syncthreads();
+    G = vmax;
+    hist_clear();
+    ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (x[e] > -INFINITY) hist_add(x[e], st_gidx(g0, e));
+    });
+    if (!ok) {
       if (tid == 0) a.status[row] = kRowPending;
       return;
     }
   }
-  const float vmax = block_max_f<kStThreads>(vmax_t, sh.redf);
-  if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
-    if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
-    return;
-  }
-  const double cl = 1.4426950408889634 / T;
-  if (!(fabs((double)vmax) * cl < 1e37)) {  // max * log2(e)/T beyond fp32 range
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
-  }
-  const int nu = r.nchunks * kStWarps;
-  // unit scales f_u and the softmax total
-  double zs = 0.0;
-  for (int u = tid; u < nu; u += kStThreads) {
-    const float mu = sh.w.n.m[u];
-    const float fu = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
-    sh.w.n.f[u] = fu;
-    zs += (double)sh.w.n.s[u] * (double)fu;
-  }
-  const double total = block_sum<kStThreads>(zs, sh.redd);  // ends with a barrier
-  double *kd = reinterpret_cast<double *>(sh.stage[1]);      // per-unit kept mass (stages idle)
-  auto unit_w = [&](float v, int gi) -> double {             // the weight of element gi
-    const int u = gi / kUnit;
-    StW Wu = W;
-    Wu.set_m(sh.w.n.m[u]);
-    return (double)Wu(v) * (double)sh.w.n.f[u];
-  };
-
-  if (!nucleus) {  // full softmax: every valid token kept
-    for (int u = tid; u < nu; u += kStThreads) kd[u] = (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
-    __syncthreads();
-    st_draw_units<DT>(sh, a, r, row, nu, kd, total, U,
-                      [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
-    return;
-  }
-
-  // pass 2 (L2): x-grid histogram, x = (max - v) / T, kSBins bins over
-  // [0, kSXRange): entry count and fixed-point mass relative to the bin's top
-  for (int b = tid; b < kSBins; b += kStThreads) {
-    sh.w.n.x.h.cnt[b] = 0u;
-    sh.w.n.x.h.q[b] = 0u;
-  }
   __syncthreads();
-  const float xs = (float)((double)kSBins / ((double)kSXRange * T));  // bins per logit unit
-  const float dx = kSXRange / (float)kSBins;                          // x per bin
-  auto bin_of = [&](float v, float &frac) -> int {  // monotone non-increasing in v
-    const float t = (vmax - v) * xs;
-    if (!(t < (float)kSBins)) return kSBins;  // the tail
-    const int b = (int)t;
-    frac = t - (float)b;
-    return b;
-  };
-  uint32_t ntail = 0;
-  ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int, int) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (x[e] > -INFINITY) {
-        float fr = 0.0f;
-        const int b = bin_of(x[e], fr);
-        if (b < kSBins) {
-          const float y = fr * dx;  // x below the bin's top, in [0, dx)
-          const float ey = fmaf(fmaf(fmaf(y, -1.0f / 6.0f, 0.5f), y, -1.0f), y, 1.0f);  // e^-y to y^4/24
-          atomicAdd(&sh.w.n.x.h.cnt[b], 1u);
-          atomicAdd(&sh.w.n.x.h.q[b], __float2uint_rn(ey * kQScale));
-        } else {
-          ++ntail;
-        }
-      }
-    }
-  });
-  if (!ok) {
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
-  }
-  // the bracket [b_lo, b_hi]: bins where the running mass crosses
-  // P*total -/+ kHistTol*total (bin kSBins = the tail)
-  const double pz = P * total;
+  // the high list: exact weights
+  const int nh = min(sh.nhigh, kHighCap);
+  double hs = 0.0;
+  for (int i = tid; i < nh; i += kStThreads) hs += unit_w(key_to_float(sh.w.n.hkey[i]), sh.w.n.hidx[i]);
+  const double H = block_sum<kStThreads>(hs, sh.redd);
+  // the bracket [b_lo, b_hi] (bins -1 .. kSBins): where the histogram's running
+  // mass crosses P*total -/+ kHistTol*total
   int b_lo, b_hi, nr;
   bool wrap = false;
   {
-    double m4[4];
-    uint32_t c4[4];
+    constexpr int kPer = kSBins / kStThreads;
+    const double rG = exp2(((double)G - (double)vmax) * cl);  // anchor weight / max weight
+    double mb[kPer];
+    uint32_t cb[kPer];
     double s = 0.0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int b = tid * 4 + q;
-      c4[q] = sh.w.n.x.h.cnt[b];
-      m4[q] = (double)sh.w.n.x.h.q[b] * (1.0 / (double)kQScale) * exp(-(double)b * (double)dx);
-      s += m4[q];
+    for (int q = 0; q < kPer; ++q) {
+      const int b = tid * kPer + q;
+      cb[q] = sh.w.n.x.h.cnt[b];
+      mb[q] = (double)sh.w.n.x.h.q[b] * (rG / (double)kQScale) * exp(-(double)(b - kUpBins) * (double)dx);
+      s += mb[q];
     }
-    double ex, inc, tt;
-    block_scan<kStThreads, double>(s, ex, inc, tt, sh.redd);
-    const double lo_t = pz - kHistTol * total, hi_t = pz + kHistTol * total;
+    double ex, inc, tot;
+    block_scan<kStThreads, double>(s, ex, inc, tot, sh.redd);
+    const double zh = H + tot;  // the tail's mass (< e^-30 of the anchor's weight each) left out
+    const double lo_t = P * zh - kHistTol * zh, hi_t = P * zh + kHistTol * zh;
     int clo = 0x7FFFFFFF, chi = 0x7FFFFFFF;
-    double acc = ex;
+    double acc = H + ex;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      acc += m4[q];
-      if (clo == 0x7FFFFFFF && acc >= lo_t) clo = tid * 4 + q;
-      if (chi == 0x7FFFFFFF && acc >= hi_t) chi = tid * 4 + q;
+    for (int q = 0; q < kPer; ++q) {
+      acc += mb[q];
+      if (clo == 0x7FFFFFFF && acc >= lo_t) clo = tid * kPer + q;
+      if (chi == 0x7FFFFFFF && acc >= hi_t) chi = tid * kPer + q;
     }
-    b_lo = block_min_i<kStThreads>(clo, sh.redi);
-    b_hi = block_min_i<kStThreads>(chi, sh.redi);
+    b_lo = H >= lo_t ? -1 : block_min_i<kStThreads>(clo, sh.redi);
+    b_hi = H >= hi_t ? -1 : block_min_i<kStThreads>(chi, sh.redi);
     if (b_lo == 0x7FFFFFFF) b_lo = kSBins;
     if (b_hi == 0x7FFFFFFF) b_hi = kSBins;
     uint32_t part = 0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int b = tid * 4 + q;
-      if (b >= b_lo && b <= b_hi) part += c4[q];
-      if (b <= b_hi && c4[q] > kBinCntMax) wrap = true;
+    for (int q = 0; q < kPer; ++q) {
+      const int b = tid * kPer + q;
+      if (b >= b_lo && b <= b_hi) part += cb[q];
+      if (b <= b_hi && cb[q] > kBinCntMax) wrap = true;
     }
     const uint32_t tail = block_sum_u32<kStThreads>(ntail, sh.redu);
-    nr = (int)block_sum_u32<kStThreads>(part, sh.redu) + (b_hi == kSBins ? (int)tail : 0);
+    nr = (int)block_sum_u32<kStThreads>(part, sh.redu) + (b_hi == kSBins ? (int)tail : 0) + (b_lo < 0 ? nh : 0);
   }
   if (__syncthreads_or(wrap) || nr > kSortCap) {  // crowded bracket: generic kernel
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  // pass 3 (L2): gather the bracket; per-unit mass above it into s_u
+  // pass 3 (L2): every weight once: per-unit mass above the bracket (into
+  // s_u), the exact total, and the bracket's elements
   if (tid == 0) sh.ncand = 0;
   __syncthreads();
   bool gover = false;
+  double zacc = 0.0;
   ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int u) {
     StW Wu = W;
     Wu.set_m(sh.w.n.m[u]);
-    float above = 0.0f;
+    float above = 0.0f, all = 0.0f;
     bool in[8];
-    int cnt = 0;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       in[e] = false;
       if (x[e] > -INFINITY) {
+        const float w = Wu(x[e]);
+        all += w;
         float fr;
         const int b = bin_of(x[e], fr);
         if (b < b_lo) {
-          above += Wu(x[e]);
+          above += w;
         } else if (b <= b_hi) {
           in[e] = true;
-          ++cnt;
         }
       }
     }
     above = warp_sum_f(above);
-    if (lane == 0) sh.w.n.s[u] = above;
-    const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-    if (wt > 0) {
-      int incl = cnt;
+    all = warp_sum_f(all);
+    if (lane == 0) {
+      sh.w.n.s[u] = above;
+      zacc += (double)all * (double)sh.w.n.f[u];
+    }
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      int base = 0;
-      if (lane == 0) base = atomicAdd(&sh.ncand, wt);
-      base = __shfl_sync(0xFFFFFFFFu, base, 0);
-      int pos = base + incl - cnt;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (in[e]) {
-          if (pos < kSortCap) {
-            sh.w.n.x.g.key[pos] = fkey(x[e]);
-            sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
-          } else {
-            gover = true;
-          }
-          ++pos;
+    for (int e = 0; e < 8; ++e) {
+      if (in[e]) {
+        const int pos = atomicAdd(&sh.ncand, 1);
+        if (pos < kSortCap) {
+          sh.w.n.x.g.key[pos] = fkey(x[e]);
+          sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
+        } else {
+          gover = true;
         }
       }
     }
@@ -1124,6 +1280,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
+  const double total = block_sum<kStThreads>(zacc, sh.redd);
+  const double pz = P * total;
   double as = 0.0;
   for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
   const double above_tot = block_sum<kStThreads>(as, sh.redd);
@@ -1172,31 +1330,19 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const float vc = rc == 0x7FFFFFFF ? -INFINITY : key_to_float(gk[rc]);
   const int ic = rc == 0x7FFFFFFF ? 0x7FFFFFFF : gi[rc];
   const int nkeep = rc == 0x7FFFFFFF ? n : rc + 1;
+  // kept mass per unit: above the bracket (s_u) plus the unit's kept bracket
+  // entries, those summed as 2^-50 fixed point (exact and order-free)
+  unsigned long long *ex64 = reinterpret_cast<unsigned long long *>(sh.stage[2]);
+  for (int u = tid; u < nu; u += kStThreads) ex64[u] = 0ull;
   __syncthreads();
-  // kept bracket entries: keys become their fp32 unit weights, then index order
   for (int i = tid; i < nkeep; i += kStThreads) {
-    StW Wu = W;
-    Wu.set_m(sh.w.n.m[gi[i] / kUnit]);
-    gk[i] = __float_as_uint(Wu(key_to_float(gk[i])));
+    const double w = unit_w(key_to_float(gk[i]), gi[i]);  // <= 1
+    atomicAdd(&ex64[gi[i] / kUnit], (unsigned long long)(w * 0x1p50));
   }
   __syncthreads();
-  if (nkeep <= kRankCap) {
-    st_rank_sort(sh, gk, gi, nkeep, true);
-  } else {
-    st_sort(gk, gi, nkeep, true);
-  }
-  // kept mass per unit: above the bracket + kept bracket entries of the unit
   double tk = 0.0;
   for (int u = tid; u < nu; u += kStThreads) {
-    int lo = 0, hi = nkeep;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (gi[mid] < u * kUnit) lo = mid + 1;
-      else hi = mid;
-    }
-    double e = 0.0;
-    for (int i = lo; i < nkeep && gi[i] < (u + 1) * kUnit; ++i) e += (double)__uint_as_float(gk[i]);
-    kd[u] = ((double)sh.w.n.s[u] + e) * (double)sh.w.n.f[u];
+    kd[u] = (double)sh.w.n.s[u] * (double)sh.w.n.f[u] + (double)ex64[u] * 0x1p-50;
     tk += kd[u];
   }
   const double tot_keep = block_sum<kStThreads>(tk, sh.redd);
