@@ -56,8 +56,8 @@ constexpr float kSXRange = 40.0f;               // units of x = logit / T
 constexpr int kUpBins = 512;                    // grid bins above the anchor
 constexpr int kSBins = kXBins + kUpBins;        // x-grid bins in all
 constexpr int kHighCap = 256;                   // values above the grid kept exactly
+constexpr int kQSlots = (kSBins + 2 + kStThreads - 1) / kStThreads * kStThreads;  // histogram indices 0..kSBins+1
 constexpr float kQScale = 65536.0f;             // fixed-point scale of in-bin weights
-constexpr uint32_t kBinCntMax = 65535u;         // a bin with more entries may wrap its mass sum
 constexpr double kHistTol = 4e-5;               // bound on the histogram's running-mass error / total
 constexpr double kMinTemperature = 1e-30;       // fp32 weights need a finite log2(e)/T
 
@@ -75,10 +75,7 @@ struct StShared {
       uint32_t hkey[kHighCap];  // values above the x-grid
       int hidx[kHighCap];
       union {
-        struct {
-          uint32_t cnt[kSBins];
-          uint32_t q[kSBins];
-        } h;  // x-grid histogram
+        uint32_t hq[kQSlots];  // x-grid histogram (fixed-point mass)
         struct {
           uint32_t key[kSortCap];
           int idx[kSortCap];
@@ -1076,47 +1073,45 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   }
 
   // ============================================================ top-p only
-  // x-grid over t = (G - v) * xs + kUpBins: kXBins bins per kSXRange units of
-  // x = logit / T, anchored at G (the maximum of chunk 0, or the row maximum
-  // on the fallback pass).  Bin -1 holds values more than kUpBins bins above
-  // G (kept exactly in the high list), bin kSBins the tail.
+  // x-grid coordinate t = (G - v) * xs + kUpBins + 1: kXBins bins per
+  // kSXRange units of x = logit / T, anchored at G (the maximum of chunk 0, or
+  // the row maximum on the fallback pass).  t < 1: more than kUpBins bins
+  // above G, kept exactly in the high list.  Index floor(t) in 1..kSBins: a
+  // grid bin; kSBins + 1: the tail (and masked tokens).  hq[i] holds the
+  // fixed-point sum of kQScale * e^-((t - i) * dx) over the elements of index
+  // i, so index i carries mass e^-((i - 1 - kUpBins) * dx) * hq[i] / kQScale
+  // relative to G.  The histogram only places the bracket: pass 2 checks the
+  // crossing exactly, and a bracket that misses it leaves the row pending.
   const float xs = (float)((double)kXBins / ((double)kSXRange * T));
   const float dx = kSXRange / (float)kXBins;
+  const float t_off = (float)(kUpBins + 1);
+  const float t_max = (float)kSBins + 1.25f;
+  // round(kQScale * e^-(fr*dx)) + 2^23 as a float (cubic, error (fr*dx)^4/24)
+  const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx,
+              q3 = -kQScale * dx * dx * dx * (1.0f / 6.0f);
+  uint32_t *hq = sh.w.n.x.hq;
   float G = -INFINITY;
-  auto bin_of = [&](float v, float &frac) -> int {  // monotone non-increasing in v
-    const float t = fmaf(G - v, xs, (float)kUpBins);
-    if (t < 0.0f) return -1;
-    if (!(t < (float)kSBins)) return kSBins;
-    const int b = (int)t;
-    frac = t - (float)b;
-    return b;
-  };
-  uint32_t ntail = 0;
-  auto hist_add = [&](float v, int gidx) {  // v > -inf
-    float fr = 0.0f;
-    const int b = bin_of(v, fr);
-    if (b < 0) {
+  auto hist_add = [&](float v, int gidx) {
+    float t = fmaf(G - v, xs, t_off);
+    if (t < 1.0f) {  // above the grid: kept exactly (rare)
       const int pos = atomicAdd(&sh.nhigh, 1);
       if (pos < kHighCap) {
         sh.w.n.hkey[pos] = fkey(v);
         sh.w.n.hidx[pos] = gidx;
       }
-    } else if (b < kSBins) {
-      const float y = fr * dx;  // x below the bin's top, in [0, dx)
-      const float ey = fmaf(fmaf(fmaf(y, -1.0f / 6.0f, 0.5f), y, -1.0f), y, 1.0f);  // e^-y to y^4/24
-      atomicAdd(&sh.w.n.x.h.cnt[b], 1u);
-      atomicAdd(&sh.w.n.x.h.q[b], __float2uint_rn(ey * kQScale));
-    } else {
-      ++ntail;
+      return;
     }
+    t = fminf(t, t_max);  // the tail, -inf and NaN land on index kSBins + 1
+    // 2^23 + floor(t): the add rounds toward -inf, so index = floor(t) exactly,
+    // the same index the bracket tests of pass 2 (t < bound) imply
+    const float tb = __fadd_rd(t, 8388608.0f);
+    const float fr = t - (tb - 8388608.0f);
+    const float qf = fmaf(fmaf(fmaf(fr, q3, q2), fr, q1), fr, q0);
+    atomicAdd(&hq[__float_as_int(tb) - 0x4B000000], (uint32_t)(__float_as_int(qf) - 0x4B000000));
   };
   auto hist_clear = [&]() {
-    for (int b = tid; b < kSBins; b += kStThreads) {
-      sh.w.n.x.h.cnt[b] = 0u;
-      sh.w.n.x.h.q[b] = 0u;
-    }
+    for (int i = tid; i < kQSlots; i += kStThreads) hq[i] = 0u;
     if (tid == 0) sh.nhigh = 0;
-    ntail = 0;
     __syncthreads();
   };
 
@@ -1145,8 +1140,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (c == 0) G = block_max_f<kStThreads>(cm, sh.redf);
     if (G > -INFINITY) {  // block-uniform
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (x[e] > -INFINITY) hist_add(x[e], st_gidx(g0, e));
+      for (int e = 0; e < 8; ++e) hist_add(x[e], st_gidx(g0, e));
     }
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && c + kStages < r.nchunks) {
@@ -1169,8 +1163,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     hist_clear();
     ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (x[e] > -INFINITY) hist_add(x[e], st_gidx(g0, e));
+      for (int e = 0; e < 8; ++e) hist_add(x[e], st_gidx(g0, e));
     });
     if (!ok) {
       if (tid == 0) a.status[row] = kRowPending;
@@ -1183,26 +1176,25 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   double hs = 0.0;
   for (int i = tid; i < nh; i += kStThreads) hs += unit_w(key_to_float(sh.w.n.hkey[i]), sh.w.n.hidx[i]);
   const double H = block_sum<kStThreads>(hs, sh.redd);
-  // the bracket [b_lo, b_hi] (bins -1 .. kSBins): where the histogram's running
-  // mass crosses P*total -/+ kHistTol*total
-  int b_lo, b_hi, nr;
-  bool wrap = false;
+  // the bracket [i_lo, i_hi] of indices (-1 = the high list, kSBins + 1 =
+  // the tail): where the estimated running mass crosses P*total -/+
+  // kHistTol*total.
+  int i_lo, i_hi;
   {
-    constexpr int kPer = kSBins / kStThreads;
+    constexpr int kPer = kQSlots / kStThreads;
     const double rG = exp2(((double)G - (double)vmax) * cl);  // anchor weight / max weight
     double mb[kPer];
-    uint32_t cb[kPer];
     double s = 0.0;
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int b = tid * kPer + q;
-      cb[q] = sh.w.n.x.h.cnt[b];
-      mb[q] = (double)sh.w.n.x.h.q[b] * (rG / (double)kQScale) * exp(-(double)(b - kUpBins) * (double)dx);
+      const int i = tid * kPer + q;
+      mb[q] = i <= kSBins ? (double)hq[i] * (rG / (double)kQScale) * exp(-(double)(i - 1 - kUpBins) * (double)dx)
+                          : 0.0;  // the tail's mass (each < e^-30 of the anchor's weight) left out
       s += mb[q];
     }
     double ex, inc, tot;
     block_scan<kStThreads, double>(s, ex, inc, tot, sh.redd);
-    const double zh = H + tot;  // the tail's mass (< e^-30 of the anchor's weight each) left out
+    const double zh = H + tot;
     const double lo_t = P * zh - kHistTol * zh, hi_t = P * zh + kHistTol * zh;
     int clo = 0x7FFFFFFF, chi = 0x7FFFFFFF;
     double acc = H + ex;
@@ -1212,25 +1204,15 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       if (clo == 0x7FFFFFFF && acc >= lo_t) clo = tid * kPer + q;
       if (chi == 0x7FFFFFFF && acc >= hi_t) chi = tid * kPer + q;
     }
-    b_lo = H >= lo_t ? -1 : block_min_i<kStThreads>(clo, sh.redi);
-    b_hi = H >= hi_t ? -1 : block_min_i<kStThreads>(chi, sh.redi);
-    if (b_lo == 0x7FFFFFFF) b_lo = kSBins;
-    if (b_hi == 0x7FFFFFFF) b_hi = kSBins;
-    uint32_t part = 0;
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      const int b = tid * kPer + q;
-      if (b >= b_lo && b <= b_hi) part += cb[q];
-      if (b <= b_hi && cb[q] > kBinCntMax) wrap = true;
-    }
-    const uint32_t tail = block_sum_u32<kStThreads>(ntail, sh.redu);
-    nr = (int)block_sum_u32<kStThreads>(part, sh.redu) + (b_hi == kSBins ? (int)tail : 0) + (b_lo < 0 ? nh : 0);
+    i_lo = H >= lo_t ? -1 : block_min_i<kStThreads>(clo, sh.redi);
+    i_hi = H >= hi_t ? -1 : block_min_i<kStThreads>(chi, sh.redi);
+    if (i_lo == 0x7FFFFFFF || i_lo > kSBins) i_lo = kSBins + 1;
+    if (i_hi == 0x7FFFFFFF || i_hi > kSBins) i_hi = kSBins + 1;
   }
-  if (__syncthreads_or(wrap) || nr > kSortCap) {  // crowded bracket: generic kernel
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
-  }
-  // pass 3 (L2): every weight once: per-unit mass above the bracket (into
+  // bracket bounds on t: above <=> t < lo_f; in <=> lo_f <= t < hi_f
+  const float lo_f = i_lo < 0 ? -INFINITY : (float)i_lo;
+  const float hi_f = i_hi < 0 ? 1.0f : (i_hi > kSBins ? INFINITY : (float)(i_hi + 1));
+  // pass 2 (L2): every weight once: per-unit mass above the bracket (into
   // s_u), the exact total, and the bracket's elements
   if (tid == 0) sh.ncand = 0;
   __syncthreads();
@@ -1240,21 +1222,16 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     StW Wu = W;
     Wu.set_m(sh.w.n.m[u]);
     float above = 0.0f, all = 0.0f;
-    bool in[8];
+    uint32_t inm = 0u;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      in[e] = false;
-      if (x[e] > -INFINITY) {
-        const float w = Wu(x[e]);
-        all += w;
-        float fr;
-        const int b = bin_of(x[e], fr);
-        if (b < b_lo) {
-          above += w;
-        } else if (b <= b_hi) {
-          in[e] = true;
-        }
-      }
+      const bool valid = x[e] > -INFINITY;
+      const float w = valid ? Wu(x[e]) : 0.0f;
+      all += w;
+      const float t = fmaf(G - x[e], xs, t_off);
+      const bool ab = t < lo_f;
+      above += ab ? w : 0.0f;
+      if (valid && !ab && t < hi_f) inm |= 1u << e;
     }
     above = warp_sum_f(above);
     all = warp_sum_f(all);
@@ -1262,21 +1239,23 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       sh.w.n.s[u] = above;
       zacc += (double)all * (double)sh.w.n.f[u];
     }
+    if (inm != 0u) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (in[e]) {
-        const int pos = atomicAdd(&sh.ncand, 1);
-        if (pos < kSortCap) {
-          sh.w.n.x.g.key[pos] = fkey(x[e]);
-          sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
-        } else {
-          gover = true;
+      for (int e = 0; e < 8; ++e) {
+        if ((inm >> e) & 1u) {
+          const int pos = atomicAdd(&sh.ncand, 1);
+          if (pos < kSortCap) {
+            sh.w.n.x.g.key[pos] = fkey(x[e]);
+            sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
+          } else {
+            gover = true;
+          }
         }
       }
     }
   });
   const int n = sh.ncand;  // st_pass ended with a barrier
-  if (__syncthreads_or(!ok || gover || n != nr)) {
+  if (__syncthreads_or(!ok || gover)) {  // a crowded bracket: generic kernel
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
@@ -1321,7 +1300,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
     rc = block_min_i<kStThreads>(cand, sh.redi);
   }
-  if (rc == 0x7FFFFFFF && b_hi < kSBins) {  // the crossing lies below the bracket
+  if (rc == 0x7FFFFFFF && i_hi <= kSBins) {  // the crossing lies below the bracket
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
