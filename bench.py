@@ -41,6 +41,20 @@ WORKLOAD = "config3: 512x151936 fp32, heterogeneous per-row top_k/top_p/temperat
 FALLBACK_HBM_GBS = 6650.0
 
 
+def profiled_traffic():
+    """DRAM bytes per launch of the streaming kernel on this workload, from the
+    committed ncu summary (dram__bytes_read.sum + dram__bytes_write.sum)."""
+    path = os.path.join(ROOT, "profiles", "stream_kernel_config3_full.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def hbm_peak():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -257,7 +271,7 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = hbm_peak()
     cpu = None
     if pool is not None:
-        sample_rows = list(range(min(B, max(2 * cores, 16))))
+        sample_rows = list(range(B))  # the whole batch: ~0.5 core-s per row
         rate, dt = cpu_reference_rate(batch, sample_rows, pool, cores)
         cpu = {"value": round(rate, 3), "unit": "rows/s", "cores": cores, "kind": "port",
                "sample": f"{len(sample_rows)} rows of the same batch, reference float64 Python "
@@ -272,7 +286,8 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"dp{world} (independent rows per rank)",
                    "l2": "inputs (311 MB) larger than L2 (126 MB); no flush"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
+                     "traffic_unit": "DRAM bytes per launch (ncu, profiles/stream_kernel_config3_full.md)",
                      "peak_source": peak_kind + " (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                      "alg_bytes_per_launch": alg_bytes, "avg_launch_us": round(avg_launch_ms * 1e3, 2)},
         "e2e": {"value": round(e2e_value, 1), "unit": "rows/s", "h2d_bytes_per_step": h2d,
@@ -284,7 +299,7 @@ def run_ours(args, rank, world, local_rank):
 
 
 def launches_per_call():
-    """ms_sample launches the cluster kernel and the pending-row pass."""
+    """ms_sample launches the streaming kernel and the pending-row pass."""
     return 2
 
 
