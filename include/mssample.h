@@ -82,7 +82,7 @@ int ms_sample(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld,
 /*
  * Same contract and results as ms_sample, always through the multi-pass
  * kernel that re-reads each row from global memory (one CTA per row) instead
- * of the cluster-resident single-read path.  It has no vocabulary-size limit
+ * of the streaming single-read path.  It has no vocabulary-size limit
  * and serves as the cross-check of the fast path.  Same reference interface
  * as ms_sample (miniserve/sampler.py:23-68).
  */

@@ -1,8 +1,8 @@
 // Generic sampling kernel: one 1024-thread CTA per row, multi-pass over the
 // row in global memory.  Exact for every input the C ABI accepts (any V, any
 // top_k / top_p, ties, masks) and simple enough to trust: it only uses
-// CTA-level barriers.  The cluster kernel hands it the rows it does not
-// resolve on chip.
+// CTA-level barriers.  The streaming kernel hands it the rows it does not
+// finish (status kRowPending).
 //
 // Semantics follow miniserve/sampler.py:23-68 (see ms_sample.cu for the map).
 #pragma once
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kGenThreads, 1)
   gen_row<DT>(a, r, sh);
 }
 
-// Finishes the rows the cluster kernel left with status kRowPending; a
+// Finishes the rows the streaming kernel left with status kRowPending; a
 // grid-stride loop, so the grid can stay one CTA per SM whatever B is.
 template <int DT>
 __global__ void __launch_bounds__(kGenThreads, 1) ms_generic_pending_kernel(SampleArgs a, int B) {

@@ -55,10 +55,10 @@ def _param(x, B: int, dtype, device):
 class Sampler:
     """Convert logit scores to token ids on the GPU (miniserve/sampler.py:20-68).
 
-    ``path="fast"`` (default) uses the cluster-resident kernel that reads each
-    row from HBM once; ``path="generic"`` forces the multi-pass kernel (no
-    vocabulary limit; the cross-check of the fast path).  Both give the same
-    results.
+    ``path="fast"`` (default) uses the streaming kernel (one CTA per row, the
+    row read from HBM once, a second L2 pass for top-p-only rows);
+    ``path="generic"`` forces the multi-pass kernel (no vocabulary limit; the
+    cross-check of the fast path).  Both give the same results.
     """
 
     def __init__(self, path: str = "fast") -> None:
