@@ -590,16 +590,58 @@ __device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int 
   st_draw_sorted(sh, a, row, didx, nkeep, tot_keep, U, [&](int i) { return dw[i]; });
 }
 
+// Two fp32 values in one 64-bit register.  sm_100 executes add/sub/fma
+// .f32x2 as one instruction for both; each half is rounded exactly as the
+// scalar instruction would round it, so packed and scalar code give the same
+// bits.
+typedef unsigned long long f2_t;
+__device__ __forceinline__ f2_t f2_pack(float lo, float hi) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(f2_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_sub(f2_t a, f2_t b) {
+  f2_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_add_rm(f2_t a, f2_t b) {  // rounded toward -inf
+  f2_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float st_ex2(float z) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(z));
+  return r;
+}
+
 // fp32 weight 2^((v - M) * log2(e) / T) from two FMAs and one ex2.approx:
 // c = c_hi + c_lo and M*c = mc_hi + mc_lo carry the constants to ~2^-48, so
 // the only roundings are the final sum (|z| * 2^-24) and ex2 (~2^-22).
-// set_t once per row, set_m per reference maximum M.
+// c_hi is c rounded toward zero and c_lo > 0, so v = -inf gives z = -inf and
+// weight 0 with no test.  set_t once per row, set_m per finite reference
+// maximum M.
 struct StW {
   float c_hi, c_lo, mc_hi, mc_lo;
   __device__ __forceinline__ void set_t(double T) {
     const double c = 1.4426950408889634 / T;  // log2(e) / T
-    c_hi = (float)c;
+    c_hi = __double2float_rz(c);
     c_lo = (float)(c - (double)c_hi);
+    if (!(c_lo > 0.0f)) c_lo = 1.17549435e-38f;  // c exact in fp32: a negligible positive tail
   }
   __device__ __forceinline__ void set_m(float M) {
     const double mc = (double)M * (double)c_hi;  // exact: 24 x 24 bits
@@ -607,10 +649,20 @@ struct StW {
     mc_lo = (float)(mc - (double)mc_hi) + (float)((double)M * (double)c_lo);
   }
   __device__ __forceinline__ float operator()(float v) const {
-    const float z = fmaf(v, c_hi, -mc_hi) + fmaf(v, c_lo, -mc_lo);
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(z));
-    return r;
+    return st_ex2(fmaf(v, c_hi, -mc_hi) + fmaf(v, c_lo, -mc_lo));
+  }
+};
+
+// The same weight for two values at once (packed arithmetic, same bits).
+struct StW2 {
+  f2_t ch, cl, nmh, nml;
+  __device__ __forceinline__ explicit StW2(const StW &w)
+      : ch(f2_pack(w.c_hi, w.c_hi)), cl(f2_pack(w.c_lo, w.c_lo)), nmh(f2_pack(-w.mc_hi, -w.mc_hi)),
+        nml(f2_pack(-w.mc_lo, -w.mc_lo)) {}
+  __device__ __forceinline__ f2_t operator()(f2_t v) const {
+    float z0, z1;
+    f2_unpack(f2_add(f2_fma(v, ch, nmh), f2_fma(v, cl, nml)), z0, z1);
+    return f2_pack(st_ex2(z0), st_ex2(z1));
   }
 };
 
@@ -865,7 +917,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     float rmax = -INFINITY, vsum = 0.0f;
     const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
-    int ncand = 0;  // exact buffer size, identical in every thread
+    bool exact_tau = false;  // tau is the k-th largest value seen (after a compaction)
+    int ncand = 0;           // exact buffer size, identical in every thread
     if (tid == 0) {
       for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_stream);
     }
@@ -884,7 +937,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         cm = fmaxf(cm, x[e]);
       }
       rmax = fmaxf(rmax, cm);
-      if (c < 3 || (c & 3) == 0) {
+      if (!exact_tau && (c < 3 || (c & 3) == 0)) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
         if (bmin != 0u && key_to_float(bmin) > tau) {
           tau = key_to_float(bmin);
@@ -912,8 +965,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       // exact count from the per-warp slots (slot c&1 is rewritten two chunks
       // on, after a barrier every thread has passed)
       ncand += __reduce_add_sync(0xFFFFFFFFu, lane < kStWarps ? sh.wcnt[c & 1][lane] : 0);
-      if (ncand > kCandCap - kChunk) {
-        // shrink to the entries >= the buffer's k-th largest (ties kept)
+      // shrink to the entries >= the buffer's k-th largest (ties kept) when the
+      // next chunk could overflow the buffer, and early on (chunks 3 and 11),
+      // where the exact k-th largest so far is a far tighter tau than the
+      // warp bound and cuts the inserts of the rest of the row
+      if (ncand > kCandCap - kChunk || ((c == 3 || c == 11) && ncand >= 2 * k)) {
         const int n0 = ncand;
         int above;
         const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
@@ -938,6 +994,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         ncand = ktot;
         tau = key_to_float(kk);
         strict = true;  // >= k entries >= kk are held: a later equal value ranks below
+        exact_tau = true;
         if (ktot > kCandCap - kChunk) over = true;  // heavy ties
       }
       if (over) break;
@@ -1030,15 +1087,16 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 
   if (mode == kStFull) {
     // one pass (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
-    float vmax_t = -INFINITY, vsum = 0.0f;
+    float vmax_t = -INFINITY;
+    f2_t vs2 = f2_pack(0.0f, 0.0f);
     ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int, int u) {
-      float cm = x[0];
-      vsum += x[0];
+      f2_t X[4];
 #pragma unroll
-      for (int e = 1; e < 8; ++e) {
-        vsum += x[e];
-        cm = fmaxf(cm, x[e]);
+      for (int j = 0; j < 4; ++j) {
+        X[j] = f2_pack(x[2 * j], x[2 * j + 1]);
+        vs2 = f2_add(vs2, X[j]);
       }
+      const float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
       vmax_t = fmaxf(vmax_t, cm);
       const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
       float mu = -INFINITY, su = 0.0f;
@@ -1046,10 +1104,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         mu = key_to_float(km);
         StW Wu = W;
         Wu.set_m(mu);
+        const StW2 W2(Wu);
+        f2_t s2 = W2(X[0]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (x[e] > -INFINITY) su += Wu(x[e]);
-        su = warp_sum_f(su);
+        for (int j = 1; j < 4; ++j) s2 = f2_add(s2, W2(X[j]));
+        float a0, a1;
+        f2_unpack(s2, a0, a1);
+        su = warp_sum_f(a0 + a1);
       }
       if (lane == 0) {
         sh.w.n.m[u] = mu;
@@ -1057,7 +1118,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
     });
     float vmax;
-    if (!finish_max(vmax_t, vsum, vmax)) return;
+    float vsum0, vsum1;
+    f2_unpack(vs2, vsum0, vsum1);
+    if (!finish_max(vmax_t, vsum0 + vsum1, vmax)) return;
     double zs = 0.0;
     for (int u = tid; u < nu; u += kStThreads) {
       const float mu = sh.w.n.m[u];
@@ -1076,8 +1139,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // x-grid coordinate t = (G - v) * xs + kUpBins + 1: kXBins bins per
   // kSXRange units of x = logit / T, anchored at G (the maximum of chunk 0, or
   // the row maximum on the fallback pass).  t < 1: more than kUpBins bins
-  // above G, kept exactly in the high list.  Index floor(t) in 1..kSBins: a
-  // grid bin; kSBins + 1: the tail (and masked tokens).  hq[i] holds the
+  // above G, kept exactly in the high list (index 0).  Index floor(t) in
+  // 1..kSBins: a grid bin; kSBins + 1: the tail (and masked tokens).  hq[i] holds the
   // fixed-point sum of kQScale * e^-((t - i) * dx) over the elements of index
   // i, so index i carries mass e^-((i - 1 - kUpBins) * dx) * hq[i] / kQScale
   // relative to G.  The histogram only places the bracket: pass 2 checks the
@@ -1086,28 +1149,50 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const float dx = kSXRange / (float)kXBins;
   const float t_off = (float)(kUpBins + 1);
   const float t_max = (float)kSBins + 1.25f;
-  // round(kQScale * e^-(fr*dx)) + 2^23 as a float (cubic, error (fr*dx)^4/24)
-  const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx,
-              q3 = -kQScale * dx * dx * dx * (1.0f / 6.0f);
+  // round(kQScale * e^-(fr*dx)) + 2^23 as a float (quadratic, error (fr*dx)^3/6 < 1.3e-6)
+  const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx;
   uint32_t *hq = sh.w.n.x.hq;
   float G = -INFINITY;
-  auto hist_add = [&](float v, int gidx) {
-    float t = fmaf(G - v, xs, t_off);
-    if (t < 1.0f) {  // above the grid: kept exactly (rare)
-      const int pos = atomicAdd(&sh.nhigh, 1);
-      if (pos < kHighCap) {
-        sh.w.n.hkey[pos] = fkey(v);
-        sh.w.n.hidx[pos] = gidx;
+  float v_high = INFINITY;  // no value at or below it lies above the grid (t < 1)
+  // Histogram of this lane's 8 values (x[4..7] sit 128 after x[0..3]), cm
+  // their maximum.  Grid coordinates are packed pairs clamped to
+  // [0.5, t_max]: index 0 collects the values above the grid (kept exactly in
+  // the high list and left out of the histogram's mass), kSBins + 1 the tail,
+  // -inf and NaN.
+  auto hist8 = [&](const float *x, int g0, float cm) {
+    if (__any_sync(0xFFFFFFFFu, cm > v_high)) {  // rare: some value may lie above the grid
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (fmaf(G - x[e], xs, t_off) < 1.0f) {
+          const int pos = atomicAdd(&sh.nhigh, 1);
+          if (pos < kHighCap) {
+            sh.w.n.hkey[pos] = fkey(x[e]);
+            sh.w.n.hidx[pos] = st_gidx(g0, e);
+          }
+        }
       }
-      return;
     }
-    t = fminf(t, t_max);  // the tail, -inf and NaN land on index kSBins + 1
-    // 2^23 + floor(t): the add rounds toward -inf, so index = floor(t) exactly,
-    // the same index the bracket tests of pass 2 (t < bound) imply
-    const float tb = __fadd_rd(t, 8388608.0f);
-    const float fr = t - (tb - 8388608.0f);
-    const float qf = fmaf(fmaf(fmaf(fr, q3, q2), fr, q1), fr, q0);
-    atomicAdd(&hq[__float_as_int(tb) - 0x4B000000], (uint32_t)(__float_as_int(qf) - 0x4B000000));
+    const f2_t G2 = f2_pack(G, G), XS2 = f2_pack(xs, xs), OFF2 = f2_pack(t_off, t_off);
+    const f2_t M2 = f2_pack(8388608.0f, 8388608.0f);
+    const f2_t Q0 = f2_pack(q0, q0), Q1 = f2_pack(q1, q1), Q2 = f2_pack(q2, q2);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float t0, t1;
+      f2_unpack(f2_fma(f2_sub(G2, f2_pack(x[2 * j], x[2 * j + 1])), XS2, OFF2), t0, t1);
+      const f2_t TC = f2_pack(fminf(fmaxf(t0, 0.5f), t_max), fminf(fmaxf(t1, 0.5f), t_max));
+      // 2^23 + floor(t): the add rounds toward -inf, so the index is floor(t)
+      const f2_t TB = f2_add_rm(TC, M2);
+      const f2_t FR = f2_sub(TC, f2_sub(TB, M2));
+      float tb0, tb1, qa, qb;
+      f2_unpack(TB, tb0, tb1);
+      f2_unpack(f2_fma(f2_fma(FR, Q2, Q1), FR, Q0), qa, qb);
+      atomicAdd(&hq[__float_as_int(tb0) - 0x4B000000], (uint32_t)(__float_as_int(qa) - 0x4B000000));
+      atomicAdd(&hq[__float_as_int(tb1) - 0x4B000000], (uint32_t)(__float_as_int(qb) - 0x4B000000));
+    }
+  };
+  auto set_anchor = [&](float g) {
+    G = g;
+    v_high = __double2float_rd((double)g + (double)(kUpBins - 1) / (double)xs);
   };
   auto hist_clear = [&]() {
     for (int i = tid; i < kQSlots; i += kStThreads) hq[i] = 0u;
@@ -1116,7 +1201,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   };
 
   // pass 1 (HBM, kept in L2): unit maxima, histogram anchored at chunk 0's max
-  float vmax_t = -INFINITY, vsum = 0.0f;
+  float vmax_t = -INFINITY;
+  f2_t vs2 = f2_pack(0.0f, 0.0f);
   hist_clear();
   if (tid == 0) {
     for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_keep);
@@ -1127,21 +1213,14 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     ph ^= 1u << s;
     float x[8];
     const int g0 = st_get8<DT>(sh, r, c, s, x);
-    float cm = x[0];
-    vsum += x[0];
 #pragma unroll
-    for (int e = 1; e < 8; ++e) {
-      vsum += x[e];
-      cm = fmaxf(cm, x[e]);
-    }
+    for (int j = 0; j < 4; ++j) vs2 = f2_add(vs2, f2_pack(x[2 * j], x[2 * j + 1]));
+    const float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
     vmax_t = fmaxf(vmax_t, cm);
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
     if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
-    if (c == 0) G = block_max_f<kStThreads>(cm, sh.redf);
-    if (G > -INFINITY) {  // block-uniform
-#pragma unroll
-      for (int e = 0; e < 8; ++e) hist_add(x[e], st_gidx(g0, e));
-    }
+    if (c == 0) set_anchor(block_max_f<kStThreads>(cm, sh.redf));
+    if (G > -INFINITY) hist8(x, g0, cm);  // block-uniform
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && c + kStages < r.nchunks) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1150,6 +1229,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   }
   ok = __syncthreads_and(ok) != 0;
   float vmax;
+  float vsum0, vsum1;
+  f2_unpack(vs2, vsum0, vsum1);
+  const float vsum = vsum0 + vsum1;
   if (!finish_max(vmax_t, vsum, vmax)) return;
   for (int u = tid; u < nu; u += kStThreads) {
     const float mu = sh.w.n.m[u];
@@ -1159,11 +1241,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // chunk 0 held no finite logit, or many values lie far above its max:
     // histogram pass (L2) anchored at the row maximum, nothing above it
     __syncthreads();
-    G = vmax;
+    set_anchor(vmax);
     hist_clear();
     ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) hist_add(x[e], st_gidx(g0, e));
+      const float cm =
+          fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
+      hist8(x, g0, cm);
     });
     if (!ok) {
       if (tid == 0) a.status[row] = kRowPending;
@@ -1188,8 +1271,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
-      mb[q] = i <= kSBins ? (double)hq[i] * (rG / (double)kQScale) * exp(-(double)(i - 1 - kUpBins) * (double)dx)
-                          : 0.0;  // the tail's mass (each < e^-30 of the anchor's weight) left out
+      // index 0: values above the grid, counted exactly in H; the tail's
+      // mass (each < e^-30 of the anchor's weight) is left out
+      mb[q] = (i >= 1 && i <= kSBins)
+                  ? (double)hq[i] * (rG / (double)kQScale) * exp(-(double)(i - 1 - kUpBins) * (double)dx)
+                  : 0.0;
       s += mb[q];
     }
     double ex, inc, tot;
@@ -1209,9 +1295,14 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (i_lo == 0x7FFFFFFF || i_lo > kSBins) i_lo = kSBins + 1;
     if (i_hi == 0x7FFFFFFF || i_hi > kSBins) i_hi = kSBins + 1;
   }
-  // bracket bounds on t: above <=> t < lo_f; in <=> lo_f <= t < hi_f
-  const float lo_f = i_lo < 0 ? -INFINITY : (float)i_lo;
-  const float hi_f = i_hi < 0 ? 1.0f : (i_hi > kSBins ? INFINITY : (float)(i_hi + 1));
+  // the bracket as values: above <=> v > v_lo; in the bracket <=> v_hi < v <= v_lo
+  // (t < bound <=> v > G - (bound - t_off) / xs).  Pass 2 is the arbiter: a
+  // value near a bin edge may land on either side of the histogram's split,
+  // which moves only the estimate; the exact checks below catch a bracket
+  // that misses the crossing.
+  auto t_to_v = [&](double tb) -> float { return (float)((double)G - (tb - (double)t_off) / (double)xs); };
+  const float v_lo = i_lo < 0 ? INFINITY : t_to_v((double)i_lo);
+  const float v_hi = i_hi < 0 ? t_to_v(1.0) : (i_hi > kSBins ? -INFINITY : t_to_v((double)(i_hi + 1)));
   // pass 2 (L2): every weight once: per-unit mass above the bracket (into
   // s_u), the exact total, and the bracket's elements
   if (tid == 0) sh.ncand = 0;
@@ -1219,30 +1310,40 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   bool gover = false;
   double zacc = 0.0;
   ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int u) {
-    StW Wu = W;
-    Wu.set_m(sh.w.n.m[u]);
-    float above = 0.0f, all = 0.0f;
-    uint32_t inm = 0u;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const bool valid = x[e] > -INFINITY;
-      const float w = valid ? Wu(x[e]) : 0.0f;
-      all += w;
-      const float t = fmaf(G - x[e], xs, t_off);
-      const bool ab = t < lo_f;
-      above += ab ? w : 0.0f;
-      if (valid && !ab && t < hi_f) inm |= 1u << e;
+    const float mu = sh.w.n.m[u];
+    if (!(mu > -INFINITY)) {  // no finite value in the unit (warp-uniform)
+      if (lane == 0) sh.w.n.s[u] = 0.0f;
+      return;
     }
-    above = warp_sum_f(above);
-    all = warp_sum_f(all);
+    StW Wu = W;
+    Wu.set_m(mu);
+    const StW2 W2(Wu);
+    f2_t all2 = f2_pack(0.0f, 0.0f), ab2 = all2;
+    bool any_in = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float xa = x[2 * j], xb = x[2 * j + 1];
+      const f2_t Wp = W2(f2_pack(xa, xb));  // -inf weighs 0
+      all2 = f2_add(all2, Wp);
+      float wa, wb;
+      f2_unpack(Wp, wa, wb);
+      const bool aa = xa > v_lo, ab = xb > v_lo;
+      ab2 = f2_add(ab2, f2_pack(aa ? wa : 0.0f, ab ? wb : 0.0f));
+      any_in |= (!aa && xa > v_hi) || (!ab && xb > v_hi);
+    }
+    float s0, s1, t0, t1;
+    f2_unpack(ab2, s0, s1);
+    f2_unpack(all2, t0, t1);
+    const float above = warp_sum_f(s0 + s1);
+    const float all = warp_sum_f(t0 + t1);
     if (lane == 0) {
       sh.w.n.s[u] = above;
       zacc += (double)all * (double)sh.w.n.f[u];
     }
-    if (inm != 0u) {
+    if (any_in) {  // rare
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        if ((inm >> e) & 1u) {
+        if (!(x[e] > v_lo) && x[e] > v_hi) {
           const int pos = atomicAdd(&sh.ncand, 1);
           if (pos < kSortCap) {
             sh.w.n.x.g.key[pos] = fkey(x[e]);
