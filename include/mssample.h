@@ -55,8 +55,12 @@ enum {
                                  the reference raises ZeroDivisionError
                                  (miniserve/sampler.py:46-47) */
   MS_ROW_BAD_TEMPERATURE = 2, /* temperature < 0, NaN or infinite */
-  MS_ROW_NONFINITE = 4        /* a NaN or +inf logit was present; NaN is read
+  MS_ROW_NONFINITE = 4,       /* a NaN or +inf logit was present; NaN is read
                                  as -inf (the reference's result is arbitrary) */
+  MS_ROW_UNSUPPORTED = 8      /* vocab-sharded calls only: the row needs the
+                                 full vocabulary (top_k off or above kmax,
+                                 a tie block past the candidate buffer, a
+                                 non-finite logit); token -1 */
 };
 
 /*
@@ -90,6 +94,49 @@ int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64
                       const double *temperature, const int32_t *top_k, const double *top_p,
                       const double *uniforms, const uint32_t *mask, int64_t mask_ld,
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);
+
+/*
+ * Vocab-sharded sampling.  Rank r of N holds the contiguous slice
+ * [v0, v0 + Vloc) of a V-token vocabulary (as a tensor-parallel LM head
+ * produces it; slices in rank order).  The global top-k is contained in the
+ * union of the slices' top-k, so a fixed-size candidate record per row and
+ * rank is all that crosses the interconnect:
+ *
+ *   1. every rank: ms_shard_candidates on its slice -> records [B][rec_words]
+ *   2. the caller all-gathers the records of all ranks, rank-major:
+ *      [nranks][B][rec_words] (e.g. ncclAllGather)
+ *   3. every rank: ms_shard_merge -> the same tokens on every rank
+ *
+ * Record of one row (32-bit words, rec_words = 2 + 2*kmax): [0] candidate
+ * count m <= kmax, [1] MS_ROW_* bits, [2, 2+kmax) order keys of the slice's
+ * top-m values (value descending, index ascending), [2+kmax, 2+2*kmax) their
+ * global token ids.  Rows the scheme cannot sample exactly (top_k off or
+ * above kmax with temperature > 0, top_k >= Vloc, tie blocks beyond the
+ * candidate buffer, non-finite logits) come back with MS_ROW_UNSUPPORTED or
+ * MS_ROW_NONFINITE and token -1; the caller samples those rows from their
+ * full vocabulary (ms_sample on the gathered row).  Greedy rows
+ * (temperature 0 or top_k 1) and top-k rows (2 <= top_k <= kmax) are exact.
+ * Same reference semantics as ms_sample (miniserve/sampler.py:23-68).
+ *
+ * kmax: 1..256, the same on every rank.  mask: optional bitmask of the slice
+ * ([B, mask_ld] u32, bit i = local token i).
+ */
+int ms_shard_candidates(const void *logits, int dtype, int64_t B, int64_t Vloc, int64_t ld, int64_t v0,
+                        int64_t V, const double *temperature, const int32_t *top_k, const uint32_t *mask,
+                        int64_t mask_ld, int32_t kmax, uint32_t *records, ms_stream_t stream);
+
+/* 32-bit words of one row's record for a given kmax (2 + 2*kmax). */
+int64_t ms_shard_record_words(int32_t kmax);
+
+/*
+ * Merge the all-gathered records ([nranks][B][rec_words]) into tokens,
+ * probabilities and statuses (same outputs as ms_sample).  nranks * kmax must
+ * be <= 2048.
+ */
+int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t kmax, int64_t V,
+                   const double *temperature, const int32_t *top_k, const double *top_p,
+                   const double *uniforms, int64_t *tokens, float *probs, int32_t *row_status,
+                   ms_stream_t stream);
 
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);

@@ -19,6 +19,7 @@ MS_ROW_OK = 0
 MS_ROW_ALL_MASKED = 1
 MS_ROW_BAD_TEMPERATURE = 2
 MS_ROW_NONFINITE = 4
+MS_ROW_UNSUPPORTED = 8
 
 _lock = threading.Lock()
 _lib = None
@@ -32,6 +33,11 @@ SIGNATURES = {
                                  _P, _P, _P, _P]),
     "ms_sample_generic": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _P, _P, _P, _P,
                                          _I64, _P, _P, _P, _P]),
+    "ms_shard_candidates": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
+                                           _I64, ctypes.c_int32, _P, _P]),
+    "ms_shard_record_words": (_I64, [ctypes.c_int32]),
+    "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,
+                                      _P, _P, _P, _P]),
     "ms_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ms_last_cuda_error": (ctypes.c_int, []),
     "ms_version": (ctypes.c_int, []),

@@ -41,6 +41,13 @@ struct SampleArgs {
   int64_t *tokens;
   float *probs;
   int32_t *status;
+  // vocab-sharded candidate mode (ms_shard_candidates): when records is set
+  // the streaming kernel writes one candidate record per row instead of a
+  // token; the row is the slice [v0, v0 + V) of a Vg-token vocabulary
+  uint32_t *records = nullptr;
+  int kmax = 0;
+  int64_t v0 = 0;
+  int64_t Vg = 0;
 };
 
 template <int DT>

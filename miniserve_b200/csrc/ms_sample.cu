@@ -18,6 +18,7 @@
 
 #include "ms_common.cuh"
 #include "ms_generic.cuh"
+#include "ms_shard.cuh"
 #include "ms_stream.cuh"
 
 namespace {
@@ -30,14 +31,9 @@ int cuda_fail(cudaError_t e) {
 
 constexpr int kMaxDevices = 64;
 
-// The streaming kernel (one CTA per row) for every row it can finish, then
-// the generic kernel for the rows it marked pending.
+// The streaming kernel alone (one CTA per row).
 template <int DT>
-cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, bool generic_only) {
-  if (generic_only || a.V > ms::kStreamMaxV) {
-    ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
-    return cudaGetLastError();
-  }
+cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int dev) {
   static std::atomic<int> ready[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!ready[dev].load(std::memory_order_acquire)) {
@@ -47,7 +43,18 @@ cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, 
     ready[dev].store(1, std::memory_order_release);
   }
   ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  return cudaGetLastError();
+}
+
+// The streaming kernel (one CTA per row) for every row it can finish, then
+// the generic kernel for the rows it marked pending.
+template <int DT>
+cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, bool generic_only) {
+  if (generic_only || a.V > ms::kStreamMaxV) {
+    ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
+    return cudaGetLastError();
+  }
+  cudaError_t e = launch_stream<DT>(a, B, s, dev);
   if (e != cudaSuccess) return e;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -112,6 +119,57 @@ int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
   return sample_impl(logits, dtype, B, V, ld, temperature, top_k, top_p, uniforms, mask, mask_ld,
                      tokens, probs, row_status, stream, true);
+}
+
+int64_t ms_shard_record_words(int32_t kmax) { return 2 + 2 * (int64_t)kmax; }
+
+int ms_shard_candidates(const void *logits, int dtype, int64_t B, int64_t Vloc, int64_t ld, int64_t v0,
+                        int64_t V, const double *temperature, const int32_t *top_k, const uint32_t *mask,
+                        int64_t mask_ld, int32_t kmax, uint32_t *records, ms_stream_t stream) {
+  if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
+  if (B < 0 || B > 0x7FFFFFFFll || Vloc < 1 || ld < Vloc || v0 < 0 || V < v0 + Vloc ||
+      V > 0x7FFFFFFFll - 4096 || kmax < 1 || kmax > ms::kMgTopK)
+    return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!logits || !temperature || !top_k || !records) return MS_E_INVALID;
+  if (mask && mask_ld < (Vloc + 31) / 32) return MS_E_INVALID;
+  if (Vloc > ms::kStreamMaxV) return MS_E_UNSUPPORTED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // top_p and the uniforms are not read in this mode; the temperature array
+  // stands in for both pointers
+  ms::SampleArgs a{logits, ld, (int)Vloc, temperature, top_k, temperature, temperature,
+                   mask, mask_ld, nullptr, nullptr, nullptr};
+  a.records = records;
+  a.kmax = kmax;
+  a.v0 = v0;
+  a.Vg = V;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = dtype == MS_DTYPE_F32 ? launch_stream<MS_DTYPE_F32>(a, (int)B, s, dev)
+                            : launch_stream<MS_DTYPE_BF16>(a, (int)B, s, dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
+}
+
+int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t kmax, int64_t V,
+                   const double *temperature, const int32_t *top_k, const double *top_p,
+                   const double *uniforms, int64_t *tokens, float *probs, int32_t *row_status,
+                   ms_stream_t stream) {
+  if (B < 0 || B > 0x7FFFFFFFll || V < 1 || V > 0x7FFFFFFFll - 4096 || kmax < 1 || kmax > ms::kMgTopK ||
+      nranks < 1)
+    return MS_E_INVALID;
+  if (nranks > ms::kMgRanks || (int64_t)nranks * kmax > ms::kMgCap) return MS_E_UNSUPPORTED;
+  if (B == 0) return MS_OK;
+  if (!records || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
+    return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ms::MergeArgs a{records, nranks, (int)B, kmax, V, temperature, top_k, top_p, uniforms,
+                  tokens, probs, row_status};
+  ms::ms_merge_kernel<<<dim3((unsigned)B), dim3(ms::kMgThreads), 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,169 @@
+// Merge step of vocab-sharded sampling: one 256-thread CTA per row reads the
+// all-gathered candidate records of every rank ([nranks][B][2 + 2*kmax]
+// words), ranks the union by (value descending, global id ascending) and
+// finishes the row exactly as miniserve/sampler.py:23-68 does on the full
+// vocabulary: the global top-k set is contained in the union of the slices'
+// top-k sets, and every weight exp(l/T - max/T) is computed in float64 from
+// the exact logit (its order key).
+#pragma once
+
+#include "ms_common.cuh"
+#include "ms_generic.cuh"
+
+namespace ms {
+
+constexpr int kMgThreads = 256;
+constexpr int kMgCap = 2048;     // candidates per row over all ranks
+constexpr int kMgTopK = 256;     // largest kmax
+constexpr int kMgRanks = 256;    // largest nranks
+
+struct MergeArgs {
+  const uint32_t *records;
+  int nranks;
+  int B;
+  int kmax;
+  int64_t V;  // the full vocabulary
+  const double *temperature;
+  const int32_t *top_k;
+  const double *top_p;
+  const double *uniforms;
+  int64_t *tokens;
+  float *probs;
+  int32_t *status;
+};
+
+struct MgShared {
+  unsigned long long comp[kMgCap + 2];  // (key, ~id) composites, padded for paired reads
+  uint32_t key[kMgTopK];                // the top-k set in rank order
+  int id[kMgTopK];
+  int kid[kMgTopK];                     // kept ids in index order
+  double kw[kMgTopK];                   // and their weights
+  int off[kMgRanks + 1];
+  uint32_t st;
+  double redd[33];
+  int redi[33];
+  unsigned long long redq[33];
+};
+
+__device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok, float prob, int32_t st) {
+  a.tokens[r] = tok;
+  a.probs[r] = prob;
+  a.status[r] = st;
+}
+
+__global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
+  __shared__ MgShared sh;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const size_t rw = (size_t)(2 + 2 * a.kmax);
+  const double T = a.temperature[row];
+  const int k = a.top_k[row];
+  const double P = a.top_p[row];
+  const double U = a.uniforms[row];
+  // per-rank counts -> offsets; statuses OR-ed
+  int m_r = 0;
+  uint32_t st_r = 0u;
+  if (tid < a.nranks) {
+    const uint32_t *rec = a.records + ((size_t)tid * a.B + row) * rw;
+    m_r = (int)min(rec[0], (uint32_t)a.kmax);
+    st_r = rec[1];
+  }
+  if (tid == 0) sh.st = 0u;
+  __syncthreads();
+  if (st_r) atomicOr(&sh.st, st_r);
+  int ex, inc, n;
+  block_scan<kMgThreads, int>(m_r, ex, inc, n, sh.redi);  // ends with a barrier
+  if (tid < a.nranks) sh.off[tid] = ex;
+  const uint32_t st = sh.st;
+  if (st != 0u) {  // bad temperature, or a slice that needs the full row
+    if (tid == 0) mg_write(a, row, -1, 0.0f, (int32_t)st);
+    return;
+  }
+  __syncthreads();
+  for (int r = 0; r < a.nranks; ++r) {
+    const uint32_t *rec = a.records + ((size_t)r * a.B + row) * rw;
+    const int mr = (int)min(rec[0], (uint32_t)a.kmax);
+    for (int i = tid; i < mr; i += kMgThreads)
+      sh.comp[sh.off[r] + i] = ((unsigned long long)rec[2 + i] << 32) | (unsigned long long)(~rec[2 + a.kmax + i]);
+  }
+  if (tid == 0) {
+    sh.comp[n] = 0ull;
+    sh.comp[n + 1] = 0ull;
+  }
+  __syncthreads();
+  if (n == 0) {  // every logit -inf
+    if (tid == 0) {
+      if (T == 0.0) mg_write(a, row, 0, 1.0f, 0);            // greedy ties at index 0 (sampler.py:33-34)
+      else mg_write(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);    // zero total (sampler.py:46-47)
+    }
+    return;
+  }
+  if (T == 0.0 || k == 1) {  // the first maximum (sampler.py:33-34, or top-k 1)
+    unsigned long long best = 0ull;
+    for (int i = tid; i < n; i += kMgThreads) best = max(best, sh.comp[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
+    if ((tid & 31) == 0) sh.redq[tid >> 5] = best;
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kMgThreads / 32; ++w) best = max(best, sh.redq[w]);
+      const int64_t id = (int64_t)(~(uint32_t)best);
+      if (T == 0.0 || U > 0.0) mg_write(a, row, id, 1.0f, 0);
+      else mg_write(a, row, 0, id == 0 ? 1.0f : 0.0f, 0);  // r == 0 stops at index 0
+    }
+    return;
+  }
+  // top-k: rank every candidate; the best min(n, k) are the row's top-k set
+  const int m = min(n, k);
+  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.comp);
+  const int npair = (n + 1) >> 1;
+  for (int i = tid; i < n; i += kMgThreads) {
+    const unsigned long long ci = sh.comp[i];
+    int rank = 0;
+    for (int j = 0; j < npair; ++j) {
+      const ulonglong2 q = c2[j];
+      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
+    }
+    if (rank < m) {
+      sh.key[rank] = (uint32_t)(ci >> 32);
+      sh.id[rank] = (int)~(uint32_t)ci;
+    }
+  }
+  __syncthreads();
+  // float64 weights over the top-k set (sampler.py:35,45): thread r, rank r
+  const double xmax = (double)key_to_float(sh.key[0]) / T;
+  const double w = tid < m ? exp((double)key_to_float(sh.key[tid]) / T - xmax) : 0.0;
+  double wex, winc, total;
+  block_scan<kMgThreads, double>(w, wex, winc, total, sh.redd);
+  int nkeep = m;
+  if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept (sampler.py:49-58)
+    const int first = block_min_i<kMgThreads>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
+    if (first != 0x7FFFFFFF) nkeep = first + 1;
+  }
+  // kept entries in index order
+  if (tid < nkeep) {
+    const int my = sh.id[tid];
+    int pos = 0;
+    for (int j = 0; j < nkeep; ++j) pos += sh.id[j] < my ? 1 : 0;
+    sh.kid[pos] = my;
+    sh.kw[pos] = w;
+  }
+  const double tot = block_sum<kMgThreads>(tid < nkeep ? w : 0.0, sh.redd);  // ends with a barrier
+  // index-order inverse CDF (sampler.py:60-68)
+  if (!(U > 0.0)) {  // r == 0 stops at index 0
+    if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.kw[0] : 0.0) / tot), 0);
+    return;
+  }
+  const double target = U * tot;
+  const double kwv = tid < nkeep ? sh.kw[tid] : 0.0;
+  double cex, cinc, ctot;
+  block_scan<kMgThreads, double>(kwv, cex, cinc, ctot, sh.redd);
+  const int who = block_min_i<kMgThreads>((tid < nkeep && kwv > 0.0 && cinc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  if (tid == 0 && who == 0x7FFFFFFF) {  // ran past the end
+    const int last = nkeep - 1;
+    mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.kw[last] : 0.0) / tot), 0);
+  }
+  if (tid == who) mg_write(a, row, sh.kid[tid], (float)(kwv / tot), 0);
+}
+
+}  // namespace ms

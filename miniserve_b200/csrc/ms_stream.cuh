@@ -525,15 +525,13 @@ __device__ __forceinline__ uint32_t st_topk_bound_nb(StShared &sh, float rmax, i
   return __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? wb[lane] : 0xFFFFFFFFu);
 }
 
-// Exact top-k finish over a candidate buffer of n <= kRankCap unordered
-// entries (sh.w.c) holding every member of the row's top-k set, ranked by
-// value descending then index ascending (the stable sort of
-// miniserve/sampler.py:37-44).  Keys below thr cannot rank in that set.
-// float64 weights exp(l/T - max/T) (sampler.py:35,45), top-p in rank order
-// (sampler.py:49-58), index-order draw (sampler.py:60-68).  The idle transfer
-// stages hold scratch.  All threads.
-__device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int n, int k, uint32_t thr,
-                                double T, double P, double U, float vmax) {
+// The top-k set of a candidate buffer of n <= kRankCap unordered entries
+// (sh.w.c) that holds every member of the row's top-k set, ranked by value
+// descending then index ascending (the stable sort of
+// miniserve/sampler.py:37-44).  Keys below thr cannot rank in that set.  The
+// best m = min(k, entries) land in sh.w.c.key/idx[0..m) in rank order;
+// returns m.  The idle transfer stages hold scratch.  All threads.
+__device__ int st_topk_rank(StShared &sh, int n, int k, uint32_t thr) {
   const int tid = threadIdx.x;
   unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
   // (key, ~index) composites: larger = earlier in rank order, all distinct
@@ -566,6 +564,16 @@ __device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int 
     }
   }
   __syncthreads();
+  return m;
+}
+
+// Exact top-k finish: st_topk_rank, float64 weights exp(l/T - max/T)
+// (miniserve/sampler.py:35,45), top-p in rank order (sampler.py:49-58),
+// index-order draw (sampler.py:60-68).  All threads.
+__device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int n, int k, uint32_t thr,
+                                double T, double P, double U, float vmax) {
+  const int tid = threadIdx.x;
+  const int m = st_topk_rank(sh, n, k, thr);
   // thread r holds rank r
   const double xmax = (double)vmax / T;
   const double w = tid < m ? exp((double)key_to_float(sh.w.c.key[tid]) / T - xmax) : 0.0;
@@ -720,6 +728,17 @@ __device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r,
 
 enum StMode : int { kStArgmax = 0, kStTopKMode = 1, kStFull = 2, kStNucleus = 3 };
 
+// Candidate record of `row` in vocab-sharded mode: [count, status, kmax keys,
+// kmax global ids].
+__device__ __forceinline__ uint32_t *st_record(const SampleArgs &a, int row) {
+  return a.records + (size_t)row * (size_t)(2 + 2 * a.kmax);
+}
+__device__ __forceinline__ void st_record_empty(const SampleArgs &a, int row, uint32_t status) {
+  uint32_t *rec = st_record(a, row);
+  rec[0] = 0u;
+  rec[1] = status;
+}
+
 // Cost class of row r, longest first: top-p-only 0, top-k 1, full softmax 2,
 // argmax and rows finished without reading the logits 3.
 __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
@@ -811,13 +830,33 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const double P = a.top_p[row];
   const double U = a.uniforms[row];
   const int V = a.V;
+  const bool shard = a.records != nullptr;
   if (!(T >= 0.0) || isinf(T)) {  // negative, NaN or infinite temperature
-    if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_BAD_TEMPERATURE);
+    if (tid == 0) {
+      if (shard) st_record_empty(a, row, MS_ROW_BAD_TEMPERATURE);
+      else write_row(a, row, -1, 0.0f, MS_ROW_BAD_TEMPERATURE);
+    }
     return;
   }
+  // a row this kernel does not finish: the generic kernel takes it, or in
+  // sharded mode its record says why (nonfinite: a NaN / +inf logit)
+  auto leave = [&](bool nonfinite) {
+    if (tid == 0) {
+      if (shard) st_record_empty(a, row, nonfinite ? MS_ROW_NONFINITE : MS_ROW_UNSUPPORTED);
+      else a.status[row] = kRowPending;
+    }
+  };
   int mode;
   if (T == 0.0 || k == 1) {
     mode = kStArgmax;
+  } else if (shard) {
+    // the slice's top-k stands for the row's only when top_k cuts the whole
+    // vocabulary and fits the record
+    if (!(k >= 2 && (int64_t)k < a.Vg && k <= a.kmax && k < V && k <= kStTopK)) {
+      leave(false);
+      return;
+    }
+    mode = kStTopKMode;
   } else if (k >= 2 && k < V) {
     mode = kStTopKMode;
   } else {
@@ -825,8 +864,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   }
   // top_k above what the streaming buffer resolves, or a temperature too small
   // for fp32 weights: the generic kernel finishes the row
-  if ((mode == kStTopKMode && k > kStTopK) || (mode != kStArgmax && !(T >= kMinTemperature))) {
-    if (tid == 0) a.status[row] = kRowPending;
+  if (!shard && ((mode == kStTopKMode && k > kStTopK) || (mode != kStArgmax && !(T >= kMinTemperature)))) {
+    leave(false);
     return;
   }
   StRow r;
@@ -890,7 +929,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       int i2 = tid < kStWarps ? sh.redi[tid] : 0x7FFFFFFF;
       warp_argmax(k2, i2);
       if (tid == 0) {
-        if (any_bad) {
+        if (shard) {  // the slice's first maximum (none when all -inf)
+          uint32_t *rec = st_record(a, row);
+          rec[0] = (!any_bad && k2 != 0u) ? 1u : 0u;
+          rec[1] = any_bad ? (uint32_t)MS_ROW_NONFINITE : 0u;
+          rec[2] = k2;
+          rec[2 + a.kmax] = (uint32_t)(a.v0 + i2);
+        } else if (any_bad) {
           a.status[row] = kRowPending;
         } else if (T == 0.0) {  // greedy; all -inf ties at index 0 (sampler.py:33-34)
           write_row(a, row, k2 == 0u ? 0 : i2, 1.0f, 0);
@@ -1014,12 +1059,15 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
     const bool bad = isnan(vsum) || vsum == INFINITY;
     if (__syncthreads_or(bad || !ok || over)) {
-      if (tid == 0) a.status[row] = kRowPending;
+      leave(__syncthreads_or(bad) != 0);
       return;
     }
     const float vmax = block_max_f<kStThreads>(rmax, sh.redf);
     if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
-      if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
+      if (tid == 0) {
+        if (shard) st_record_empty(a, row, 0u);  // no candidate in this slice
+        else write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
+      }
       return;
     }
     // exact top-k of the buffer; fewer valid tokens than top_k keep all
@@ -1047,7 +1095,20 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       n = ktot;
     }
     if (n > kRankCap) {  // a tie block larger than the rank sort: generic kernel
-      if (tid == 0) a.status[row] = kRowPending;
+      leave(false);
+      return;
+    }
+    if (shard) {  // the slice's top-k, in rank order, with global ids
+      const int m = st_topk_rank(sh, n, k, st_topk_bound(sh, rmax, jw));
+      uint32_t *rec = st_record(a, row);
+      for (int i = tid; i < m; i += kStThreads) {
+        rec[2 + i] = sh.w.c.key[i];
+        rec[2 + a.kmax + i] = (uint32_t)(a.v0 + sh.w.c.idx[i]);
+      }
+      if (tid == 0) {
+        rec[0] = (uint32_t)m;
+        rec[1] = 0u;
+      }
       return;
     }
     st_finish_small(sh, a, row, n, k, st_topk_bound(sh, rmax, jw), T, P, U, vmax);

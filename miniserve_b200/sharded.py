@@ -1,0 +1,172 @@
+"""Vocab-sharded sampling: one process per GPU, each holding a contiguous
+slice of the vocabulary (as a tensor-parallel LM head produces the logits).
+
+Step 1 runs ``ms_shard_candidates`` on the rank's slice: per row, the slice's
+top-k values (value descending, index ascending) with their global token ids,
+in a fixed-size record.  Step 2 all-gathers the records of every rank (NCCL
+over NVLink on GPUs; the only data that crosses the interconnect is
+``B * (2 + 2*kmax) * 4`` bytes per rank).  Step 3 runs ``ms_shard_merge`` on
+every rank, which finishes each row exactly as miniserve's
+``Sampler.sample`` (miniserve/sampler.py:23-68) does on the whole vocabulary:
+the row's top-k set is contained in the union of the slices' top-k sets.
+
+Rows the record cannot carry exactly (temperature > 0 with top_k off or above
+kmax, a non-finite logit, a tie block larger than the candidate buffer) come
+back flagged; for those rows only, every rank all-gathers the full logits and
+samples them with the single-GPU kernel, so every row is exact.  All ranks see
+identical statuses, so they take the same collective steps.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence, Tuple
+
+from . import _lib
+from .sampler import Sampler, _param, _torch, uniform_for_seed
+
+KMAX_LIMIT = 256
+
+
+def record_words(kmax: int) -> int:
+    """32-bit words in one row's candidate record."""
+    return 2 + 2 * int(kmax)
+
+
+def shard_bounds(V: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous slice [v0, v1) of rank `rank` (slices in rank order)."""
+    return (V * rank) // world, (V * (rank + 1)) // world
+
+
+def choose_kmax(top_k: Sequence[int], temperature: Sequence[float]) -> int:
+    """Smallest record width that carries every greedy / top-k row (<= 256)."""
+    need = 1
+    for k, t in zip(top_k, temperature):
+        if t != 0.0 and 2 <= k <= KMAX_LIMIT:
+            need = max(need, int(k))
+    return need
+
+
+def exchange_records(records, group=None):
+    """All-gather [B, W] int32 records of every rank -> [world, B, W], rank-major."""
+    torch = _torch()
+    import torch.distributed as dist
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return records.unsqueeze(0)
+    world = dist.get_world_size(group)
+    out = torch.empty((world * records.shape[0],) + tuple(records.shape[1:]), dtype=records.dtype,
+                      device=records.device)
+    dist.all_gather_into_tensor(out, records.contiguous(), group=group)
+    return out.view((world,) + tuple(records.shape))
+
+
+def gather_rows(logits_slice, rows, V: int, group=None):
+    """Full-vocabulary logits [len(rows), V] of the given rows, assembled from
+    every rank's slice (slices may differ in width by one token)."""
+    torch = _torch()
+    import torch.distributed as dist
+    part = logits_slice[rows]
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return part.contiguous()
+    world = dist.get_world_size(group)
+    width = max(b - a for a, b in (shard_bounds(V, world, r) for r in range(world)))
+    padded = torch.zeros((part.shape[0], width), dtype=part.dtype, device=part.device)
+    padded[:, : part.shape[1]] = part
+    out = torch.empty((world * padded.shape[0], width), dtype=part.dtype, device=part.device)
+    dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
+    out = out.view(world, padded.shape[0], width)
+    cols = [out[r, :, : b - a] for r, (a, b) in enumerate(shard_bounds(V, world, r) for r in range(world))]
+    return torch.cat(cols, dim=1).contiguous()
+
+
+class ShardedSampler:
+    """Sample [B, V] rows whose vocabulary is split across the ranks of `group`."""
+
+    def __init__(self, V: int, group=None) -> None:
+        self.V = int(V)
+        self.group = group
+        self._single = Sampler()
+
+    def sample(self, logits_slice, v0: int, temperature=1.0, top_k=0, top_p=1.0,
+               uniforms=None, seeds: Optional[Sequence[Optional[int]]] = None,
+               mask=None):
+        """``logits_slice``: this rank's [B, Vloc] CUDA tensor (fp32/bf16) for
+        tokens [v0, v0 + Vloc); ``mask``: optional [B, ceil(Vloc/32)] bitmask of
+        the slice.  Per-row parameters must be the same on every rank.  Returns
+        (tokens i64, probs f32, status i32), identical on every rank."""
+        torch = _torch()
+        if logits_slice.dim() != 2 or not logits_slice.is_cuda:
+            raise ValueError("logits_slice must be a [B, Vloc] CUDA tensor")
+        if logits_slice.stride(1) != 1:
+            logits_slice = logits_slice.contiguous()
+        dtype = {torch.float32: _lib.MS_DTYPE_F32, torch.bfloat16: _lib.MS_DTYPE_BF16}.get(logits_slice.dtype)
+        if dtype is None:
+            raise TypeError(f"logits dtype {logits_slice.dtype} is not float32 or bfloat16")
+        B, Vloc = logits_slice.shape
+        dev = logits_slice.device
+        T = _param(temperature, B, torch.float64, dev)
+        K = _param(top_k, B, torch.int32, dev)
+        P = _param(top_p, B, torch.float64, dev)
+        if uniforms is None:
+            seeds = [None] * B if seeds is None else list(seeds)
+            uniforms = [uniform_for_seed(s) for s in seeds]
+        U = _param(uniforms, B, torch.float64, dev)
+        kmax = choose_kmax(K.tolist(), T.tolist())
+        W = record_words(kmax)
+        L = _lib.lib()
+        mask_ptr, mask_ld = None, 0
+        if mask is not None:
+            mask_ptr, mask_ld = mask.data_ptr(), mask.stride(0)
+        records = torch.empty((B, W), dtype=torch.int32, device=dev)
+        tokens = torch.empty(B, dtype=torch.int64, device=dev)
+        probs = torch.empty(B, dtype=torch.float32, device=dev)
+        status = torch.empty(B, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            rc = L.ms_shard_candidates(logits_slice.data_ptr(), dtype, B, Vloc, logits_slice.stride(0), int(v0),
+                                       self.V, T.data_ptr(), K.data_ptr(), mask_ptr, mask_ld, kmax,
+                                       records.data_ptr(), stream)
+            _lib.check(rc, "ms_shard_candidates")
+            allrec = exchange_records(records, self.group)
+            nranks = allrec.shape[0]
+            rc = L.ms_shard_merge(allrec.data_ptr(), nranks, B, kmax, self.V, T.data_ptr(), K.data_ptr(),
+                                  P.data_ptr(), U.data_ptr(), tokens.data_ptr(), probs.data_ptr(),
+                                  status.data_ptr(), stream)
+            _lib.check(rc, "ms_shard_merge")
+        redo = ((status & (_lib.MS_ROW_UNSUPPORTED | _lib.MS_ROW_NONFINITE)) != 0).nonzero().flatten()
+        if redo.numel():
+            rows = redo.to(dev)
+            full = gather_rows(logits_slice, rows, self.V, self.group)
+            fmask = None
+            if mask is not None:
+                fmask = _full_mask(mask, rows, Vloc, self.V, self.group)
+            t2, p2, s2 = self._single.sample_batch(full, T[rows], K[rows], P[rows], uniforms=U[rows], mask=fmask)
+            tokens[rows], probs[rows], status[rows] = t2, p2, s2
+        return tokens, probs, status
+
+
+def _full_mask(mask, rows, Vloc: int, V: int, group):
+    """Full-vocabulary bitmask of `rows` from every rank's slice mask."""
+    torch = _torch()
+    import torch.distributed as dist
+    bits = _unpack_bits(mask[rows], Vloc)
+    if group is not None or (dist.is_available() and dist.is_initialized()):
+        bits = gather_rows(bits, torch.arange(bits.shape[0], device=bits.device), V, group)
+    return _pack_bits(bits)
+
+
+def _unpack_bits(words, n: int):
+    torch = _torch()
+    w = words.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(32, device=w.device, dtype=torch.int64)
+    bits = ((w.unsqueeze(-1) >> shifts) & 1).reshape(w.shape[0], -1)[:, :n]
+    return bits.to(torch.uint8)
+
+
+def _pack_bits(bits):
+    torch = _torch()
+    B, n = bits.shape
+    W = (n + 31) // 32
+    padded = torch.zeros((B, W * 32), dtype=torch.int64, device=bits.device)
+    padded[:, :n] = bits.to(torch.int64)
+    shifts = torch.arange(32, device=bits.device, dtype=torch.int64)
+    words = (padded.reshape(B, W, 32) << shifts).sum(-1)
+    return ((words + 2**31) % 2**32 - 2**31).to(torch.int32)  # the same 32 bits as int32

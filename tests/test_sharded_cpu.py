@@ -1,0 +1,88 @@
+"""Host side of the vocab-sharded path on CPU: slice bounds, record width,
+and a world_size-2 gloo run of the record all-gather and the full-row gather,
+with the decomposition (union of the slices' top-k) checked against the
+oracle on the full rows."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle
+import sharded_ref
+from miniserve_b200 import sharded
+
+
+def test_shard_bounds_partition():
+    for V in (1, 7, 4096, 151936, 256000):
+        for world in (1, 2, 3, 4, 8):
+            b = [sharded.shard_bounds(V, world, r) for r in range(world)]
+            assert b[0][0] == 0 and b[-1][1] == V
+            assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
+            assert max(e - s for s, e in b) - min(e - s for s, e in b) <= 1
+
+
+def test_choose_kmax():
+    assert sharded.choose_kmax([0, 1, 50, 20], [1.0, 1.0, 0.9, 0.0]) == 50
+    assert sharded.choose_kmax([0, 300], [1.0, 1.0]) == 1
+    assert sharded.record_words(50) == 102
+
+
+def _batch(B=24, V=12288, seed=5):
+    rng = np.random.default_rng(seed)
+    base = -1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))
+    x = np.stack([(base[rng.permutation(V)] + rng.normal(0, 0.5, V)).astype(np.float32) for _ in range(B)])
+    x[3, 100:200] = x[3].max()  # a tie block across the max
+    T = rng.choice([0.0, 0.9, 1.3], B)
+    K = rng.choice([1, 20, 50], B).astype(np.int32)
+    P = rng.choice([0.95, 0.7, 1.0], B)
+    U = rng.random(B)
+    return x, T, K, P, U
+
+
+def _worker(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, T, K, P, U = _batch()
+        B, V = x.shape
+        v0, v1 = sharded.shard_bounds(V, world, rank)
+        kmax = sharded.choose_kmax(K.tolist(), T.tolist())
+        rec = sharded_ref.np_records(x[:, v0:v1], v0, V, T, K, kmax)
+        allrec = sharded.exchange_records(torch.from_numpy(rec.view(np.int32)))
+        rows = torch.tensor([0, 3, 7])
+        full = sharded.gather_rows(torch.from_numpy(x[:, v0:v1].copy()), rows, V)
+        if rank == 0:
+            out.put((allrec.numpy().view(np.uint32), full.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_exchange_and_decomposition():
+    import multiprocessing as mp
+    world = 2
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    allrec, full = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    x, T, K, P, U = _batch()
+    B, V = x.shape
+    assert allrec.shape[0] == world
+    np.testing.assert_array_equal(full, x[[0, 3, 7]])
+    kmax = sharded.choose_kmax(K.tolist(), T.tolist())
+    rows, st = sharded_ref.sparse_rows(allrec, B, V, kmax)
+    assert not st.any()
+    t_sparse = oracle.c_sample(rows, T, K, P, U)[0]
+    t_full = oracle.c_sample(x, T, K, P, U)[0]
+    np.testing.assert_array_equal(t_sparse, t_full)
