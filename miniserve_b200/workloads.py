@@ -107,6 +107,53 @@ def config3(seed: int = 3, B: int = 512, V: int = QWEN_VOCAB) -> Batch:
     return Batch("config3", x, T, k.astype(np.int32), p, uniforms_for(seeds), seeds)
 
 
+_JSON_HEAVY = '{}[]:,"\\0123456789' + "truefalsn"  # structural characters, digits, literal letters
+
+
+def json_vocab(seed: int = 4, V: int = QWEN_VOCAB):
+    """Synthetic vocabulary: V printable-ASCII strings of 1-8 characters, JSON
+    structural characters, digits and true/false/null letters 4x as likely."""
+    rng = random.Random(seed)
+    chars = [chr(c) for c in range(0x20, 0x7F)]
+    weights = [4 if c in _JSON_HEAVY else 1 for c in chars]
+    return ["".join(rng.choices(chars, weights, k=rng.randint(1, 8))) for _ in range(V)]
+
+
+def _json_value(rng: random.Random, depth: int):
+    r = rng.random()
+    if depth < 4 and r < 0.3:
+        return {f"k{rng.randint(0, 99)}": _json_value(rng, depth + 1) for _ in range(rng.randint(0, 16))}
+    if depth < 4 and r < 0.55:
+        return [_json_value(rng, depth + 1) for _ in range(rng.randint(0, 16))]
+    if r < 0.7:
+        return "".join(rng.choice('abc xyz_"\\/\n\t') for _ in range(rng.randint(0, 6)))
+    if r < 0.85:
+        return rng.choice([rng.randint(-1000, 1000), round(rng.uniform(-100, 100), rng.randint(0, 4)), 1e21, -0.5])
+    return rng.choice([True, False, None])
+
+
+def json_prefixes(seed: int = 4, B: int = 128):
+    """B seeded prefixes of seeded random JSON values (nesting depth <= 4,
+    <= 16 items per level), cut at a random length."""
+    import json
+    rng = random.Random(seed * 7919 + 1)
+    out = []
+    for _ in range(B):
+        text = json.dumps(_json_value(rng, 0), separators=(",", ":") if rng.random() < 0.5 else (", ", ": "))
+        out.append(text[: rng.randint(0, len(text))])
+    return out
+
+
+def config4(seed: int = 4, B: int = 128, V: int = QWEN_VOCAB) -> Batch:
+    """JSON-grammar rows: N(0, 2^2) logits, T=0.8, p=0.95, k=0; the synthetic
+    vocabulary and prefixes ride in ``extra`` (the mask is built from them)."""
+    rng = np.random.default_rng(seed)
+    x = rng.normal(0.0, 2.0, (B, V)).astype(np.float32)
+    seeds = row_seeds(seed, B)
+    return Batch("config4", x, np.full(B, 0.8), np.zeros(B, np.int32), np.full(B, 0.95), uniforms_for(seeds),
+                 seeds, extra={"vocab": json_vocab(seed, V), "prefixes": json_prefixes(seed, B)})
+
+
 def config5(seed: int = 5, B: int = 1024, V: int = 256000) -> Batch:
     """Vocab-sharded large vocab: Zipf logits; k=50, p=0.95, T=0.9."""
     rng = np.random.default_rng(seed)

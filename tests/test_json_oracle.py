@@ -1,0 +1,76 @@
+"""The JSON prefix oracle (oracle/json_prefix.py) against the reference's own
+answers: the committed golden vectors (tests/golden/json_prefix_golden.json,
+made by tests/golden/make_json_golden.py from miniserve's
+JSONLogitsProcessor.is_valid_prefix, miniserve/sampler.py:139-148), and, where
+the reference tree is present, a fresh fuzz against it."""
+import json
+import os
+import random
+import sys
+
+import pytest
+
+from oracle import json_prefix as jp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _golden():
+    with open(os.path.join(HERE, "golden", "json_prefix_golden.json")) as f:
+        return json.load(f)
+
+
+def test_oracle_matches_golden_cases():
+    g = _golden()
+    bad = [(s, a) for s, a in g["cases"] if jp.is_valid_prefix(s) != a]
+    assert not bad, bad[:10]
+    assert len(g["cases"]) > 5000
+
+
+def test_oracle_matches_golden_long_probes():
+    for h, u, n, t, a in _golden()["long"]:
+        assert jp.is_valid_prefix(h + u * n + t) == a, (h, u, n, t, a)
+
+
+def test_known_answers():
+    # the probes of the reference's behaviour that decide the mask's classes
+    assert jp.is_valid_prefix("") is True
+    assert jp.is_valid_prefix(" {x") is True          # leading space: parsed, "Expecting property name"
+    assert jp.is_valid_prefix("{anything") is True    # raw first character '{'
+    assert jp.is_valid_prefix("[1,]") is True         # "Expecting value"
+    assert jp.is_valid_prefix("1.") is False          # "Extra data"
+    assert jp.is_valid_prefix("01") is False
+    assert jp.is_valid_prefix("true,") is False
+    assert jp.is_valid_prefix("[1]]") is False
+    assert jp.is_valid_prefix('"\\q') is False         # "Invalid \\escape"
+    assert jp.is_valid_prefix('"\\u0041') is False     # four digits need one more character
+    assert jp.is_valid_prefix('"\\u0041x') is True
+    assert jp.is_valid_prefix('"\x01') is False        # "Invalid control character at"
+    assert jp.is_valid_prefix("nulx") is True
+    assert jp.is_valid_prefix("-Infinity") is True
+
+
+def test_pack_mask_layout():
+    words = jp.pack_mask([True, False, True] + [False] * 29 + [True])
+    assert words.tolist() == [0b101, 1]
+
+
+def test_fuzz_against_live_reference():
+    ref = os.environ.get("MINISERVE_REF", "/root/reference")
+    if not os.path.exists(os.path.join(ref, "miniserve", "sampler.py")):
+        pytest.skip("reference tree not present (the golden vectors pin the oracle)")
+    sys.path.insert(0, ref)
+    from miniserve.sampler import JSONLogitsProcessor
+    f = JSONLogitsProcessor().is_valid_prefix
+    rng = random.Random(7)
+    alpha = list('{}[]:,"\\ \t\n\r0123456789.-+eEtrufalsenNIyi') + [
+        "\\u", "\\ud834", "true", "null", "NaN", "-Infinity", "\x01", "é"]
+    for _ in range(20000):
+        s = "".join(rng.choice(alpha) for _ in range(rng.randint(0, 14)))
+        if rng.random() < 0.3:
+            s = "[" + s
+        try:
+            want = f(s)
+        except (RecursionError, ValueError):
+            want = jp.RAISE
+        assert jp.is_valid_prefix(s) == want, repr(s)
