@@ -138,6 +138,39 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
                    const double *uniforms, int64_t *tokens, float *probs, int32_t *row_status,
                    ms_stream_t stream);
 
+/*
+ * JSON-grammar allowed-token mask: bit t of a row is
+ * JSONLogitsProcessor.is_valid_prefix(prefix + vocab[t])
+ * (miniserve/sampler.py:139-148; the allowed_token_ids(partial, vocab) the
+ * reference names at sampler.py:120), with is_valid_prefix's answers as
+ * CPython 3.12's json decoder gives them.  No counterpart computes this mask
+ * in the reference.
+ *
+ * A row's parse state (ms_json_state_words() 32-bit words) lives in a
+ * caller-owned device buffer [B][words]:
+ *   ms_json_init     the state after each row's prefix: text r is
+ *                    prefix_bytes[prefix_off[r] .. prefix_off[r+1]) (UTF-8)
+ *   ms_json_advance  append token tokens[r] (< 0: nothing) of the vocabulary
+ *                    to row r, e.g. the token just sampled
+ *   ms_build_json_mask
+ *                    mask [B, mask_ld] u32, bit (t & 31) of word (t >> 5) set
+ *                    when token t may follow (the layout ms_sample's mask
+ *                    takes).  row_status bit 1: some token makes the
+ *                    reference raise instead (an integer of more than 4300
+ *                    digits, or 9997 nested containers), bit 2: some token
+ *                    opens or closes more than 64 containers beyond the row's
+ *                    own; those tokens' bits are 0.
+ * The vocabulary is vocab_bytes[vocab_off[t] .. vocab_off[t+1]) (UTF-8), with
+ * vocab_off an int64 array of V + 1 entries.  B <= 65535 for the mask.
+ */
+int64_t ms_json_state_words(void);
+int ms_json_init(const uint8_t *prefix_bytes, const int64_t *prefix_off, int64_t B, uint32_t *states,
+                 ms_stream_t stream);
+int ms_json_advance(uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                    int64_t V, const int64_t *tokens, ms_stream_t stream);
+int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream);
+
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);
 

@@ -38,6 +38,10 @@ SIGNATURES = {
     "ms_shard_record_words": (_I64, [ctypes.c_int32]),
     "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,
                                       _P, _P, _P, _P]),
+    "ms_json_state_words": (_I64, []),
+    "ms_json_init": (ctypes.c_int, [_P, _P, _I64, _P, _P]),
+    "ms_json_advance": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P]),
+    "ms_build_json_mask": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _P]),
     "ms_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ms_last_cuda_error": (ctypes.c_int, []),
     "ms_version": (ctypes.c_int, []),

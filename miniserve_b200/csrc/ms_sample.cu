@@ -18,6 +18,7 @@
 
 #include "ms_common.cuh"
 #include "ms_generic.cuh"
+#include "ms_json.cuh"
 #include "ms_shard.cuh"
 #include "ms_stream.cuh"
 
@@ -170,6 +171,53 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;
+}
+
+int64_t ms_json_state_words(void) { return ms::kJsonStateWords; }
+
+int ms_json_init(const uint8_t *prefix_bytes, const int64_t *prefix_off, int64_t B, uint32_t *states,
+                 ms_stream_t stream) {
+  if (B < 0) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!prefix_bytes || !prefix_off || !states) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((B + 127) / 128);
+  ms::ms_json_feed_kernel<<<grid, 128, 0, s>>>(states, B, prefix_bytes, prefix_off, B, nullptr, 1);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_json_advance(uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                    int64_t V, const int64_t *tokens, ms_stream_t stream) {
+  if (B < 0 || V < 1) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!states || !vocab_bytes || !vocab_off || !tokens) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((B + 127) / 128);
+  ms::ms_json_feed_kernel<<<grid, 128, 0, s>>>(states, B, vocab_bytes, vocab_off, V, tokens, 0);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
+  if (B < 0 || B > 65535 || V < 1 || V > 0x7FFFFFFFll || mask_ld < (V + 31) / 32) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!states || !vocab_bytes || !vocab_off || !mask || !row_status) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(row_status, 0, (size_t)B * sizeof(int32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  // about eight CTAs per SM over all rows; every warp of a CTA at least one word
+  const int64_t nwords = (V + 31) / 32;
+  int64_t x = (1184 + B - 1) / B;
+  x = x < 1 ? 1 : x;
+  const int64_t xmax = (nwords + ms::kJsonThreads / 32 - 1) / (ms::kJsonThreads / 32);
+  x = x > xmax ? xmax : x;
+  ms::JsonVocab voc{vocab_bytes, vocab_off, V};
+  ms::ms_json_mask_kernel<<<dim3((unsigned)x, (unsigned)B), ms::kJsonThreads, 0, s>>>(states, voc, mask, mask_ld,
+                                                                                       row_status);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
 
 }  // extern "C"

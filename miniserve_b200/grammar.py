@@ -1,0 +1,75 @@
+"""JSON-grammar allowed-token masks on the GPU.
+
+``allowed[b][t] = is_valid_prefix(prefix_b + vocab[t])`` for miniserve's
+``JSONLogitsProcessor.is_valid_prefix`` (miniserve/sampler.py:139-148), the
+``allowed_token_ids(partial, vocab)`` the reference names at sampler.py:120.
+Each row keeps a parse state on the device (``init`` from the prefixes,
+``advance`` by the token just sampled); ``build`` evaluates every token of the
+vocabulary against it and returns the [B, ceil(V/32)] bitmask that
+``Sampler.sample_batch(..., mask=...)`` applies.
+"""
+from __future__ import annotations
+
+from typing import Sequence, Tuple
+
+from . import _lib
+from .sampler import _torch
+
+ROW_RAISES = 1      # some token makes the reference raise (its bit is 0)
+ROW_TOKEN_DEEP = 2  # some token opens/closes more than 64 containers beyond the row's (its bit is 0)
+
+
+def _pack_texts(texts: Sequence[str], device):
+    torch = _torch()
+    blobs = [t.encode("utf-8") for t in texts]
+    off = [0]
+    for b in blobs:
+        off.append(off[-1] + len(b))
+    data = b"".join(blobs) or b"\0"
+    by = torch.frombuffer(bytearray(data), dtype=torch.uint8).to(device)
+    return by, torch.tensor(off, dtype=torch.int64, device=device)
+
+
+class JsonMaskBuilder:
+    """Masks over a fixed vocabulary (a list of token strings)."""
+
+    def __init__(self, vocab: Sequence[str], device="cuda") -> None:
+        torch = _torch()
+        self.device = torch.device(device)
+        self.V = len(vocab)
+        self.vocab_bytes, self.vocab_off = _pack_texts(vocab, self.device)
+        self.words = int(_lib.lib().ms_json_state_words())
+
+    def _stream(self):
+        return _torch().cuda.current_stream(self.device).cuda_stream
+
+    def init(self, prefixes: Sequence[str]):
+        """Parse states [B, words] (int32) after each row's prefix."""
+        torch = _torch()
+        B = len(prefixes)
+        by, off = _pack_texts(prefixes, self.device)
+        states = torch.empty((B, self.words), dtype=torch.int32, device=self.device)
+        rc = _lib.lib().ms_json_init(by.data_ptr(), off.data_ptr(), B, states.data_ptr(), self._stream())
+        _lib.check(rc, "ms_json_init")
+        return states
+
+    def advance(self, states, tokens) -> None:
+        """Append token tokens[b] (int64 ids, < 0: none) to row b, in place."""
+        torch = _torch()
+        t = torch.as_tensor(tokens, dtype=torch.int64, device=self.device)
+        rc = _lib.lib().ms_json_advance(states.data_ptr(), states.shape[0], self.vocab_bytes.data_ptr(),
+                                        self.vocab_off.data_ptr(), self.V, t.data_ptr(), self._stream())
+        _lib.check(rc, "ms_json_advance")
+
+    def build(self, states, out=None) -> Tuple["object", "object"]:
+        """(mask [B, ceil(V/32)] int32, row_status [B] int32)."""
+        torch = _torch()
+        B = states.shape[0]
+        W = (self.V + 31) // 32
+        mask = torch.empty((B, W), dtype=torch.int32, device=self.device) if out is None else out
+        status = torch.empty(B, dtype=torch.int32, device=self.device)
+        rc = _lib.lib().ms_build_json_mask(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
+                                           self.vocab_off.data_ptr(), self.V, mask.data_ptr(), mask.stride(0),
+                                           status.data_ptr(), self._stream())
+        _lib.check(rc, "ms_build_json_mask")
+        return mask, status

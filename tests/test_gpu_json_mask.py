@@ -1,0 +1,126 @@
+"""The GPU JSON-grammar mask against the oracle (oracle/json_prefix.py, pinned
+to miniserve's is_valid_prefix) and the reference's golden answers; then the
+masked sampling of config 4 against the C oracle.  Needs a B200."""
+import json
+import os
+import random
+
+import numpy as np
+import pytest
+
+from oracle import json_prefix as jp
+from parity import compare
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.fixture(scope="module")
+def torch():
+    t = pytest.importorskip("torch")
+    if not t.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    return t
+
+
+def _bits(mask_row, V):
+    w = np.asarray(mask_row).view(np.uint32)
+    return ((w[:, None] >> np.arange(32, dtype=np.uint32)) & 1).reshape(-1)[:V].astype(bool)
+
+
+def test_golden_strings_split_at_every_point(torch):
+    """Each golden string, split into (prefix, token) at several points, gives
+    the reference's answer (a raise gives bit 0 and row status 1)."""
+    from miniserve_b200.grammar import JsonMaskBuilder
+    with open(os.path.join(HERE, "golden", "json_prefix_golden.json")) as f:
+        cases = json.load(f)["cases"]
+    rng = random.Random(5)
+    pairs = []
+    for s, a in cases:
+        for k in sorted({0, len(s), rng.randint(0, len(s))}):
+            pairs.append((s[:k], s[k:], a))
+    # one row per distinct prefix, the tokens as the vocabulary
+    tokens = sorted({t for _, t, _ in pairs})
+    tid = {t: i for i, t in enumerate(tokens)}
+    prefixes = sorted({p for p, _, _ in pairs})
+    pid = {p: i for i, p in enumerate(prefixes)}
+    b = JsonMaskBuilder(tokens)
+    bad = []
+    for lo in range(0, len(prefixes), 4096):
+        chunk = prefixes[lo:lo + 4096]
+        mask, st = b.build(b.init(chunk))
+        torch.cuda.synchronize()
+        m = mask.cpu().numpy()
+        for p, t, a in pairs:
+            i = pid[p] - lo
+            if 0 <= i < len(chunk):
+                got = bool(_bits(m[i], len(tokens))[tid[t]])
+                if got != (a is True):
+                    bad.append((p, t, a))
+    assert not bad, bad[:10]
+
+
+def test_config4_masks_vs_oracle(torch):
+    """Config-4 rows: full-vocabulary masks for the short prefixes, sampled
+    tokens for the long ones."""
+    from miniserve_b200 import workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    V = 151936
+    vocab = workloads.json_vocab(4, V)
+    prefixes = workloads.json_prefixes(4, 128)
+    b = JsonMaskBuilder(vocab)
+    mask, st = b.build(b.init(prefixes))
+    torch.cuda.synchronize()
+    m = mask.cpu().numpy()
+    assert not st.cpu().numpy().any()
+    rng = random.Random(11)
+    checked = 0
+    full_rows = 0
+    for r, p in enumerate(prefixes):
+        bits = _bits(m[r], V)
+        if len(p) <= 8 and full_rows < 12:
+            full_rows += 1
+            idx = range(V)
+        else:
+            idx = rng.sample(range(V), 300 if len(p) < 2000 else 40)
+        for t in idx:
+            want = jp.is_valid_prefix(p + vocab[t]) is True
+            assert bits[t] == want, (r, p[-30:], vocab[t], want)
+            checked += 1
+    assert checked > 10 * V
+
+
+def test_advance_matches_init(torch):
+    """State after prefix + sampled token == state built from the joined text."""
+    from miniserve_b200 import workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    vocab = workloads.json_vocab(4, 4096)
+    prefixes = [p for p in workloads.json_prefixes(4, 128) if len(p) < 600][:48]
+    b = JsonMaskBuilder(vocab)
+    rng = np.random.default_rng(2)
+    toks = rng.integers(0, len(vocab), len(prefixes))
+    s1 = b.init(prefixes)
+    b.advance(s1, torch.from_numpy(toks))
+    s2 = b.init([p + vocab[t] for p, t in zip(prefixes, toks)])
+    m1, _ = b.build(s1)
+    m2, _ = b.build(s2)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(m1.cpu().numpy(), m2.cpu().numpy())
+
+
+def test_config4_masked_sampling(torch):
+    """Config 4 end to end: masks on the GPU, masked sampling vs the C oracle
+    with the same mask."""
+    from miniserve_b200 import Sampler, workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    cfg = workloads.config4(4, B=128)
+    b = JsonMaskBuilder(cfg.extra["vocab"])
+    mask, st = b.build(b.init(cfg.extra["prefixes"]))
+    x = torch.from_numpy(cfg.logits).cuda()
+    tok, prob, status = Sampler().sample_batch(x, cfg.temperature, cfg.top_k, cfg.top_p, uniforms=cfg.uniforms,
+                                               mask=mask)
+    torch.cuda.synchronize()
+    compare(tok.cpu().numpy(), prob.cpu().numpy().astype(np.float64), status.cpu().numpy(), cfg.logits,
+            cfg.temperature, cfg.top_k, cfg.top_p, cfg.uniforms, mask=mask.cpu().numpy().view(np.uint32),
+            label="config4 masked")
