@@ -298,6 +298,154 @@ def run_ours(args, rank, world, local_rank):
     }
 
 
+# ------------------------------------------------------- other BASELINE configs
+def _time_ms(step, steps, warmup, stream, world):
+    """Device ms per step: CUDA events on the launching stream, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()) / steps
+
+
+def run_workload(args, rank, world, local_rank):
+    """--workload config2 / config4 / config5: the BASELINE configurations other
+    than the metric's, device-timed (one JSON line, rank 0)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from miniserve_b200 import _lib, sharded, workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    peak, _ = hbm_peak()
+    out = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+           "vs_baseline": None, "data": "synthetic (seeded; BASELINE.json configuration)"}
+    clocks = ClockSampler(local_rank).__enter__()
+    clocks.wait_first()
+    if args.workload == "config2":
+        b = workloads.config2(2 + rank)
+        B, V = b.B, b.V
+        esz = 2 if args.bf16 else 4
+        x = torch.from_numpy(b.logits).to(dev)
+        if args.bf16:
+            x = x.to(torch.bfloat16)
+        T, K, P, U = (torch.from_numpy(a).to(dev) for a in (b.temperature, b.top_k, b.top_p, b.uniforms))
+        tok = torch.empty(B, dtype=torch.int64, device=dev)
+        prob = torch.empty(B, dtype=torch.float32, device=dev)
+        st = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def step():
+            _lib.check(L.ms_sample(x.data_ptr(), 1 if args.bf16 else 0, B, V, V, T.data_ptr(), K.data_ptr(),
+                                   P.data_ptr(), U.data_ptr(), None, 0, tok.data_ptr(), prob.data_ptr(),
+                                   st.data_ptr(), sptr), "ms_sample")
+        ms = _time_ms(step, args.steps, args.warmup, stream, world)
+        alg = B * (V * esz + 52)
+        out.update(metric="logits rows sampled/sec at 256x151936 greedy + temperature (config 2)",
+                   value=round(world * B / (ms / 1e3), 1), unit="rows/s", ms_per_step=round(ms, 5),
+                   scaling="weak", dtype="bf16" if args.bf16 else "f32",
+                   config={"workload": "config2", "batch_rows": B, "vocab": V},
+                   roofline={"bound": "hbm", "achieved": round(alg / (ms / 1e3) / 1e9, 1), "peak": peak,
+                             "unit": "GB/s", "frac": round(alg / (ms / 1e3) / 1e9 / peak, 4), "traffic": None})
+    elif args.workload == "config4":
+        b = workloads.config4(4 + rank)
+        B, V = b.B, b.V
+        builder = JsonMaskBuilder(b.extra["vocab"], device=dev)
+        states = builder.init(b.extra["prefixes"])
+        x = torch.from_numpy(b.logits).to(dev)
+        T, K, P, U = (torch.from_numpy(a).to(dev) for a in (b.temperature, b.top_k, b.top_p, b.uniforms))
+        W = (V + 31) // 32
+        mask = torch.empty((B, W), dtype=torch.int32, device=dev)
+        mst = torch.empty(B, dtype=torch.int32, device=dev)
+        tok = torch.empty(B, dtype=torch.int64, device=dev)
+        prob = torch.empty(B, dtype=torch.float32, device=dev)
+        st = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def build():
+            _lib.check(L.ms_build_json_mask(states.data_ptr(), B, builder.vocab_bytes.data_ptr(),
+                                            builder.vocab_off.data_ptr(), V, mask.data_ptr(), W, mst.data_ptr(),
+                                            sptr), "ms_build_json_mask")
+
+        def sample():
+            _lib.check(L.ms_sample(x.data_ptr(), 0, B, V, V, T.data_ptr(), K.data_ptr(), P.data_ptr(),
+                                   U.data_ptr(), mask.data_ptr(), W, tok.data_ptr(), prob.data_ptr(),
+                                   st.data_ptr(), sptr), "ms_sample")
+
+        def step():
+            build()
+            sample()
+        ms_build = _time_ms(build, args.steps, args.warmup, stream, world)
+        ms_sample = _time_ms(sample, args.steps, args.warmup, stream, world)
+        ms = _time_ms(step, args.steps, args.warmup, stream, world)
+        alg = B * (V * 4 + 4 * W + 52)
+        out.update(metric="JSON-grammar rows sampled/sec at 128x151936 (config 4: mask build + masked sampling)",
+                   value=round(world * B / (ms / 1e3), 1), unit="rows/s", ms_per_step=round(ms, 5),
+                   scaling="weak", dtype="f32",
+                   config={"workload": "config4", "batch_rows": B, "vocab": V,
+                           "vocab_bytes": int(builder.vocab_bytes.numel()),
+                           "prefix_chars": int(sum(len(p) for p in b.extra["prefixes"]))},
+                   mask_build_us=round(ms_build * 1e3, 2), masked_sample_us=round(ms_sample * 1e3, 2),
+                   roofline={"bound": "hbm", "kernel": "masked sampling",
+                             "achieved": round(alg / (ms_sample / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(alg / (ms_sample / 1e3) / 1e9 / peak, 4), "traffic": None})
+    else:  # config5: vocab-sharded over the ranks
+        b = workloads.config5(5)
+        B, V = b.B, b.V
+        v0, v1 = sharded.shard_bounds(V, world, rank)
+        x = torch.from_numpy(np.ascontiguousarray(b.logits[:, v0:v1])).to(dev)
+        del b.logits
+        T, K, P, U = (torch.from_numpy(a).to(dev) for a in (b.temperature, b.top_k, b.top_p, b.uniforms))
+        kmax = 50
+        Wr = sharded.record_words(kmax)
+        rec = torch.empty((B, Wr), dtype=torch.int32, device=dev)
+        allrec = torch.empty((world * B, Wr), dtype=torch.int32, device=dev)
+        tok = torch.empty(B, dtype=torch.int64, device=dev)
+        prob = torch.empty(B, dtype=torch.float32, device=dev)
+        st = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def step():
+            _lib.check(L.ms_shard_candidates(x.data_ptr(), 0, B, v1 - v0, v1 - v0, v0, V, T.data_ptr(),
+                                             K.data_ptr(), None, 0, kmax, rec.data_ptr(), sptr),
+                       "ms_shard_candidates")
+            if world > 1:
+                dist.all_gather_into_tensor(allrec, rec)
+                src = allrec
+            else:
+                src = rec
+            _lib.check(L.ms_shard_merge(src.data_ptr(), world, B, kmax, V, T.data_ptr(), K.data_ptr(),
+                                        P.data_ptr(), U.data_ptr(), tok.data_ptr(), prob.data_ptr(),
+                                        st.data_ptr(), sptr), "ms_shard_merge")
+        ms = _time_ms(step, args.steps, args.warmup, stream, world)
+        alg = B * ((v1 - v0) * 4 + 52)
+        out.update(metric="logits rows sampled/sec at 1024x256000, vocab sharded over the GPUs (config 5)",
+                   value=round(B / (ms / 1e3), 1), unit="rows/s", ms_per_step=round(ms, 5), scaling="strong",
+                   dtype="f32", config={"workload": "config5", "batch_rows": B, "vocab": V,
+                                        "parallelism": f"vocab slices x{world}", "kmax": kmax,
+                                        "gather_bytes_per_rank": B * Wr * 4},
+                   roofline={"bound": "hbm", "per_gpu": True, "achieved": round(alg / (ms / 1e3) / 1e9, 1),
+                             "peak": peak, "unit": "GB/s", "frac": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+                             "traffic": None})
+    clocks.__exit__(None, None, None)
+    out["clocks"] = clocks.summary()
+    return out if rank == 0 else None
+
+
 def launches_per_call():
     """ms_sample launches the streaming kernel and the pending-row pass."""
     return 2
@@ -347,6 +495,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["config3", "config2", "config4", "config5"], default="config3",
+                    help="config3 (default) is the metric's configuration; the others print their own line")
+    ap.add_argument("--bf16", action="store_true", help="config2: bf16 logits")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -365,7 +516,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        out = run_ours(args, rank, world, local_rank)
+        out = run_ours(args, rank, world, local_rank) if args.workload == "config3" else \
+            run_workload(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

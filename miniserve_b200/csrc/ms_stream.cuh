@@ -225,7 +225,7 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
 template <int DT>
 __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
   const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
-  if (!r.mask && tma_elems(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
+  if (tma_elems(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
     if (DT == MS_DTYPE_F32) {
       const float4 *p = reinterpret_cast<const float4 *>(sh.stage[s]);
       const float4 f0 = p[j >> 2], f1 = p[(j + 128) >> 2];
@@ -248,6 +248,15 @@ __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c
       x[5] = __uint_as_float(h1.x & 0xFFFF0000u);
       x[6] = __uint_as_float(h1.y << 16);
       x[7] = __uint_as_float(h1.y & 0xFFFF0000u);
+    }
+    if (r.mask) {  // each group of 4 lies in one 32-bit mask word
+      const int g0 = c * kChunk + j, g1 = g0 + 128;
+      const uint32_t m0 = __ldg(r.mask + (g0 >> 5)) >> (g0 & 31), m1 = __ldg(r.mask + (g1 >> 5)) >> (g1 & 31);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (!((m0 >> e) & 1u)) x[e] = -INFINITY;
+        if (!((m1 >> e) & 1u)) x[4 + e] = -INFINITY;
+      }
     }
   } else {
     st_get4<DT>(sh, r, c, s, j, x);
