@@ -661,9 +661,9 @@ struct StW {
     if (!(c_lo > 0.0f)) c_lo = 1.17549435e-38f;  // c exact in fp32: a negligible positive tail
   }
   __device__ __forceinline__ void set_m(float M) {
-    const double mc = (double)M * (double)c_hi;  // exact: 24 x 24 bits
-    mc_hi = (float)mc;
-    mc_lo = (float)(mc - (double)mc_hi) + (float)((double)M * (double)c_lo);
+    mc_hi = M * c_hi;
+    const float e = fmaf(M, c_hi, -mc_hi);  // the product's rounding error, exactly
+    mc_lo = fmaf(M, c_lo, e);
   }
   __device__ __forceinline__ float operator()(float v) const {
     return st_ex2(fmaf(v, c_hi, -mc_hi) + fmaf(v, c_lo, -mc_lo));
@@ -1388,24 +1388,22 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     StW Wu = W;
     Wu.set_m(mu);
     const StW2 W2(Wu);
-    f2_t all2 = f2_pack(0.0f, 0.0f), ab2 = all2;
-    bool any_in = false;
+    float all = 0.0f, above = 0.0f;
+    uint32_t in_any = 0u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float xa = x[2 * j], xb = x[2 * j + 1];
-      const f2_t Wp = W2(f2_pack(xa, xb));  // -inf weighs 0
-      all2 = f2_add(all2, Wp);
       float wa, wb;
-      f2_unpack(Wp, wa, wb);
+      f2_unpack(W2(f2_pack(xa, xb)), wa, wb);  // -inf weighs 0
+      all += wa + wb;
       const bool aa = xa > v_lo, ab = xb > v_lo;
-      ab2 = f2_add(ab2, f2_pack(aa ? wa : 0.0f, ab ? wb : 0.0f));
-      any_in |= (!aa && xa > v_hi) || (!ab && xb > v_hi);
+      above += (aa ? wa : 0.0f) + (ab ? wb : 0.0f);
+      in_any |= (uint32_t)(xa > v_hi) & (uint32_t)!aa;
+      in_any |= (uint32_t)(xb > v_hi) & (uint32_t)!ab;
     }
-    float s0, s1, t0, t1;
-    f2_unpack(ab2, s0, s1);
-    f2_unpack(all2, t0, t1);
-    const float above = warp_sum_f(s0 + s1);
-    const float all = warp_sum_f(t0 + t1);
+    const bool any_in = in_any != 0u;
+    above = warp_sum_f(above);
+    all = warp_sum_f(all);
     if (lane == 0) {
       sh.w.n.s[u] = above;
       zacc += (double)all * (double)sh.w.n.f[u];
