@@ -87,7 +87,7 @@ struct StShared {
   int wcnt[2][kStWarps];  // per-warp insert counts of the last two chunks
   int pick[kStWarps][4];  // row ordering: per-warp class counts
   int ptot[4];
-  uint32_t hist256[256];
+  alignas(16) uint32_t sel[4][256];  // st_select_kth: one digit histogram per round
   unsigned long long full[kStages];
   double redd[33];
   uint32_t redu[33];
@@ -132,24 +132,31 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
-// Bytes of chunk c delivered by TMA (a multiple of 16); elements past them
-// (at most 3 fp32 / 7 bf16 at the row's end) are read from global memory.
+template <int DT>
+__host__ __device__ constexpr int st_esz() {
+  return DT == MS_DTYPE_F32 ? 4 : 2;
+}
+
+// Elements of chunk c delivered by TMA (a multiple of 16 bytes); elements past
+// them (at most 3 fp32 / 7 bf16 at the row's end) are read from global memory.
+template <int DT>
 __device__ __forceinline__ int tma_elems(const StRow &r, int c) {
   if (!r.tma) return 0;
   const int ne = min(kChunk, r.V - c * kChunk);
-  return ((ne * r.esz) & ~15) / r.esz;
+  return ne & -(16 / st_esz<DT>());
 }
 
 // thread 0: start the copy of chunk c into stage s
+template <int DT>
 __device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, int s, uint64_t pol) {
-  const uint32_t bytes = (uint32_t)(tma_elems(r, c) * r.esz);
+  const uint32_t bytes = (uint32_t)(tma_elems<DT>(r, c) * st_esz<DT>());
   const uint32_t mb = st_smem(&sh.full[s]);
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(bytes) : "memory");
   if (bytes) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
             st_smem(sh.stage[s])),
-        "l"(r.g + (int64_t)c * kChunk * r.esz), "r"(bytes), "r"(mb), "l"(pol)
+        "l"(r.g + (int64_t)c * kChunk * st_esz<DT>()), "r"(bytes), "r"(mb), "l"(pol)
         : "memory");
   }
 }
@@ -158,14 +165,18 @@ __device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, in
 __device__ __forceinline__ bool st_wait(StShared &sh, int s, uint32_t parity) {
   const uint32_t mb = st_smem(&sh.full[s]);
   uint32_t done = 0;
-  const uint64_t t0 = st_ns();
+  uint64_t t0 = 0;  // the clock is read only once the wait has spun a while
   for (uint32_t it = 0; !done; ++it) {
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
         : "=r"(done)
         : "r"(mb), "r"(parity)
         : "memory");
-    if (!done && (it & 1023u) == 1023u && st_ns() - t0 > 1000000000ull) return false;
+    if (!done && (it & 1023u) == 1023u) {
+      const uint64_t t = st_ns();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) return false;
+    }
   }
   return true;
 }
@@ -176,7 +187,7 @@ template <int DT>
 __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int c, int s, int j,
                                         float x[4]) {
   const int ne = min(kChunk, r.V - c * kChunk);
-  const int nt = tma_elems(r, c);
+  const int nt = tma_elems<DT>(r, c);
   if (j + 4 <= nt) {
     if (DT == MS_DTYPE_F32) {
       const float4 f = reinterpret_cast<const float4 *>(sh.stage[s])[j >> 2];
@@ -225,7 +236,7 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
 template <int DT>
 __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
   const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
-  if (tma_elems(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
+  if (tma_elems<DT>(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
     if (DT == MS_DTYPE_F32) {
       const float4 *p = reinterpret_cast<const float4 *>(sh.stage[s]);
       const float4 f0 = p[j >> 2], f1 = p[(j + 128) >> 2];
@@ -264,6 +275,24 @@ __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c
   }
   return c * kChunk + j;
 }
+// Maxima that let a NaN through (max.NaN), so one running maximum both finds
+// the row's largest value and flags a NaN; a row holding NaN or +inf
+// (st_bad) leaves the fast paths.
+__device__ __forceinline__ float st_maxn(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float st_max3n(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float st_max8n(const float *x) {
+  return st_max3n(st_max3n(x[0], x[1], x[2]), st_max3n(x[3], x[4], x[5]), st_maxn(x[6], x[7]));
+}
+__device__ __forceinline__ bool st_bad(float running_max) { return !(running_max < INFINITY); }
+
 // global index of x[e] given that of x[0]
 __device__ __forceinline__ int st_gidx(int g0, int e) { return e < 4 ? g0 + e : g0 + 124 + e; }
 
@@ -276,7 +305,7 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
   const int tid = threadIdx.x;
   bool ok = true;
   if (tid == 0) {
-    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol);
+    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol);
   }
   for (int c = 0; c < r.nchunks; ++c) {
     const int s = c % kStages;
@@ -288,7 +317,7 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && c + kStages < r.nchunks) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      st_issue(sh, r, c + kStages, s, pol);
+      st_issue<DT>(sh, r, c + kStages, s, pol);
     }
   }
   return __syncthreads_and(ok) != 0;
@@ -301,71 +330,76 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 }
 
 // --------------------------------------------------------- block selection
-// k-th largest (1-based) among n keys in shared memory, keys with a 0
-// "invalid" marker excluded by the caller.  Returns the key; *n_above gets
-// the number of keys strictly above it.  4 passes of 8-bit digits.
+// The k-th largest of n keys (1 <= k <= n), by four rounds of 8-bit digits;
+// *n_above = the keys strictly above it.  Each round has its own histogram
+// (cleared up front), and every warp scans it for itself, so a round costs
+// one barrier.  All threads.
 __device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int k, int *n_above) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  __syncthreads();  // no warp still scans the histograms of an earlier call
+  for (int b = tid; b < 4 * 256; b += kStThreads) (&sh.sel[0][0])[b] = 0u;
+  __syncthreads();
   uint32_t prefix = 0;
   int rem = k, above = 0;
   for (int d = 0; d < 4; ++d) {
     const int shift = 24 - 8 * d;
-    for (int b = tid; b < 256; b += kStThreads) sh.hist256[b] = 0u;
-    __syncthreads();
-    // keys share leading digits heavily: one atomic per distinct digit per warp
+    uint32_t *h = sh.sel[d];
     for (int i0 = 0; i0 < n; i0 += kStThreads) {
       const int i = i0 + tid;
       const uint32_t key = i < n ? keys[i] : 0u;
       const bool in = i < n && (d == 0 || (key >> (shift + 8)) == prefix);
+      const uint32_t digit = (key >> shift) & 255u;
+      // keys share leading digits heavily: the first active lane's digit
+      // takes one atomic for every lane that holds it
       const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
-      if (in) {
-        const uint32_t digit = (key >> shift) & 255u;
-        const unsigned same = __match_any_sync(act, digit);
-        if ((tid & 31) == __ffs(same) - 1) atomicAdd(&sh.hist256[digit], (uint32_t)__popc(same));
+      if (act) {
+        const int first = __ffs(act) - 1;
+        const uint32_t lead = __shfl_sync(0xFFFFFFFFu, digit, first);
+        const unsigned same = __ballot_sync(0xFFFFFFFFu, in && digit == lead);
+        if (lane == first) {
+          atomicAdd(&h[lead], (uint32_t)__popc(same));
+        } else if (in && digit != lead) {
+          atomicAdd(&h[digit], 1u);
+        }
       }
     }
     __syncthreads();
-    // digit whose running count from the top reaches rem
-    if (tid < 32) {
-      // each lane owns 8 digits, highest digits on lane 0
-      uint32_t c8[8], s = 0;
+    // every warp: the digit whose running count from the top reaches rem;
+    // lane l holds digits 255 - 8l - q, q = 0..7
+    const uint4 *h4 = reinterpret_cast<const uint4 *>(h);
+    const uint4 lo = h4[(248 - 8 * lane) >> 2], hi = h4[((248 - 8 * lane) >> 2) + 1];
+    const uint32_t c8[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
+    uint32_t s8 = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s8 += c8[q];
+    uint32_t incl = s8;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - s8;
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= (uint32_t)rem && excl < (uint32_t)rem);
+    uint32_t dig = 0, before = 0;
+    if (hit && lane == __ffs(hit) - 1) {
+      uint32_t acc = excl;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        c8[q] = sh.hist256[255 - (tid * 8 + q)];
-        s += c8[q];
-      }
-      uint32_t incl = s;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (tid >= o) incl += y;
-      }
-      const uint32_t excl = incl - s;
-      const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= (uint32_t)rem && excl < (uint32_t)rem);
-      if (hit) {
-        const int lane = __ffs(hit) - 1;
-        if (tid == lane) {
-          uint32_t acc = excl;
-          for (int q = 0; q < 8; ++q) {
-            if (acc + c8[q] >= (uint32_t)rem) {
-              sh.bcast_i[0] = 255 - (tid * 8 + q);
-              sh.bcast_i[1] = (int)acc;
-              break;
-            }
-            acc += c8[q];
-          }
+        if (acc + c8[q] >= (uint32_t)rem) {
+          dig = 255u - (uint32_t)(8 * lane + q);
+          before = acc;
+          break;
         }
-      } else if (tid == 0) {  // fewer than rem keys: cannot happen for valid k
-        sh.bcast_i[0] = 0;
-        sh.bcast_i[1] = 0;
+        acc += c8[q];
       }
     }
-    __syncthreads();
-    const uint32_t digit = (uint32_t)sh.bcast_i[0];
-    rem -= sh.bcast_i[1];
-    above += sh.bcast_i[1];
-    prefix = (prefix << 8) | digit;
-    __syncthreads();
+    // no hit only for k > n, which callers exclude
+    const int src = hit ? __ffs(hit) - 1 : 0;
+    dig = __shfl_sync(0xFFFFFFFFu, dig, src);
+    before = __shfl_sync(0xFFFFFFFFu, before, src);
+    rem -= (int)before;
+    above += (int)before;
+    prefix = (prefix << 8) | dig;
   }
   *n_above = above;
   return prefix;
@@ -901,30 +935,22 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 
   // ================================================================ argmax
   if (mode == kStArgmax) {
-    float mv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    int mi[4] = {0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF, 0x7FFFFFFF};
-    float vsum = 0.0f;
-    // slot e & 3 sees its elements in increasing index order: strict > keeps
-    // the first maximum
+    // a thread sees its elements in increasing index order: a strictly
+    // larger chunk maximum moves the thread's best to its first occurrence
+    float tm = -INFINITY, tnan = -INFINITY;
+    int ti = 0x7FFFFFFF;
     ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int) {
+      const float cm = st_max8n(x);
+      tnan = st_maxn(tnan, cm);
+      if (cm > tm) {  // rare after the first chunks
+        int e = 7;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        vsum += x[e];
-        if (x[e] > mv[e & 3]) {
-          mv[e & 3] = x[e];
-          mi[e & 3] = st_gidx(g0, e);
-        }
+        for (int q = 6; q >= 0; --q) e = x[q] == cm ? q : e;
+        tm = cm;
+        ti = st_gidx(g0, e);
       }
     });
-    float tm = mv[0];
-    int ti = mi[0];
-#pragma unroll
-    for (int e = 1; e < 4; ++e)
-      if (mv[e] > tm || (mv[e] == tm && mi[e] < ti)) {
-        tm = mv[e];
-        ti = mi[e];
-      }
-    const bool bad = isnan(vsum) || vsum == INFINITY;
+    const bool bad = st_bad(tnan);
     uint32_t bk = tm > -INFINITY ? fkey(tm) : 0u;
     int bi = tm > -INFINITY ? ti : 0x7FFFFFFF;
     warp_argmax(bk, bi);
@@ -968,13 +994,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // candidates.  A warp with no value at or above tau skips the insert.
     float tau = -INFINITY;
     bool strict = false;
-    float rmax = -INFINITY, vsum = 0.0f;
+    float rmax = -INFINITY;  // NaN once a NaN has been seen
     const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
     bool exact_tau = false;  // tau is the k-th largest value seen (after a compaction)
     int ncand = 0;           // exact buffer size, identical in every thread
     if (tid == 0) {
-      for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_stream);
+      for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_stream);
     }
     int c = 0;
     for (; c < r.nchunks; ++c) {
@@ -983,14 +1009,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       ph ^= 1u << s;
       float x[8];
       const int g0 = st_get8<DT>(sh, r, c, s, x);
-      float cm = x[0];
-      vsum += x[0];
-#pragma unroll
-      for (int e = 1; e < 8; ++e) {
-        vsum += x[e];
-        cm = fmaxf(cm, x[e]);
-      }
-      rmax = fmaxf(rmax, cm);
+      const float cm = st_max8n(x);
+      rmax = st_maxn(rmax, cm);
       if (!exact_tau && (c < 3 || (c & 3) == 0)) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
         if (bmin != 0u && key_to_float(bmin) > tau) {
@@ -1019,11 +1039,18 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       // exact count from the per-warp slots (slot c&1 is rewritten two chunks
       // on, after a barrier every thread has passed)
       ncand += __reduce_add_sync(0xFFFFFFFFu, lane < kStWarps ? sh.wcnt[c & 1][lane] : 0);
+      // early on (chunks 3 and 11) the buffer's exact k-th largest is a far
+      // tighter tau than the warp bound and cuts the inserts of the rest of
+      // the row; entries below it stay in the buffer, dead
+      if ((c == 3 || c == 11) && ncand >= 2 * k && ncand <= kCandCap - kChunk) {
+        int above;
+        tau = key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above));
+        strict = true;  // >= k entries >= tau are held: a later equal value ranks below
+        exact_tau = true;
+      }
       // shrink to the entries >= the buffer's k-th largest (ties kept) when the
-      // next chunk could overflow the buffer, and early on (chunks 3 and 11),
-      // where the exact k-th largest so far is a far tighter tau than the
-      // warp bound and cuts the inserts of the rest of the row
-      if (ncand > kCandCap - kChunk || ((c == 3 || c == 11) && ncand >= 2 * k)) {
+      // next chunk could overflow the buffer
+      if (ncand > kCandCap - kChunk) {
         const int n0 = ncand;
         int above;
         const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
@@ -1054,7 +1081,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       if (over) break;
       if (tid == 0 && c + kStages < r.nchunks) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        st_issue(sh, r, c + kStages, s, pol_stream);
+        st_issue<DT>(sh, r, c + kStages, s, pol_stream);
       }
     }
     if (over) {
@@ -1066,7 +1093,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         ph ^= 1u << s2;
       }
     }
-    const bool bad = isnan(vsum) || vsum == INFINITY;
+    const bool bad = st_bad(rmax);
     if (__syncthreads_or(bad || !ok || over)) {
       leave(__syncthreads_or(bad) != 0);
       return;
@@ -1079,8 +1106,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       return;
     }
-    // exact top-k of the buffer; fewer valid tokens than top_k keep all
+    // exact top-k of the buffer; fewer valid tokens than top_k keep all.  thr:
+    // keys below it cannot rank in the top-k set (the buffer's k-th largest
+    // when the buffer is large, else the warp bound)
     int n = ncand;
+    uint32_t thr;
     if (n > kRankCap) {
       int above;
       const uint32_t kk = st_select_kth(sh, sh.w.c.key, n, k, &above);
@@ -1102,13 +1132,19 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       __syncthreads();
       n = ktot;
+      thr = kk;
+    } else if (n >= 2 * k) {
+      int above;
+      thr = st_select_kth(sh, sh.w.c.key, n, k, &above);
+    } else {
+      thr = st_topk_bound(sh, rmax, jw);
     }
     if (n > kRankCap) {  // a tie block larger than the rank sort: generic kernel
       leave(false);
       return;
     }
     if (shard) {  // the slice's top-k, in rank order, with global ids
-      const int m = st_topk_rank(sh, n, k, st_topk_bound(sh, rmax, jw));
+      const int m = st_topk_rank(sh, n, k, thr);
       uint32_t *rec = st_record(a, row);
       for (int i = tid; i < m; i += kStThreads) {
         rec[2 + i] = sh.w.c.key[i];
@@ -1120,7 +1156,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       return;
     }
-    st_finish_small(sh, a, row, n, k, st_topk_bound(sh, rmax, jw), T, P, U, vmax);
+    st_finish_small(sh, a, row, n, k, thr, T, P, U, vmax);
     return;
   }
 
@@ -1137,9 +1173,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     return (double)Wu(v) * (double)sh.w.n.f[u];
   };
   // after pass 1: the row maximum, or a status written and false
-  auto finish_max = [&](float vmax_t, float vsum, float &vmax) -> bool {
-    const bool bad = isnan(vsum) || vsum == INFINITY;
-    if (__syncthreads_or(bad || !ok)) {
+  auto finish_max = [&](float vmax_t, float &vmax) -> bool {
+    if (__syncthreads_or(st_bad(vmax_t) || !ok)) {
       if (tid == 0) a.status[row] = kRowPending;
       return false;
     }
@@ -1157,17 +1192,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 
   if (mode == kStFull) {
     // one pass (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
-    float vmax_t = -INFINITY;
-    f2_t vs2 = f2_pack(0.0f, 0.0f);
+    float vmax_t = -INFINITY;  // NaN once a NaN has been seen
     ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int, int u) {
       f2_t X[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        X[j] = f2_pack(x[2 * j], x[2 * j + 1]);
-        vs2 = f2_add(vs2, X[j]);
-      }
-      const float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
-      vmax_t = fmaxf(vmax_t, cm);
+      for (int j = 0; j < 4; ++j) X[j] = f2_pack(x[2 * j], x[2 * j + 1]);
+      const float cm = st_max8n(x);
+      vmax_t = st_maxn(vmax_t, cm);
       const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
       float mu = -INFINITY, su = 0.0f;
       if (km != 0u) {  // warp-uniform
@@ -1188,9 +1219,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
     });
     float vmax;
-    float vsum0, vsum1;
-    f2_unpack(vs2, vsum0, vsum1);
-    if (!finish_max(vmax_t, vsum0 + vsum1, vmax)) return;
+    if (!finish_max(vmax_t, vmax)) return;
     double zs = 0.0;
     for (int u = tid; u < nu; u += kStThreads) {
       const float mu = sh.w.n.m[u];
@@ -1224,6 +1253,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   uint32_t *hq = sh.w.n.x.hq;
   float G = -INFINITY;
   float v_high = INFINITY;  // no value at or below it lies above the grid (t < 1)
+  float v_tail = INFINITY;  // every value at or below it lies in the tail (t >= kSBins + 1)
   // Histogram of this lane's 8 values (x[4..7] sit 128 after x[0..3]), cm
   // their maximum.  Grid coordinates are packed pairs clamped to
   // [0.5, t_max]: index 0 collects the values above the grid (kept exactly in
@@ -1242,6 +1272,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         }
       }
     }
+    if (!__any_sync(0xFFFFFFFFu, cm > v_tail)) return;  // the warp's values all lie in the tail
     const f2_t G2 = f2_pack(G, G), XS2 = f2_pack(xs, xs), OFF2 = f2_pack(t_off, t_off);
     const f2_t M2 = f2_pack(8388608.0f, 8388608.0f);
     const f2_t Q0 = f2_pack(q0, q0), Q1 = f2_pack(q1, q1), Q2 = f2_pack(q2, q2);
@@ -1256,13 +1287,16 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       float tb0, tb1, qa, qb;
       f2_unpack(TB, tb0, tb1);
       f2_unpack(f2_fma(f2_fma(FR, Q2, Q1), FR, Q0), qa, qb);
-      atomicAdd(&hq[__float_as_int(tb0) - 0x4B000000], (uint32_t)(__float_as_int(qa) - 0x4B000000));
-      atomicAdd(&hq[__float_as_int(tb1) - 0x4B000000], (uint32_t)(__float_as_int(qb) - 0x4B000000));
+      // grid bins only: the high list's index 0 and the tail carry no histogram mass
+      const int i0 = __float_as_int(tb0) - 0x4B000000, i1 = __float_as_int(tb1) - 0x4B000000;
+      if ((unsigned)(i0 - 1) < (unsigned)kSBins) atomicAdd(&hq[i0], (uint32_t)(__float_as_int(qa) - 0x4B000000));
+      if ((unsigned)(i1 - 1) < (unsigned)kSBins) atomicAdd(&hq[i1], (uint32_t)(__float_as_int(qb) - 0x4B000000));
     }
   };
   auto set_anchor = [&](float g) {
     G = g;
     v_high = __double2float_rd((double)g + (double)(kUpBins - 1) / (double)xs);
+    v_tail = __double2float_rd((double)g - (double)kXBins / (double)xs);
   };
   auto hist_clear = [&]() {
     for (int i = tid; i < kQSlots; i += kStThreads) hq[i] = 0u;
@@ -1271,11 +1305,10 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   };
 
   // pass 1 (HBM, kept in L2): unit maxima, histogram anchored at chunk 0's max
-  float vmax_t = -INFINITY;
-  f2_t vs2 = f2_pack(0.0f, 0.0f);
+  float vmax_t = -INFINITY;  // NaN once a NaN has been seen
   hist_clear();
   if (tid == 0) {
-    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue(sh, r, c, c, pol_keep);
+    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_keep);
   }
   for (int c = 0; c < r.nchunks; ++c) {
     const int s = c % kStages;
@@ -1283,10 +1316,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     ph ^= 1u << s;
     float x[8];
     const int g0 = st_get8<DT>(sh, r, c, s, x);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) vs2 = f2_add(vs2, f2_pack(x[2 * j], x[2 * j + 1]));
-    const float cm = fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
-    vmax_t = fmaxf(vmax_t, cm);
+    const float cm = st_max8n(x);
+    vmax_t = st_maxn(vmax_t, cm);
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
     if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
     if (c == 0) set_anchor(block_max_f<kStThreads>(cm, sh.redf));
@@ -1294,15 +1325,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     __syncthreads();  // every thread is done with stage s
     if (tid == 0 && c + kStages < r.nchunks) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      st_issue(sh, r, c + kStages, s, pol_keep);
+      st_issue<DT>(sh, r, c + kStages, s, pol_keep);
     }
   }
   ok = __syncthreads_and(ok) != 0;
   float vmax;
-  float vsum0, vsum1;
-  f2_unpack(vs2, vsum0, vsum1);
-  const float vsum = vsum0 + vsum1;
-  if (!finish_max(vmax_t, vsum, vmax)) return;
+  if (!finish_max(vmax_t, vmax)) return;
   for (int u = tid; u < nu; u += kStThreads) {
     const float mu = sh.w.n.m[u];
     sh.w.n.f[u] = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
@@ -1314,9 +1342,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     set_anchor(vmax);
     hist_clear();
     ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
-      const float cm =
-          fmaxf(fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3])), fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7])));
-      hist8(x, g0, cm);
+      hist8(x, g0, st_max8n(x));
     });
     if (!ok) {
       if (tid == 0) a.status[row] = kRowPending;
