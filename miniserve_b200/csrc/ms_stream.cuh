@@ -35,6 +35,8 @@
 // ms_generic_pending_kernel.
 #pragma once
 
+#include <cfloat>
+
 #include "ms_common.cuh"
 #include "ms_generic.cuh"
 
@@ -292,6 +294,15 @@ __device__ __forceinline__ float st_max8n(const float *x) {
   return st_max3n(st_max3n(x[0], x[1], x[2]), st_max3n(x[3], x[4], x[5]), st_maxn(x[6], x[7]));
 }
 __device__ __forceinline__ bool st_bad(float running_max) { return !(running_max < INFINITY); }
+
+// x[e] for a run-time e without indexing the array (which would put it in
+// local memory)
+__device__ __forceinline__ float st_pick8(const float *x, int e) {
+  const float a = (e & 1) ? x[1] : x[0], b = (e & 1) ? x[3] : x[2];
+  const float c = (e & 1) ? x[5] : x[4], d = (e & 1) ? x[7] : x[6];
+  const float ab = (e & 2) ? b : a, cd = (e & 2) ? d : c;
+  return (e & 4) ? cd : ab;
+}
 
 // global index of x[e] given that of x[0]
 __device__ __forceinline__ int st_gidx(int g0, int e) { return e < 4 ? g0 + e : g0 + 124 + e; }
@@ -993,7 +1004,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // chunk 0, barrier-free every 4th chunk after); ties at tau stay
     // candidates.  A warp with no value at or above tau skips the insert.
     float tau = -INFINITY;
-    bool strict = false;
+    float tf = -FLT_MAX;  // candidates: x >= tf (the next float above tau when strict; -inf never)
+    auto set_tau = [&](float t, bool strict) {
+      tau = t;
+      tf = strict ? key_to_float(fkey(t) + 1u) : fmaxf(t, -FLT_MAX);
+    };
     float rmax = -INFINITY;  // NaN once a NaN has been seen
     const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
@@ -1013,25 +1028,25 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       rmax = st_maxn(rmax, cm);
       if (!exact_tau && (c < 3 || (c & 3) == 0)) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
-        if (bmin != 0u && key_to_float(bmin) > tau) {
-          tau = key_to_float(bmin);
-          strict = false;
-        }
+        if (bmin != 0u && key_to_float(bmin) > tau) set_tau(key_to_float(bmin), false);
       }
-      // insert: only lanes holding a candidate, one shared atomic per entry
-      // (u32 shared atomics run at full rate).  The buffer holds at most
-      // kCandCap - kChunk entries before each chunk, so it cannot overflow.
+      // insert: only lanes holding a candidate, one shared atomic per lane for
+      // all its entries.  The buffer holds at most kCandCap - kChunk entries
+      // before each chunk, so it cannot overflow.
       int cnt = 0;
-      if (strict ? cm > tau : cm >= tau) {
+      if (cm >= tf) {  // NaN never
+        unsigned m = 0;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (x[e] > -INFINITY && (strict ? x[e] > tau : x[e] >= tau)) {
-            const int pos = atomicAdd(&sh.ncand, 1);  // positions only
-            sh.w.c.key[pos] = fkey(x[e]);
-            sh.w.c.idx[pos] = st_gidx(g0, e);
-            ++cnt;
-          }
-        }
+        for (int e = 0; e < 8; ++e) m |= (x[e] >= tf ? 1u : 0u) << e;
+        cnt = __popc(m);
+        int pos = atomicAdd(&sh.ncand, cnt);  // positions only
+        do {
+          const int e = __ffs(m) - 1;
+          m &= m - 1;
+          sh.w.c.key[pos] = fkey(st_pick8(x, e));
+          sh.w.c.idx[pos] = st_gidx(g0, e);
+          ++pos;
+        } while (m);
       }
       const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
       if (lane == 0) sh.wcnt[c & 1][tid >> 5] = wt;
@@ -1044,8 +1059,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       // the row; entries below it stay in the buffer, dead
       if ((c == 3 || c == 11) && ncand >= 2 * k && ncand <= kCandCap - kChunk) {
         int above;
-        tau = key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above));
-        strict = true;  // >= k entries >= tau are held: a later equal value ranks below
+        // >= k entries >= the k-th largest are held: a later equal value ranks below
+        set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above)), true);
         exact_tau = true;
       }
       // shrink to the entries >= the buffer's k-th largest (ties kept) when the
@@ -1073,8 +1088,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         if (tid == 0) sh.ncand = ktot;
         __syncthreads();
         ncand = ktot;
-        tau = key_to_float(kk);
-        strict = true;  // >= k entries >= kk are held: a later equal value ranks below
+        set_tau(key_to_float(kk), true);  // >= k entries >= kk are held: a later equal value ranks below
         exact_tau = true;
         if (ktot > kCandCap - kChunk) over = true;  // heavy ties
       }
