@@ -53,9 +53,9 @@ constexpr int kRankCap = 1024;                  // largest set sorted by rank co
 constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
 constexpr int kMaxUnits = 1024;                 // per-unit summaries kept per row
 constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
-constexpr int kXBins = 2048;                    // x-grid bins per kSXRange (top-p)
+constexpr int kXBins = 4096;                    // x-grid bins per kSXRange (top-p)
 constexpr float kSXRange = 40.0f;               // units of x = logit / T
-constexpr int kUpBins = 512;                    // grid bins above the anchor
+constexpr int kUpBins = 1024;                   // grid bins above the anchor
 constexpr int kSBins = kXBins + kUpBins;        // x-grid bins in all
 constexpr int kHighCap = 256;                   // values above the grid kept exactly
 constexpr int kQSlots = (kSBins + 2 + kStThreads - 1) / kStThreads * kStThreads;  // histogram indices 0..kSBins+1
@@ -1262,7 +1262,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const float dx = kSXRange / (float)kXBins;
   const float t_off = (float)(kUpBins + 1);
   const float t_max = (float)kSBins + 1.25f;
-  // round(kQScale * e^-(fr*dx)) + 2^23 as a float (quadratic, error (fr*dx)^3/6 < 1.3e-6)
+  // round(kQScale * e^-(fr*dx)) + 2^23 as a float (quadratic, error (fr*dx)^3/6 < 1.6e-7)
   const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx;
   uint32_t *hq = sh.w.n.x.hq;
   float G = -INFINITY;
@@ -1479,27 +1479,24 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   }
   uint32_t *gk = sh.w.n.x.g.key;
   int *gi = sh.w.n.x.g.idx;
-  if (n <= kRankCap) {
-    st_rank_sort(sh, gk, gi, n, false);
-  } else {
-    st_sort(gk, gi, n, false);
-  }
-  // the cut: first entry (value desc, index asc) whose running mass reaches
-  // P*total (miniserve/sampler.py:50-57)
+  // The cut: the first bracket entry in (value desc, index asc) order whose
+  // running mass, after above_tot, reaches P*total (miniserve/sampler.py:50-57)
+  // -- (ck, ci); or none, when the bracket's mass falls short.
   const double need = pz - above_tot;
-  int rc;
-  {
-    const int per = (n + kStThreads - 1) / kStThreads;
-    const int p0 = tid * per, p1 = min(n, p0 + per);
+  // the first of m sorted entries whose running mass from `base` reaches
+  // need, or 0x7FFFFFFF
+  auto scan_sorted = [&](const uint32_t *sk, const int *si, int m, double base) -> int {
+    const int per = (m + kStThreads - 1) / kStThreads;
+    const int p0 = tid * per, p1 = min(m, p0 + per);
     double sw = 0.0;
-    for (int i = p0; i < p1; ++i) sw += unit_w(key_to_float(gk[i]), gi[i]);
+    for (int i = p0; i < p1; ++i) sw += unit_w(key_to_float(sk[i]), si[i]);
     double ex, inc, tt;
     block_scan<kStThreads, double>(sw, ex, inc, tt, sh.redd);
     int cand = 0x7FFFFFFF;
-    if (p0 < p1 && inc >= need) {
-      double acc = ex;
+    if (p0 < p1 && base + inc >= need) {
+      double acc = base + ex;
       for (int i = p0; i < p1; ++i) {
-        acc += unit_w(key_to_float(gk[i]), gi[i]);
+        acc += unit_w(key_to_float(sk[i]), si[i]);
         if (acc >= need) {
           cand = i;
           break;
@@ -1507,25 +1504,143 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       if (cand == 0x7FFFFFFF) cand = p1 - 1;
     }
-    rc = block_min_i<kStThreads>(cand, sh.redi);
+    return block_min_i<kStThreads>(cand, sh.redi);
+  };
+  uint32_t ck = 0u;
+  int ci = 0x7FFFFFFF;
+  int state = 2;  // 0: the cut found, 1: none, 2: not resolved yet
+  if (n > kRankCap / 4) {
+    // A large bracket: 256 key buckets with fixed-point masses place the
+    // crossing within a window of buckets, and only the window is sorted.
+    // Bucket b holds keys kmin + [b << bsh, (b + 1) << bsh).
+    int lo_i = 0x7FFFFFFF, hi_i = 0x7FFFFFFF;
+    for (int i = tid; i < n; i += kStThreads) {
+      lo_i = min(lo_i, (int)(gk[i] ^ 0x80000000u));
+      hi_i = min(hi_i, (int)(~gk[i] ^ 0x80000000u));
+    }
+    const uint32_t kmin = (uint32_t)block_min_i<kStThreads>(lo_i, sh.redi) ^ 0x80000000u;
+    const uint32_t kmax = ~((uint32_t)block_min_i<kStThreads>(hi_i, sh.redi) ^ 0x80000000u);
+    const int bsh = max(0, 24 - __clz((int)(kmax - kmin)));
+    // w * qs < 2^18 for every entry: qs from the top key's weight, with a
+    // margin far above the weights' rounding
+    const double qs = 262144.0 / (exp2(((double)key_to_float(kmax) - (double)vmax) * cl) * 1.001);
+    uint32_t *bcnt = reinterpret_cast<uint32_t *>(sh.stage[0]);  // [256] entries, [256] mass
+    for (int q = tid; q < 512; q += kStThreads) bcnt[q] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += kStThreads) {
+      const int bk = (int)((gk[i] - kmin) >> bsh);
+      const double w = unit_w(key_to_float(gk[i]), gi[i]);
+      atomicAdd(&bcnt[bk], 1u);
+      atomicAdd(&bcnt[256 + bk], (uint32_t)fmin(w * qs, 524288.0));  // floor: w*qs - 1 < q <= w*qs
+    }
+    __syncthreads();
+    // every warp: C(b), N(b) = bucket mass and entries at or above b.  The
+    // exact scaled mass at or above b lies in [C(b), C(b) + N(b)), so the
+    // crossing bucket b* (highest b whose exact mass reaches need) satisfies
+    // b_lo <= b* <= b_hi with b_lo = highest b with C(b) >= T and b_hi =
+    // highest b with C(b) + N(b) >= T.
+    const double T = need * qs;
+    uint32_t cq[8], cn[8], sq = 0, sn = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int bk = 255 - 8 * lane - q;
+      cn[q] = bcnt[bk];
+      cq[q] = bcnt[256 + bk];
+      sq += cq[q];
+      sn += cn[q];
+    }
+    uint32_t iq = sq, in_ = sn;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t yq = __shfl_up_sync(0xFFFFFFFFu, iq, o), yn = __shfl_up_sync(0xFFFFFFFFu, in_, o);
+      if (lane >= o) {
+        iq += yq;
+        in_ += yn;
+      }
+    }
+    double cacc = (double)(iq - sq), nacc = (double)(in_ - sn);
+    int blo = -1, bhi = -1;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      cacc += (double)cq[q];
+      nacc += (double)cn[q];
+      if (blo < 0 && cacc >= T) blo = 255 - 8 * lane - q;
+      if (bhi < 0 && cacc + nacc >= T) bhi = 255 - 8 * lane - q;
+    }
+    blo = __reduce_max_sync(0xFFFFFFFFu, blo);  // highest bucket: lowest lane's first hit
+    bhi = __reduce_max_sync(0xFFFFFFFFu, bhi);
+    if (bhi < 0) {
+      state = 1;  // even the largest possible bracket mass falls short of need
+    } else {
+      const int wlo = max(blo, 0);
+      // exact mass above the window, and the window's entries gathered
+      double am = 0.0;
+      int wc = 0;
+      for (int i = tid; i < n; i += kStThreads) {
+        const int bk = (int)((gk[i] - kmin) >> bsh);
+        if (bk > bhi) am += unit_w(key_to_float(gk[i]), gi[i]);
+        else if (bk >= wlo) ++wc;
+      }
+      const double A = block_sum<kStThreads>(am, sh.redd);
+      int wex, win, m;
+      block_scan<kStThreads, int>(wc, wex, win, m, sh.redi);
+      if (A < need && m <= kRankCap) {  // otherwise the buckets misled: sort everything
+        uint32_t *wk = reinterpret_cast<uint32_t *>(sh.stage[1] + 8192);
+        int *wi = reinterpret_cast<int *>(sh.stage[1] + 12288);
+        for (int i = tid; i < n; i += kStThreads) {
+          const int bk = (int)((gk[i] - kmin) >> bsh);
+          if (bk <= bhi && bk >= wlo) {
+            wk[wex] = gk[i];
+            wi[wex] = gi[i];
+            ++wex;
+          }
+        }
+        __syncthreads();
+        st_rank_sort(sh, wk, wi, m, false);
+        const int pc = scan_sorted(wk, wi, m, A);
+        if (pc != 0x7FFFFFFF) {
+          ck = wk[pc];
+          ci = wi[pc];
+          state = 0;
+        } else if (blo < 0) {
+          state = 1;  // the window reaches the bracket's bottom: its mass falls short
+        }
+      }
+    }
   }
-  if (rc == 0x7FFFFFFF && i_hi <= kSBins) {  // the crossing lies below the bracket
+  if (state == 2) {  // a small bracket, or the buckets misled: sort it all
+    if (n <= kRankCap) {
+      st_rank_sort(sh, gk, gi, n, false);
+    } else {
+      st_sort(gk, gi, n, false);
+    }
+    const int pc = scan_sorted(gk, gi, n, 0.0);
+    if (pc != 0x7FFFFFFF) {
+      ck = gk[pc];
+      ci = gi[pc];
+      state = 0;
+    } else {
+      state = 1;
+    }
+  }
+  if (state == 1 && i_hi <= kSBins) {  // the crossing lies below the bracket
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  // rc == none with the tail bracketed: the running sum never reaches top_p,
-  // every token is kept
-  const float vc = rc == 0x7FFFFFFF ? -INFINITY : key_to_float(gk[rc]);
-  const int ic = rc == 0x7FFFFFFF ? 0x7FFFFFFF : gi[rc];
-  const int nkeep = rc == 0x7FFFFFFF ? n : rc + 1;
+  // no cut with the tail bracketed: the running sum never reaches top_p, every
+  // token is kept
+  const float vc = state == 1 ? -INFINITY : key_to_float(ck);
+  const int ic = state == 1 ? 0x7FFFFFFF : ci;
   // kept mass per unit: above the bracket (s_u) plus the unit's kept bracket
   // entries, those summed as 2^-50 fixed point (exact and order-free)
   unsigned long long *ex64 = reinterpret_cast<unsigned long long *>(sh.stage[2]);
   for (int u = tid; u < nu; u += kStThreads) ex64[u] = 0ull;
   __syncthreads();
-  for (int i = tid; i < nkeep; i += kStThreads) {
-    const double w = unit_w(key_to_float(gk[i]), gi[i]);  // <= 1
-    atomicAdd(&ex64[gi[i] / kUnit], (unsigned long long)(w * 0x1p50));
+  for (int i = tid; i < n; i += kStThreads) {
+    if (state == 1 || gk[i] > ck || (gk[i] == ck && gi[i] <= ci)) {  // at or before the cut
+      const double w = unit_w(key_to_float(gk[i]), gi[i]);  // <= 1
+      atomicAdd(&ex64[gi[i] / kUnit], (unsigned long long)(w * 0x1p50));
+    }
   }
   __syncthreads();
   double tk = 0.0;
