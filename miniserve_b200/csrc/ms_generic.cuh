@@ -370,6 +370,9 @@ __global__ void __launch_bounds__(kGenThreads, 1)
 template <int DT>
 __global__ void __launch_bounds__(kGenThreads, 1) ms_generic_pending_kernel(SampleArgs a, int B) {
   __shared__ GenShared sh;
+  // launched as a programmatic dependent of ms_stream_kernel: wait for that
+  // grid (and its status writes) to complete; a no-op for a plain launch
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int r = blockIdx.x; r < B; r += gridDim.x) {
     if (a.status[r] != kRowPending) continue;
     gen_row<DT>(a, r, sh);

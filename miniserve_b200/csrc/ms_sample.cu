@@ -60,7 +60,21 @@ cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, 
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = B < sms ? B : sms;
-  ms::ms_generic_pending_kernel<DT><<<dim3((unsigned)grid), dim3(ms::kGenThreads), 0, s>>>(a, B);
+  // a programmatic dependent launch: the pending pass is launched while the
+  // streaming kernel's last CTAs run and waits (griddepcontrol.wait) for that
+  // grid's completion before it reads a status
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(ms::kGenThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, ms::ms_generic_pending_kernel<DT>, a, B);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 }  // namespace

@@ -876,6 +876,9 @@ template <int DT>
 __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) {
   extern __shared__ __align__(128) unsigned char st_raw[];
   StShared &sh = *reinterpret_cast<StShared *>(st_raw);
+  // every CTA of this grid has started: a programmatic dependent launch (the
+  // pending-row pass) may begin launching
+  asm volatile("griddepcontrol.launch_dependents;");
   const int row = st_pick_row(sh, a, (int)gridDim.x);
   const int tid = threadIdx.x;
   const int lane = tid & 31;
