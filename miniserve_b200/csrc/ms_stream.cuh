@@ -110,6 +110,7 @@ struct StRow {
   int esz;
   bool tma;             // 16-byte aligned row: chunks arrive by TMA
   int nchunks;
+  int nfull;            // leading chunks delivered whole by TMA
 };
 
 __device__ __forceinline__ uint32_t st_smem(const void *p) {
@@ -163,24 +164,29 @@ __device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, in
   }
 }
 
+__device__ __forceinline__ bool st_try_wait(uint32_t mb, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(mb), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// the rare case of st_wait: keep probing, false after ~1 s
+__device__ __noinline__ bool st_wait_slow(uint32_t mb, uint32_t parity) {
+  const uint64_t t0 = st_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (st_try_wait(mb, parity)) return true;
+    if ((it & 1023u) == 0u && st_ns() - t0 > 1000000000ull) return false;
+  }
+}
+
 // all threads: wait for the current phase of stage s; false after ~1 s
 __device__ __forceinline__ bool st_wait(StShared &sh, int s, uint32_t parity) {
   const uint32_t mb = st_smem(&sh.full[s]);
-  uint32_t done = 0;
-  uint64_t t0 = 0;  // the clock is read only once the wait has spun a while
-  for (uint32_t it = 0; !done; ++it) {
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(done)
-        : "r"(mb), "r"(parity)
-        : "memory");
-    if (!done && (it & 1023u) == 1023u) {
-      const uint64_t t = st_ns();
-      if (t0 == 0) t0 = t;
-      else if (t - t0 > 1000000000ull) return false;
-    }
-  }
-  return true;
+  return st_try_wait(mb, parity) || st_wait_slow(mb, parity);
 }
 
 // Four consecutive elements (chunk-local j, a multiple of 4) of chunk c in
@@ -238,7 +244,7 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
 template <int DT>
 __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
   const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
-  if (tma_elems<DT>(r, c) == kChunk) {  // the whole chunk is in the stage (block-uniform)
+  if (c < r.nfull) {  // the whole chunk is in the stage (block-uniform)
     if (DT == MS_DTYPE_F32) {
       const float4 *p = reinterpret_cast<const float4 *>(sh.stage[s]);
       const float4 f0 = p[j >> 2], f1 = p[(j + 128) >> 2];
@@ -318,8 +324,7 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
   if (tid == 0) {
     for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol);
   }
-  for (int c = 0; c < r.nchunks; ++c) {
-    const int s = c % kStages;
+  for (int c = 0, s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
     if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
     ph ^= 1u << s;
     float x[8];
@@ -932,6 +937,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   r.V = V;
   r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
   r.nchunks = (V + kChunk - 1) / kChunk;
+  r.nfull = r.tma ? V / kChunk : 0;
   if (tid < kStages) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
   }
@@ -1021,8 +1027,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_stream);
     }
     int c = 0;
-    for (; c < r.nchunks; ++c) {
-      const int s = c % kStages;
+    for (int s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
       if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
       ph ^= 1u << s;
       float x[8];
@@ -1327,8 +1332,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   if (tid == 0) {
     for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_keep);
   }
-  for (int c = 0; c < r.nchunks; ++c) {
-    const int s = c % kStages;
+  for (int c = 0, s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
     if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
     ph ^= 1u << s;
     float x[8];
