@@ -1269,7 +1269,6 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const float xs = (float)((double)kXBins / ((double)kSXRange * T));
   const float dx = kSXRange / (float)kXBins;
   const float t_off = (float)(kUpBins + 1);
-  const float t_max = (float)kSBins + 1.25f;
   // round(kQScale * e^-(fr*dx)) + 2^23 as a float (quadratic, error (fr*dx)^3/6 < 1.6e-7)
   const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx;
   uint32_t *hq = sh.w.n.x.hq;
@@ -1277,10 +1276,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   float v_high = INFINITY;  // no value at or below it lies above the grid (t < 1)
   float v_tail = INFINITY;  // every value at or below it lies in the tail (t >= kSBins + 1)
   // Histogram of this lane's 8 values (x[4..7] sit 128 after x[0..3]), cm
-  // their maximum.  Grid coordinates are packed pairs clamped to
-  // [0.5, t_max]: index 0 collects the values above the grid (kept exactly in
-  // the high list and left out of the histogram's mass), kSBins + 1 the tail,
-  // -inf and NaN.
+  // their maximum, in packed pairs.  Only grid bins 1..kSBins take mass:
+  // values above the grid (t < 1) are kept exactly in the high list, and the
+  // tail (t >= kSBins + 1, -inf and NaN included) is left out.
   auto hist8 = [&](const float *x, int g0, float cm) {
     if (__any_sync(0xFFFFFFFFu, cm > v_high)) {  // rare: some value may lie above the grid
 #pragma unroll
@@ -1300,19 +1298,20 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const f2_t Q0 = f2_pack(q0, q0), Q1 = f2_pack(q1, q1), Q2 = f2_pack(q2, q2);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float t0, t1;
-      f2_unpack(f2_fma(f2_sub(G2, f2_pack(x[2 * j], x[2 * j + 1])), XS2, OFF2), t0, t1);
-      const f2_t TC = f2_pack(fminf(fmaxf(t0, 0.5f), t_max), fminf(fmaxf(t1, 0.5f), t_max));
-      // 2^23 + floor(t): the add rounds toward -inf, so the index is floor(t)
+      const f2_t TC = f2_fma(f2_sub(G2, f2_pack(x[2 * j], x[2 * j + 1])), XS2, OFF2);
+      // 2^23 + floor(t): the add rounds toward -inf, so for 0 <= t < 2^23 the
+      // float's low mantissa bits are floor(t).  Any t outside the grid bins
+      // (t < 1, t >= kSBins + 1, huge, infinite or NaN) gives an index outside
+      // 1..kSBins and adds nothing.
       const f2_t TB = f2_add_rm(TC, M2);
       const f2_t FR = f2_sub(TC, f2_sub(TB, M2));
       float tb0, tb1, qa, qb;
       f2_unpack(TB, tb0, tb1);
       f2_unpack(f2_fma(f2_fma(FR, Q2, Q1), FR, Q0), qa, qb);
       // grid bins only: the high list's index 0 and the tail carry no histogram mass
-      const int i0 = __float_as_int(tb0) - 0x4B000000, i1 = __float_as_int(tb1) - 0x4B000000;
-      if ((unsigned)(i0 - 1) < (unsigned)kSBins) atomicAdd(&hq[i0], (uint32_t)(__float_as_int(qa) - 0x4B000000));
-      if ((unsigned)(i1 - 1) < (unsigned)kSBins) atomicAdd(&hq[i1], (uint32_t)(__float_as_int(qb) - 0x4B000000));
+      const uint32_t i0 = __float_as_uint(tb0) - 0x4B000000u, i1 = __float_as_uint(tb1) - 0x4B000000u;
+      if (i0 - 1u < (uint32_t)kSBins) atomicAdd(&hq[i0], __float_as_uint(qa) - 0x4B000000u);
+      if (i1 - 1u < (uint32_t)kSBins) atomicAdd(&hq[i1], __float_as_uint(qb) - 0x4B000000u);
     }
   };
   auto set_anchor = [&](float g) {
@@ -1435,6 +1434,18 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     StW Wu = W;
     Wu.set_m(mu);
     const StW2 W2(Wu);
+    const float fu = sh.w.n.f[u];
+    // the total: every lane adds its own weights (no warp reduction)
+    if (!(mu > v_hi)) {  // nothing above or in the bracket (warp-uniform): weights only
+      f2_t a2 = W2(f2_pack(x[0], x[1]));
+#pragma unroll
+      for (int j = 1; j < 4; ++j) a2 = f2_add(a2, W2(f2_pack(x[2 * j], x[2 * j + 1])));
+      float a0, a1;
+      f2_unpack(a2, a0, a1);
+      zacc += (double)(a0 + a1) * (double)fu;
+      if (lane == 0) sh.w.n.s[u] = 0.0f;
+      return;
+    }
     float all = 0.0f, above = 0.0f;
     uint32_t in_any = 0u;
 #pragma unroll
@@ -1450,11 +1461,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
     const bool any_in = in_any != 0u;
     above = warp_sum_f(above);
-    all = warp_sum_f(all);
-    if (lane == 0) {
-      sh.w.n.s[u] = above;
-      zacc += (double)all * (double)sh.w.n.f[u];
-    }
+    zacc += (double)all * (double)fu;
+    if (lane == 0) sh.w.n.s[u] = above;
     if (any_in) {  // rare
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
