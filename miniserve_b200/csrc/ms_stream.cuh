@@ -346,18 +346,21 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 }
 
 // --------------------------------------------------------- block selection
-// The k-th largest of n keys (1 <= k <= n), by four rounds of 8-bit digits;
-// *n_above = the keys strictly above it.  Each round has its own histogram
-// (cleared up front), and every warp scans it for itself, so a round costs
-// one barrier.  All threads.
-__device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int k, int *n_above) {
+// The k-th largest of n keys (1 <= k <= n), by rounds of 8-bit digits from
+// the top; *n_above = the keys whose leading digits are above its.  With
+// rounds == 4 the key itself; with fewer, its leading 8*rounds bits followed
+// by zeros (a lower bound on it).  Each round has its own histogram (cleared
+// up front), and every warp scans it for itself, so a round costs one
+// barrier.  All threads.
+__device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int k, int *n_above,
+                                  int rounds = 4) {
   const int tid = threadIdx.x, lane = tid & 31;
   __syncthreads();  // no warp still scans the histograms of an earlier call
-  for (int b = tid; b < 4 * 256; b += kStThreads) (&sh.sel[0][0])[b] = 0u;
+  for (int b = tid; b < rounds * 256; b += kStThreads) (&sh.sel[0][0])[b] = 0u;
   __syncthreads();
   uint32_t prefix = 0;
   int rem = k, above = 0;
-  for (int d = 0; d < 4; ++d) {
+  for (int d = 0; d < rounds; ++d) {
     const int shift = 24 - 8 * d;
     uint32_t *h = sh.sel[d];
     for (int i0 = 0; i0 < n; i0 += kStThreads) {
@@ -418,7 +421,7 @@ __device__ uint32_t st_select_kth(StShared &sh, const uint32_t *keys, int n, int
     prefix = (prefix << 8) | dig;
   }
   *n_above = above;
-  return prefix;
+  return rounds == 4 ? prefix : prefix << (32 - 8 * rounds);
 }
 
 // ------------------------------------------------------------ bitonic sort
@@ -1065,16 +1068,21 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
       if (lane == 0) sh.wcnt[c & 1][tid >> 5] = wt;
       __syncthreads();  // stage s is free; the buffer is settled
+      // refill stage s first, so the copy runs under a select or compaction
+      if (tid == 0 && c + kStages < r.nchunks) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        st_issue<DT>(sh, r, c + kStages, s, pol_stream);
+      }
       // exact count from the per-warp slots (slot c&1 is rewritten two chunks
       // on, after a barrier every thread has passed)
       ncand += __reduce_add_sync(0xFFFFFFFFu, lane < kStWarps ? sh.wcnt[c & 1][lane] : 0);
-      // early on (chunks 3 and 11) the buffer's exact k-th largest is a far
+      // early on (chunks 3 and 11) the buffer's k-th largest, to 16 leading
+      // bits (two digit rounds; a lower bound within 2^-7 of it), is a far
       // tighter tau than the warp bound and cuts the inserts of the rest of
       // the row; entries below it stay in the buffer, dead
       if ((c == 3 || c == 11) && ncand >= 2 * k && ncand <= kCandCap - kChunk) {
         int above;
-        // >= k entries >= the k-th largest are held: a later equal value ranks below
-        set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above)), true);
+        set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above, 2)), false);
         exact_tau = true;
       }
       // shrink to the entries >= the buffer's k-th largest (ties kept) when the
@@ -1107,15 +1115,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         if (ktot > kCandCap - kChunk) over = true;  // heavy ties
       }
       if (over) break;
-      if (tid == 0 && c + kStages < r.nchunks) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        st_issue<DT>(sh, r, c + kStages, s, pol_stream);
-      }
     }
     if (over) {
-      // copies of chunks c+1 .. c+kStages-1 are in flight: let them land
+      // copies of chunks c+1 .. c+kStages are in flight: let them land
       // before this CTA's shared memory is released
-      for (int c2 = c + 1; c2 < r.nchunks && c2 < c + kStages; ++c2) {
+      for (int c2 = c + 1; c2 < r.nchunks && c2 <= c + kStages; ++c2) {
         const int s2 = c2 % kStages;
         if (!st_wait(sh, s2, (ph >> s2) & 1u)) ok = false;
         ph ^= 1u << s2;
@@ -1390,14 +1394,17 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const double rG = exp2(((double)G - (double)vmax) * cl);  // anchor weight / max weight
     double mb[kPer];
     double s = 0.0;
+    // bin i's weight e^-((i - 1 - kUpBins) dx) * rG / kQScale: one exp for the
+    // thread's first bin, then a factor e^-dx per bin
+    const double step = exp(-(double)dx);
+    double wb = exp(-(double)(tid * kPer - 1 - kUpBins) * (double)dx) * (rG / (double)kQScale);
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
       const int i = tid * kPer + q;
       // index 0: values above the grid, counted exactly in H; the tail's
       // mass (each < e^-30 of the anchor's weight) is left out
-      mb[q] = (i >= 1 && i <= kSBins)
-                  ? (double)hq[i] * (rG / (double)kQScale) * exp(-(double)(i - 1 - kUpBins) * (double)dx)
-                  : 0.0;
+      mb[q] = (i >= 1 && i <= kSBins) ? (double)hq[i] * wb : 0.0;
+      wb *= step;
       s += mb[q];
     }
     double ex, inc, tot;
