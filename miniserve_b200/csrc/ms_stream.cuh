@@ -92,6 +92,8 @@ struct StShared {
   alignas(16) uint32_t sel[4][256];  // st_select_kth: one digit histogram per round
   unsigned long long full[kStages];
   double redd[33];
+  double r1d[2][64];  // one-barrier reductions (st_bsum and friends): two halves
+  int r1i[2][32];
   uint32_t redu[33];
   int redi[33];
   float redf[33];
@@ -343,6 +345,94 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
   return v;
+}
+
+// ------------------------------------------- one-barrier block reductions
+// A call writes the warps' partials into one of two scratch halves,
+// alternating per call (`rf` flips; every thread makes the same calls in the
+// same order), and every warp combines the partials itself.  A half is
+// written again only after another call's barrier, which every thread passes
+// after reading it.  All threads.
+__device__ __forceinline__ double st_bsum(StShared &sh, int &rf, double v) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  double *p = sh.r1d[rf];
+  rf ^= 1;
+  if (lane == 0) p[warp] = v;
+  __syncthreads();
+  return warp_sum(lane < kStWarps ? p[lane] : 0.0);
+}
+// two sums at once
+__device__ __forceinline__ void st_bsum2(StShared &sh, int &rf, double a, double b, double &sa, double &sb) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  double *p = sh.r1d[rf];
+  rf ^= 1;
+  if (lane == 0) {
+    p[warp] = a;
+    p[32 + warp] = b;
+  }
+  __syncthreads();
+  sa = warp_sum(lane < kStWarps ? p[lane] : 0.0);
+  sb = warp_sum(lane < kStWarps ? p[32 + lane] : 0.0);
+}
+__device__ __forceinline__ int st_bmin(StShared &sh, int &rf, int v) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_min_sync(0xFFFFFFFFu, v);
+  int *p = sh.r1i[rf];
+  rf ^= 1;
+  if (lane == 0) p[warp] = v;
+  __syncthreads();
+  return __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? p[lane] : 0x7FFFFFFF);
+}
+// exclusive and inclusive prefix sums over threads in thread order, and the total
+__device__ __forceinline__ void st_bscan(StShared &sh, int &rf, double v, double &ex, double &inc, double &tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  double xprev = __shfl_up_sync(0xFFFFFFFFu, x, 1);
+  if (lane == 0) xprev = 0.0;
+  double *p = sh.r1d[rf];
+  rf ^= 1;
+  if (lane == 31) p[warp] = x;
+  __syncthreads();
+  double w = lane < kStWarps ? p[lane] : 0.0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+    if (lane >= o) w += y;
+  }
+  const double prev = __shfl_sync(0xFFFFFFFFu, w, (warp + 31) & 31);
+  tot = __shfl_sync(0xFFFFFFFFu, w, kStWarps - 1);
+  ex = (warp > 0 ? prev : 0.0) + xprev;
+  inc = (warp > 0 ? prev : 0.0) + x;
+}
+__device__ __forceinline__ void st_bscan_i(StShared &sh, int &rf, int v, int &ex, int &tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  int *p = sh.r1i[rf];
+  rf ^= 1;
+  if (lane == 31) p[warp] = x;
+  __syncthreads();
+  int w = lane < kStWarps ? p[lane] : 0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+    if (lane >= o) w += y;
+  }
+  const int prev = __shfl_sync(0xFFFFFFFFu, w, (warp + 31) & 31);
+  tot = __shfl_sync(0xFFFFFFFFu, w, kStWarps - 1);
+  ex = (warp > 0 ? prev : 0) + x - v;
 }
 
 // --------------------------------------------------------- block selection
@@ -751,7 +841,7 @@ __device__ __forceinline__ float st_load1(const StRow &r, int gi) {
 // scan, then that unit's 256 elements re-read with keptw(v, gi), the same
 // float64 weights the unit sums were made of.  Writes the row.  All threads.
 template <int DT, class KW>
-__device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r, int row, int nu,
+__device__ void st_draw_units(StShared &sh, int &rf, const SampleArgs &a, const StRow &r, int row, int nu,
                               const double *kept, double total, double U, KW keptw) {
   const int tid = threadIdx.x;
   if (!(U > 0.0)) {  // r == 0 stops at index 0 (sampler.py:66)
@@ -762,10 +852,10 @@ __device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r,
   const int u0 = 2 * tid;
   const double k0 = u0 < nu ? kept[u0] : 0.0, k1 = u0 + 1 < nu ? kept[u0 + 1] : 0.0;
   double ex, inc, tt;
-  block_scan<kStThreads, double>(k0 + k1, ex, inc, tt, sh.redd);
+  st_bscan(sh, rf, k0 + k1, ex, inc, tt);
   int cand = 0x7FFFFFFF;
   if (k0 + k1 > 0.0 && inc >= target) cand = (k0 > 0.0 && ex + k0 >= target) ? u0 : u0 + 1;
-  const int us = block_min_i<kStThreads>(cand, sh.redi);
+  const int us = st_bmin(sh, rf, cand);
   if (us == 0x7FFFFFFF) {  // ran past the end (sampler.py:68)
     if (tid == 0) write_row(a, row, a.V - 1, (float)(keptw(st_load1<DT>(r, a.V - 1), a.V - 1) / total), 0);
     return;
@@ -776,10 +866,10 @@ __device__ void st_draw_units(StShared &sh, const SampleArgs &a, const StRow &r,
   const int gi = us * kUnit + tid;
   const double w = (tid < kUnit && gi < a.V) ? keptw(st_load1<DT>(r, gi), gi) : 0.0;
   double wex, winc, wtot;
-  block_scan<kStThreads, double>(w, wex, winc, wtot, sh.redd);
-  int who = block_min_i<kStThreads>((w > 0.0 && before + winc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  st_bscan(sh, rf, w, wex, winc, wtot);
+  int who = st_bmin(sh, rf, (w > 0.0 && before + winc >= target) ? tid : 0x7FFFFFFF);
   if (who == 0x7FFFFFFF) {  // rounding left the target past the unit: its last kept element
-    who = -block_min_i<kStThreads>(w > 0.0 ? -tid : 1, sh.redi);
+    who = -st_bmin(sh, rf, w > 0.0 ? -tid : 1);
   }
   if (who < 0) {  // no kept element in the unit (cannot happen for consistent sums)
     if (tid == 0) a.status[row] = kRowPending;
@@ -961,6 +1051,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
   bool ok = true;
+  int rf = 0;  // scratch half of the next one-barrier reduction
 
   // ================================================================ argmax
   if (mode == kStArgmax) {
@@ -1261,7 +1352,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       zs += kd[u];
     }
     const double total = block_sum<kStThreads>(zs, sh.redd);  // ends with a barrier
-    st_draw_units<DT>(sh, a, r, row, nu, kd, total, U,
+    st_draw_units<DT>(sh, rf, a, r, row, nu, kd, total, U,
                       [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
     return;
   }
@@ -1496,11 +1587,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  const double total = block_sum<kStThreads>(zacc, sh.redd);
-  const double pz = P * total;
   double as = 0.0;
   for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
-  const double above_tot = block_sum<kStThreads>(as, sh.redd);
+  double total, above_tot;
+  st_bsum2(sh, rf, zacc, as, total, above_tot);
+  const double pz = P * total;
   if (above_tot > 0.0 && above_tot >= pz) {  // the crossing lies above the bracket
     if (tid == 0) a.status[row] = kRowPending;
     return;
@@ -1519,7 +1610,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     double sw = 0.0;
     for (int i = p0; i < p1; ++i) sw += unit_w(key_to_float(sk[i]), si[i]);
     double ex, inc, tt;
-    block_scan<kStThreads, double>(sw, ex, inc, tt, sh.redd);
+    st_bscan(sh, rf, sw, ex, inc, tt);
     int cand = 0x7FFFFFFF;
     if (p0 < p1 && base + inc >= need) {
       double acc = base + ex;
@@ -1532,7 +1623,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       if (cand == 0x7FFFFFFF) cand = p1 - 1;
     }
-    return block_min_i<kStThreads>(cand, sh.redi);
+    return st_bmin(sh, rf, cand);
   };
   uint32_t ck = 0u;
   int ci = 0x7FFFFFFF;
@@ -1546,8 +1637,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       lo_i = min(lo_i, (int)(gk[i] ^ 0x80000000u));
       hi_i = min(hi_i, (int)(~gk[i] ^ 0x80000000u));
     }
-    const uint32_t kmin = (uint32_t)block_min_i<kStThreads>(lo_i, sh.redi) ^ 0x80000000u;
-    const uint32_t kmax = ~((uint32_t)block_min_i<kStThreads>(hi_i, sh.redi) ^ 0x80000000u);
+    const uint32_t kmin = (uint32_t)st_bmin(sh, rf, lo_i) ^ 0x80000000u;
+    const uint32_t kmax = ~((uint32_t)st_bmin(sh, rf, hi_i) ^ 0x80000000u);
     const int bsh = max(0, 24 - __clz((int)(kmax - kmin)));
     // w * qs < 2^18 for every entry: qs from the top key's weight, with a
     // margin far above the weights' rounding
@@ -1609,9 +1700,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         if (bk > bhi) am += unit_w(key_to_float(gk[i]), gi[i]);
         else if (bk >= wlo) ++wc;
       }
-      const double A = block_sum<kStThreads>(am, sh.redd);
-      int wex, win, m;
-      block_scan<kStThreads, int>(wc, wex, win, m, sh.redi);
+      const double A = st_bsum(sh, rf, am);
+      int wex, m;
+      st_bscan_i(sh, rf, wc, wex, m);
       if (A < need && m <= kRankCap) {  // otherwise the buckets misled: sort everything
         uint32_t *wk = reinterpret_cast<uint32_t *>(sh.stage[1] + 8192);
         int *wi = reinterpret_cast<int *>(sh.stage[1] + 12288);
@@ -1676,8 +1767,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     kd[u] = (double)sh.w.n.s[u] * (double)sh.w.n.f[u] + (double)ex64[u] * 0x1p-50;
     tk += kd[u];
   }
-  const double tot_keep = block_sum<kStThreads>(tk, sh.redd);
-  st_draw_units<DT>(sh, a, r, row, nu, kd, tot_keep, U, [&](float v, int g) -> double {
+  const double tot_keep = st_bsum(sh, rf, tk);
+  st_draw_units<DT>(sh, rf, a, r, row, nu, kd, tot_keep, U, [&](float v, int g) -> double {
     if (!(v > -INFINITY) || !(v > vc || (v == vc && g <= ic))) return 0.0;
     return unit_w(v, g);
   });
