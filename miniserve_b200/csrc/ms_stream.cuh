@@ -1551,7 +1551,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       return;
     }
     float all = 0.0f, above = 0.0f;
-    uint32_t in_any = 0u;
+    uint32_t inb = 0u;  // bit e: x[e] lies in the bracket
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float xa = x[2 * j], xb = x[2 * j + 1];
@@ -1560,26 +1560,25 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       all += wa + wb;
       const bool aa = xa > v_lo, ab = xb > v_lo;
       above += (aa ? wa : 0.0f) + (ab ? wb : 0.0f);
-      in_any |= (uint32_t)(xa > v_hi) & (uint32_t)!aa;
-      in_any |= (uint32_t)(xb > v_hi) & (uint32_t)!ab;
+      inb |= ((uint32_t)(xa > v_hi) & (uint32_t)!aa) << (2 * j);
+      inb |= ((uint32_t)(xb > v_hi) & (uint32_t)!ab) << (2 * j + 1);
     }
-    const bool any_in = in_any != 0u;
     above = warp_sum_f(above);
     zacc += (double)all * (double)fu;
     if (lane == 0) sh.w.n.s[u] = above;
-    if (any_in) {  // rare
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (!(x[e] > v_lo) && x[e] > v_hi) {
-          const int pos = atomicAdd(&sh.ncand, 1);
-          if (pos < kSortCap) {
-            sh.w.n.x.g.key[pos] = fkey(x[e]);
-            sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
-          } else {
-            gover = true;
-          }
+    if (inb) {  // the lane's bracket entries: one atomic for all of them
+      int pos = atomicAdd(&sh.ncand, __popc(inb));
+      do {
+        const int e = __ffs(inb) - 1;
+        inb &= inb - 1;
+        if (pos < kSortCap) {
+          sh.w.n.x.g.key[pos] = fkey(st_pick8(x, e));
+          sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
+        } else {
+          gover = true;
         }
-      }
+        ++pos;
+      } while (inb);
     }
   });
   const int n = sh.ncand;  // st_pass ended with a barrier
