@@ -893,18 +893,17 @@ __device__ __forceinline__ void st_record_empty(const SampleArgs &a, int row, ui
 
 // Cost class of row r, longest first: top-p-only 0, top-k 1, full softmax 2,
 // argmax and rows finished without reading the logits 3.
-// Estimated cost class of a row, most expensive first: 0 top-p rows at
-// temperature >= 1 (two passes, and the crossing sits in the dense middle of
-// the distribution, so the bracket is large), 1 the other top-p rows and top-k
-// rows with k >= 128 (many candidate inserts), 2 the other top-k rows and
-// full-softmax rows, 3 argmax rows.
+// Estimated cost class of a row, most expensive first: 0 top-p rows (two
+// passes), 1 top-k rows with k >= 128 (many candidate inserts), 2 the other
+// top-k rows and full-softmax rows, 3 argmax rows.  The first CTAs of a
+// launch land one per SM, so the top-p rows (fewer than the SMs in a typical
+// batch) also avoid sharing an SM with each other.
 __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
   const double T = a.temperature[r];
   const int k = a.top_k[r];
   if (!(T > 0.0) || isinf(T) || k == 1) return 3;
   if (k >= 2 && k < a.V) return k >= 128 ? 1 : 2;
-  if (!(a.top_p[r] < 1.0)) return 2;
-  return T >= 1.0 ? 0 : 1;
+  return a.top_p[r] < 1.0 ? 0 : 2;
 }
 
 // The row CTA blockIdx.x takes: rows ordered by (cost class, index), so the
