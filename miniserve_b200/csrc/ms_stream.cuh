@@ -555,7 +555,7 @@ __device__ void st_sort(uint32_t *key, int *idx, int n, bool by_index) {
 // Index-order inverse CDF over m entries already sorted by index, weight w(i)
 // (zero = not kept).  total is the kept set's weight.  Writes the row.
 template <class W>
-__device__ void st_draw_sorted(StShared &sh, const SampleArgs &a, int row, const int *idx, int m,
+__device__ void st_draw_sorted(StShared &sh, int &rf, const SampleArgs &a, int row, const int *idx, int m,
                                double total, double U, W w) {
   const int tid = threadIdx.x;
   if (!(U > 0.0)) {  // r == 0 stops at index 0 (miniserve/sampler.py:66)
@@ -568,8 +568,8 @@ __device__ void st_draw_sorted(StShared &sh, const SampleArgs &a, int row, const
   double s = 0.0;
   for (int i = p0; i < p1; ++i) s += w(i);
   double ex, inc, tot;
-  block_scan<kStThreads, double>(s, ex, inc, tot, sh.redd);
-  const int who = block_min_i<kStThreads>((s > 0.0 && inc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  st_bscan(sh, rf, s, ex, inc, tot);
+  const int who = st_bmin(sh, rf, (s > 0.0 && inc >= target) ? tid : 0x7FFFFFFF);
   if (who == 0x7FFFFFFF) {  // ran past the end (miniserve/sampler.py:68)
     if (tid == 0)
       write_row(a, row, a.V - 1, (float)((m > 0 && idx[m - 1] == a.V - 1 ? w(m - 1) : 0.0) / total), 0);
@@ -683,7 +683,7 @@ __device__ __forceinline__ uint32_t st_topk_bound_nb(StShared &sh, float rmax, i
 // miniserve/sampler.py:37-44).  Keys below thr cannot rank in that set.  The
 // best m = min(k, entries) land in sh.w.c.key/idx[0..m) in rank order;
 // returns m.  The idle transfer stages hold scratch.  All threads.
-__device__ int st_topk_rank(StShared &sh, int n, int k, uint32_t thr) {
+__device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
   const int tid = threadIdx.x;
   unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
   // (key, ~index) composites: larger = earlier in rank order, all distinct
@@ -694,8 +694,8 @@ __device__ int st_topk_rank(StShared &sh, int n, int k, uint32_t thr) {
   const int f0 = (tid < n && sh.w.c.key[tid] >= thr) ? 1 : 0;
   const int f1 = (i1 < n && sh.w.c.key[i1] >= thr) ? 1 : 0;
   const unsigned long long c0 = f0 ? compose(tid) : 0ull, c1 = f1 ? compose(i1) : 0ull;
-  int ex, inc, n2;
-  block_scan<kStThreads, int>(f0 + f1, ex, inc, n2, sh.redi);
+  int ex, n2;
+  st_bscan_i(sh, rf, f0 + f1, ex, n2);
   if (f0) comp[ex] = c0;
   if (f1) comp[ex + f0] = c1;
   if (tid == 0) comp[n2] = 0ull;  // pad for the paired reads
@@ -722,18 +722,18 @@ __device__ int st_topk_rank(StShared &sh, int n, int k, uint32_t thr) {
 // Exact top-k finish: st_topk_rank, float64 weights exp(l/T - max/T)
 // (miniserve/sampler.py:35,45), top-p in rank order (sampler.py:49-58),
 // index-order draw (sampler.py:60-68).  All threads.
-__device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int n, int k, uint32_t thr,
+__device__ void st_finish_small(StShared &sh, int &rf, const SampleArgs &a, int row, int n, int k, uint32_t thr,
                                 double T, double P, double U, float vmax) {
   const int tid = threadIdx.x;
-  const int m = st_topk_rank(sh, n, k, thr);
+  const int m = st_topk_rank(sh, rf, n, k, thr);
   // thread r holds rank r
   const double xmax = (double)vmax / T;
   const double w = tid < m ? exp((double)key_to_float(sh.w.c.key[tid]) / T - xmax) : 0.0;
   double wex, winc, total;
-  block_scan<kStThreads, double>(w, wex, winc, total, sh.redd);
+  st_bscan(sh, rf, w, wex, winc, total);
   int nkeep = m;
   if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept
-    const int first = block_min_i<kStThreads>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
+    const int first = st_bmin(sh, rf, (tid < m && winc >= P * total) ? tid : 0x7FFFFFFF);
     if (first != 0x7FFFFFFF) nkeep = first + 1;
   }
   // kept entries in index order: position = kept entries of smaller index
@@ -746,8 +746,8 @@ __device__ void st_finish_small(StShared &sh, const SampleArgs &a, int row, int 
     didx[pos] = my;
     dw[pos] = w;
   }
-  const double tot_keep = block_sum<kStThreads>(tid < nkeep ? w : 0.0, sh.redd);
-  st_draw_sorted(sh, a, row, didx, nkeep, tot_keep, U, [&](int i) { return dw[i]; });
+  const double tot_keep = st_bsum(sh, rf, tid < nkeep ? w : 0.0);
+  st_draw_sorted(sh, rf, a, row, didx, nkeep, tot_keep, U, [&](int i) { return dw[i]; });
 }
 
 // Two fp32 values in one 64-bit register.  sm_100 executes add/sub/fma
@@ -1256,8 +1256,10 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       n = ktot;
       thr = kk;
     } else if (n >= 2 * k) {
+      // the k-th largest to 16 leading bits: a lower bound that leaves only
+      // its ties in those bits to the exact ranking
       int above;
-      thr = st_select_kth(sh, sh.w.c.key, n, k, &above);
+      thr = st_select_kth(sh, sh.w.c.key, n, k, &above, 2);
     } else {
       thr = st_topk_bound(sh, rmax, jw);
     }
@@ -1266,7 +1268,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       return;
     }
     if (shard) {  // the slice's top-k, in rank order, with global ids
-      const int m = st_topk_rank(sh, n, k, thr);
+      const int m = st_topk_rank(sh, rf, n, k, thr);
       uint32_t *rec = st_record(a, row);
       for (int i = tid; i < m; i += kStThreads) {
         rec[2 + i] = sh.w.c.key[i];
@@ -1278,7 +1280,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       return;
     }
-    st_finish_small(sh, a, row, n, k, thr, T, P, U, vmax);
+    st_finish_small(sh, rf, a, row, n, k, thr, T, P, U, vmax);
     return;
   }
 
