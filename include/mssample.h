@@ -171,6 +171,20 @@ int ms_json_advance(uint32_t *states, int64_t B, const uint8_t *vocab_bytes, con
 int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
                        int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream);
 
+/* A fixed-width copy of the vocabulary for ms_build_json_mask_packed, made
+ * once per vocabulary: packed [V, 4] u32 (16-byte aligned; token t's first 16
+ * bytes, zero-padded), lens [V] (its length, 255 for tokens longer than 16
+ * bytes, which the mask reads from vocab_bytes).  Same vocabulary layout as
+ * ms_build_json_mask.  An addition to the reference interface (no counterpart
+ * in miniserve/sampler.py): a faster equivalent of ms_build_json_mask. */
+int ms_json_pack_vocab(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V, uint32_t *packed,
+                       uint8_t *lens, ms_stream_t stream);
+/* ms_build_json_mask with token bytes from ms_json_pack_vocab's tables; the
+ * same mask and row_status. */
+int ms_build_json_mask_packed(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                              const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens, int64_t V,
+                              uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream);
+
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);
 

@@ -374,7 +374,29 @@ struct JsonVocab {
   const uint8_t *bytes;
   const int64_t *off;  // [V + 1]
   int64_t V;
+  // optional fixed-width copy (ms_json_pack_vocab): token t's first 16 bytes
+  // in packed[t], its length in lens[t] (kJsonLongToken when longer)
+  const uint4 *packed;
+  const uint8_t *lens;
 };
+
+constexpr uint8_t kJsonLongToken = 255;
+
+// One thread per token: the token's bytes zero-padded to 16 and its length.
+__global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, int64_t V, uint4 *packed,
+                                    uint8_t *lens) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= V) return;
+  const int64_t b = off[t], e = off[t + 1];
+  const int64_t n = e - b;
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  const int m = n < 16 ? (int)n : 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < m) w[i >> 2] |= (uint32_t)bytes[b + i] << (8 * (i & 3));
+  packed[t] = make_uint4(w[0], w[1], w[2], w[3]);
+  lens[t] = n <= 16 ? (uint8_t)n : kJsonLongToken;
+}
 
 __device__ __forceinline__ void j_load_state(const uint32_t *g, uint32_t *sbits, JState &st) {
   const uint4 h = *reinterpret_cast<const uint4 *>(g);
@@ -431,8 +453,19 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     if (t < voc.V) {
       JState st = st0;
       JStackTok stk(sbits, st0.depth);
-      const int64_t b = voc.off[t], e = voc.off[t + 1];
-      for (int64_t i = b; i < e && !st.decided && !stk.over; ++i) j_step(st, stk, voc.bytes[i]);
+      const int nb = voc.lens ? voc.lens[t] : kJsonLongToken;
+      if (nb != kJsonLongToken) {  // the bytes from registers, low byte first
+        const uint4 q = voc.packed[t];
+        uint64_t lo = (uint64_t)q.x | ((uint64_t)q.y << 32), hi = (uint64_t)q.z | ((uint64_t)q.w << 32);
+        for (int i = 0; i < nb && !st.decided && !stk.over; ++i) {
+          j_step(st, stk, (uint8_t)lo);
+          lo = (lo >> 8) | (hi << 56);
+          hi >>= 8;
+        }
+      } else {
+        const int64_t b = voc.off[t], e = voc.off[t + 1];
+        for (int64_t i = b; i < e && !st.decided && !stk.over; ++i) j_step(st, stk, voc.bytes[i]);
+      }
       r = stk.over ? (uint8_t)J_UNDECIDED : j_finish(st, stk);
       my_flags |= r == J_RAISE ? 1 : (stk.over ? 2 : 0);
     }

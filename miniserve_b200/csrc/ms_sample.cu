@@ -213,11 +213,14 @@ int ms_json_advance(uint32_t *states, int64_t B, const uint8_t *vocab_bytes, con
   return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
 
-int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
-                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
+namespace {
+int build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                    const uint32_t *packed, const uint8_t *lens, int64_t V, uint32_t *mask, int64_t mask_ld,
+                    int32_t *row_status, ms_stream_t stream) {
   if (B < 0 || B > 65535 || V < 1 || V > 0x7FFFFFFFll || mask_ld < (V + 31) / 32) return MS_E_INVALID;
   if (B == 0) return MS_OK;
   if (!states || !vocab_bytes || !vocab_off || !mask || !row_status) return MS_E_INVALID;
+  if ((packed == nullptr) != (lens == nullptr) || (reinterpret_cast<uintptr_t>(packed) & 15u)) return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(row_status, 0, (size_t)B * sizeof(int32_t), s);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -227,11 +230,37 @@ int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_b
   x = x < 1 ? 1 : x;
   const int64_t xmax = (nwords + ms::kJsonThreads / 32 - 1) / (ms::kJsonThreads / 32);
   x = x > xmax ? xmax : x;
-  ms::JsonVocab voc{vocab_bytes, vocab_off, V};
+  ms::JsonVocab voc{vocab_bytes, vocab_off, V, reinterpret_cast<const uint4 *>(packed), lens};
   ms::ms_json_mask_kernel<<<dim3((unsigned)x, (unsigned)B), ms::kJsonThreads, 0, s>>>(states, voc, mask, mask_ld,
                                                                                        row_status);
   e = cudaGetLastError();
   return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+}  // namespace
+
+int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
+  return build_json_mask(states, B, vocab_bytes, vocab_off, nullptr, nullptr, V, mask, mask_ld, row_status, stream);
+}
+
+int ms_json_pack_vocab(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V, uint32_t *packed,
+                       uint8_t *lens, ms_stream_t stream) {
+  if (V < 1 || V > 0x7FFFFFFFll) return MS_E_INVALID;
+  if (!vocab_bytes || !vocab_off || !packed || !lens || (reinterpret_cast<uintptr_t>(packed) & 15u)) {
+    return MS_E_INVALID;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ms::ms_json_pack_kernel<<<(unsigned)((V + 255) / 256), 256, 0, s>>>(vocab_bytes, vocab_off, V,
+                                                                     reinterpret_cast<uint4 *>(packed), lens);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_build_json_mask_packed(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                              const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens, int64_t V,
+                              uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
+  if (!packed || !lens) return MS_E_INVALID;
+  return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, V, mask, mask_ld, row_status, stream);
 }
 
 }  // extern "C"

@@ -39,6 +39,12 @@ class JsonMaskBuilder:
         self.V = len(vocab)
         self.vocab_bytes, self.vocab_off = _pack_texts(vocab, self.device)
         self.words = int(_lib.lib().ms_json_state_words())
+        # fixed-width copy of the vocabulary (16 bytes a token) for the mask
+        self.packed = torch.empty((self.V, 4), dtype=torch.int32, device=self.device)
+        self.lens = torch.empty(self.V, dtype=torch.uint8, device=self.device)
+        rc = _lib.lib().ms_json_pack_vocab(self.vocab_bytes.data_ptr(), self.vocab_off.data_ptr(), self.V,
+                                           self.packed.data_ptr(), self.lens.data_ptr(), self._stream())
+        _lib.check(rc, "ms_json_pack_vocab")
 
     def _stream(self):
         return _torch().cuda.current_stream(self.device).cuda_stream
@@ -61,15 +67,24 @@ class JsonMaskBuilder:
                                         self.vocab_off.data_ptr(), self.V, t.data_ptr(), self._stream())
         _lib.check(rc, "ms_json_advance")
 
-    def build(self, states, out=None) -> Tuple["object", "object"]:
-        """(mask [B, ceil(V/32)] int32, row_status [B] int32)."""
+    def build(self, states, out=None, packed: bool = True) -> Tuple["object", "object"]:
+        """(mask [B, ceil(V/32)] int32, row_status [B] int32).  packed=False
+        reads every token from the variable-length vocabulary instead of the
+        fixed-width copy (same result)."""
         torch = _torch()
         B = states.shape[0]
         W = (self.V + 31) // 32
         mask = torch.empty((B, W), dtype=torch.int32, device=self.device) if out is None else out
         status = torch.empty(B, dtype=torch.int32, device=self.device)
-        rc = _lib.lib().ms_build_json_mask(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
-                                           self.vocab_off.data_ptr(), self.V, mask.data_ptr(), mask.stride(0),
-                                           status.data_ptr(), self._stream())
-        _lib.check(rc, "ms_build_json_mask")
+        if packed:
+            rc = _lib.lib().ms_build_json_mask_packed(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
+                                                      self.vocab_off.data_ptr(), self.packed.data_ptr(),
+                                                      self.lens.data_ptr(), self.V, mask.data_ptr(), mask.stride(0),
+                                                      status.data_ptr(), self._stream())
+            _lib.check(rc, "ms_build_json_mask_packed")
+        else:
+            rc = _lib.lib().ms_build_json_mask(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
+                                               self.vocab_off.data_ptr(), self.V, mask.data_ptr(), mask.stride(0),
+                                               status.data_ptr(), self._stream())
+            _lib.check(rc, "ms_build_json_mask")
         return mask, status

@@ -109,6 +109,27 @@ def test_advance_matches_init(torch):
     np.testing.assert_array_equal(m1.cpu().numpy(), m2.cpu().numpy())
 
 
+def test_packed_matches_unpacked(torch):
+    """The fixed-width vocabulary path gives the same masks and statuses as the
+    variable-length one, tokens longer than 16 bytes included."""
+    from miniserve_b200 import workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    vocab = workloads.json_vocab(4, 20000)
+    rng = random.Random(3)
+    for i in range(0, len(vocab), 97):  # some long tokens (17-40 bytes)
+        vocab[i] = "".join(rng.choice('{}[]:," 0123456789.eE-truefalsn\\') for _ in range(rng.randint(17, 40)))
+    prefixes = workloads.json_prefixes(4, 96)
+    b = JsonMaskBuilder(vocab)
+    s = b.init(prefixes)
+    m1, st1 = b.build(s, packed=True)
+    m2, st2 = b.build(s, packed=False)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(m1.cpu().numpy(), m2.cpu().numpy())
+    np.testing.assert_array_equal(st1.cpu().numpy(), st2.cpu().numpy())
+    lens = b.lens.cpu().numpy()
+    assert (lens == 255).sum() == sum(len(v.encode()) > 16 for v in vocab)
+
+
 def test_config4_masked_sampling(torch):
     """Config 4 end to end: masks on the GPU, masked sampling vs the C oracle
     with the same mask."""
