@@ -51,6 +51,11 @@ constexpr int kCandCap = 6144;                  // top-k candidate buffer entrie
 constexpr int kSortCap = 4096;                  // largest set st_sort handles
 constexpr int kRankCap = 1024;                  // largest set sorted by rank counting
 constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
+// top-k loop: chunks whose warp bounds refresh tau (0-2, then every 4th) and
+// chunks that select the buffer's k-th largest (3, 11); a row has at most 64
+// chunks
+constexpr unsigned long long kRefreshChunks = 0x1111111111111117ull;
+constexpr unsigned long long kSelectChunks = (1ull << 3) | (1ull << 11);
 constexpr int kMaxUnits = 1024;                 // per-unit summaries kept per row
 constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
 constexpr int kXBins = 4096;                    // x-grid bins per kSXRange (top-p)
@@ -86,7 +91,6 @@ struct StShared {
     } n;
   } w;
   uint32_t wbound[kStWarps];
-  int wcnt[2][kStWarps];  // per-warp insert counts of the last two chunks
   int pick[kStWarps][4];  // row ordering: per-warp class counts
   int ptot[4];
   alignas(16) uint32_t sel[4][256];  // st_select_kth: one digit histogram per round
@@ -1121,7 +1125,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
     bool exact_tau = false;  // tau is the k-th largest value seen (after a compaction)
-    int ncand = 0;           // exact buffer size, identical in every thread
+    int ub = 0;  // bound on the buffer's size (its size after a sync point), the same in every thread
     if (tid == 0) {
       for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_stream);
     }
@@ -1133,7 +1137,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       const int g0 = st_get8<DT>(sh, r, c, s, x);
       const float cm = st_max8n(x);
       rmax = st_maxn(rmax, cm);
-      if (!exact_tau && (c < 3 || (c & 3) == 0)) {
+      if (!exact_tau && ((kRefreshChunks >> c) & 1u)) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
         if (bmin != 0u && key_to_float(bmin) > tau) set_tau(key_to_float(bmin), false);
       }
@@ -1155,54 +1159,57 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
           ++pos;
         } while (m);
       }
-      const int wt = __reduce_add_sync(0xFFFFFFFFu, cnt);
-      if (lane == 0) sh.wcnt[c & 1][tid >> 5] = wt;
-      __syncthreads();  // stage s is free; the buffer is settled
+      // barrier: stage s is free and the buffer settled; every inserting lane
+      // added at most 8 entries
+      ub += 8 * __syncthreads_count(cnt > 0);
       // refill stage s first, so the copy runs under a select or compaction
       if (tid == 0 && c + kStages < r.nchunks) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         st_issue<DT>(sh, r, c + kStages, s, pol_stream);
       }
-      // exact count from the per-warp slots (slot c&1 is rewritten two chunks
-      // on, after a barrier every thread has passed)
-      ncand += __reduce_add_sync(0xFFFFFFFFu, lane < kStWarps ? sh.wcnt[c & 1][lane] : 0);
-      // early on (chunks 3 and 11) the buffer's k-th largest, to 16 leading
-      // bits (two digit rounds; a lower bound within 2^-7 of it), is a far
-      // tighter tau than the warp bound and cuts the inserts of the rest of
-      // the row; entries below it stay in the buffer, dead
-      if ((c == 3 || c == 11) && ncand >= 2 * k && ncand <= kCandCap - kChunk) {
-        int above;
-        set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, ncand, k, &above, 2)), false);
-        exact_tau = true;
-      }
-      // shrink to the entries >= the buffer's k-th largest (ties kept) when the
-      // next chunk could overflow the buffer
-      if (ncand > kCandCap - kChunk) {
-        const int n0 = ncand;
-        int above;
-        const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
-        uint32_t kv[kCandCap / kStThreads];
-        int iv[kCandCap / kStThreads];
-        int nk = 0;
-        for (int i = tid; i < n0; i += kStThreads) {
-          if (sh.w.c.key[i] >= kk) {
-            kv[nk] = sh.w.c.key[i];
-            iv[nk] = sh.w.c.idx[i];
-            ++nk;
-          }
-        }
-        int kex, kin, ktot;
-        block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
-        for (int q = 0; q < nk; ++q) {
-          sh.w.c.key[kex + q] = kv[q];
-          sh.w.c.idx[kex + q] = iv[q];
-        }
-        if (tid == 0) sh.ncand = ktot;
+      const bool sel_pt = (kSelectChunks >> c) & 1u;
+      if (sel_pt || ub > kCandCap - kChunk) {
+        // a sync point: every thread reads the exact size before any inserts again
+        const int n0 = sh.ncand;
         __syncthreads();
-        ncand = ktot;
-        set_tau(key_to_float(kk), true);  // >= k entries >= kk are held: a later equal value ranks below
-        exact_tau = true;
-        if (ktot > kCandCap - kChunk) over = true;  // heavy ties
+        ub = n0;
+        // early on (chunks 3 and 11) the buffer's k-th largest, to 16 leading
+        // bits (two digit rounds; a lower bound within 2^-7 of it), is a far
+        // tighter tau than the warp bound and cuts the inserts of the rest of
+        // the row; entries below it stay in the buffer, dead
+        if (sel_pt && n0 >= 2 * k && n0 <= kCandCap - kChunk) {
+          int above;
+          set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, n0, k, &above, 2)), false);
+          exact_tau = true;
+        }
+        // shrink to the entries >= the buffer's k-th largest (ties kept) when
+        // the next chunk could overflow the buffer
+        if (n0 > kCandCap - kChunk) {
+          int above;
+          const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
+          uint32_t kv[kCandCap / kStThreads];
+          int iv[kCandCap / kStThreads];
+          int nk = 0;
+          for (int i = tid; i < n0; i += kStThreads) {
+            if (sh.w.c.key[i] >= kk) {
+              kv[nk] = sh.w.c.key[i];
+              iv[nk] = sh.w.c.idx[i];
+              ++nk;
+            }
+          }
+          int kex, kin, ktot;
+          block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
+          for (int q = 0; q < nk; ++q) {
+            sh.w.c.key[kex + q] = kv[q];
+            sh.w.c.idx[kex + q] = iv[q];
+          }
+          if (tid == 0) sh.ncand = ktot;
+          __syncthreads();
+          ub = ktot;
+          set_tau(key_to_float(kk), true);  // >= k entries >= kk are held: a later equal value ranks below
+          exact_tau = true;
+          if (ktot > kCandCap - kChunk) over = true;  // heavy ties
+        }
       }
       if (over) break;
     }
@@ -1231,7 +1238,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // exact top-k of the buffer; fewer valid tokens than top_k keep all.  thr:
     // keys below it cannot rank in the top-k set (the buffer's k-th largest
     // when the buffer is large, else the warp bound)
-    int n = ncand;
+    int n = sh.ncand;  // no insert since the barriers above
     uint32_t thr;
     if (n > kRankCap) {
       int above;
