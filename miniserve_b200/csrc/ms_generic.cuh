@@ -48,6 +48,12 @@ struct SampleArgs {
   int kmax = 0;
   int64_t v0 = 0;
   int64_t Vg = 0;
+  // pair mode: the streaming kernel runs as clusters of two CTAs;
+  // top-p rows are shared by the two CTAs of a cluster when the batch leaves
+  // room: B + (top-p rows) <= slots (CTAs the GPU holds at once)
+  int pairs = 0;
+  int slots = 0;
+  int rows = 0;  // B (pair mode)
 };
 
 template <int DT>

@@ -43,7 +43,28 @@ cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int de
     if (e != cudaSuccess) return e;
     ready[dev].store(1, std::memory_order_release);
   }
-  ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
+  if (!a.pairs) {
+    ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
+    return cudaGetLastError();
+  }
+  // pair mode: clusters of two CTAs.  Work items (a shared top-p row or two
+  // rows) number at most (B + top-p rows) / 2 + 1 <= slots / 2 + 1 when rows
+  // are shared, and one row per CTA needs B <= slots CTAs otherwise
+  const int clusters = B < a.slots / 2 + 1 ? B : a.slots / 2 + 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.blockDim = dim3(ms::kStThreads);
+  cfg.dynamicSmemBytes = sizeof(ms::StShared);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, ms::ms_stream_kernel<DT>, a);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -55,10 +76,16 @@ cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, 
     ms::ms_generic_kernel<DT><<<dim3((unsigned)B), dim3(ms::kGenThreads), 0, s>>>(a, nullptr, nullptr);
     return cudaGetLastError();
   }
-  cudaError_t e = launch_stream<DT>(a, B, s, dev);
-  if (e != cudaSuccess) return e;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // a batch of at most one row per SM runs in pair mode, where top-p rows take
+  // two CTAs each (larger batches keep the GPU's CTA slots busy without it)
+  ms::SampleArgs ap = a;
+  ap.slots = 2 * sms;
+  ap.pairs = B <= sms ? 1 : 0;
+  ap.rows = B;
+  cudaError_t e = launch_stream<DT>(ap, B, s, dev);
+  if (e != cudaSuccess) return e;
   const int grid = B < sms ? B : sms;
   // a programmatic dependent launch: the pending pass is launched while the
   // streaming kernel's last CTAs run and waits (griddepcontrol.wait) for that

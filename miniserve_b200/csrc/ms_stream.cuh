@@ -106,6 +106,17 @@ struct StShared {
   double bcast_d[4];
   int ncand;
   int nhigh;
+  struct {  // written by the partner CTA of a shared row, one slot per exchange
+    float j1_g;
+    uint32_t j2_flags;
+    float j2_vmax;
+    int j2_nhigh;
+    uint32_t j2b_flags;
+    double j3_H;
+    int j4_n;
+    uint32_t j4_flags;
+    double j5_z;
+  } xch;
 };
 
 // ------------------------------------------------------------- the stream
@@ -117,10 +128,45 @@ struct StRow {
   bool tma;             // 16-byte aligned row: chunks arrive by TMA
   int nchunks;
   int nfull;            // leading chunks delivered whole by TMA
+  int cb, ce;           // the chunks this CTA streams: [cb, ce)
 };
 
 __device__ __forceinline__ uint32_t st_smem(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---- clusters of two CTAs sharing a top-p row (pair mode).  Data crosses
+// between the two CTAs only as stores into the partner's shared memory
+// followed by st_cluster_sync, which every thread of both CTAs reaches at the
+// same points of the shared row's code.
+__device__ __forceinline__ uint32_t st_crank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the partner CTA's shared-memory address of p
+__device__ __forceinline__ uint32_t st_peer(const void *p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(st_smem(p)), "r"(st_crank() ^ 1u));
+  return r;
+}
+__device__ __forceinline__ void st_peer_u32(uint32_t ra, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ra), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_peer_f32(uint32_t ra, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_peer_f64(uint32_t ra, double v) {
+  asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(ra), "d"(v) : "memory");
+}
+__device__ __forceinline__ void st_peer_v4(uint32_t ra, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+// every thread of both CTAs; stores before it are visible to both after it
+__device__ __forceinline__ void st_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t st_ns() {
@@ -328,16 +374,17 @@ __device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph
   const int tid = threadIdx.x;
   bool ok = true;
   if (tid == 0) {
-    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int c = r.cb; c < r.cb + kStages && c < r.ce; ++c) st_issue<DT>(sh, r, c, c - r.cb, pol);
   }
-  for (int c = 0, s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
+  for (int c = r.cb, s = 0; c < r.ce; ++c, s = s == kStages - 1 ? 0 : s + 1) {
     if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
     ph ^= 1u << s;
     float x[8];
     const int g0 = st_get8<DT>(sh, r, c, s, x);
     body(x, g0, c * kStWarps + (tid >> 5));
     __syncthreads();  // every thread is done with stage s
-    if (tid == 0 && c + kStages < r.nchunks) {
+    if (tid == 0 && c + kStages < r.ce) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       st_issue<DT>(sh, r, c + kStages, s, pol);
     }
@@ -910,10 +957,15 @@ __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
   return a.top_p[r] < 1.0 ? 0 : 2;
 }
 
-// The row CTA blockIdx.x takes: rows ordered by (cost class, index), so the
-// CTAs launched first take the longest rows and the batch ends with short
-// ones.  Every CTA computes the same order from the per-row parameters.
-__device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B) {
+// The row this CTA takes, from the rows ordered by (cost class, index), so
+// the CTAs launched first take the longest rows and the batch ends with short
+// ones; -1 for none.  Every CTA computes the same order from the per-row
+// parameters.  One CTA per row: CTA i takes position i.  Pair mode (clusters
+// of two CTAs): cluster i takes work item i - the i-th top-p row,
+// shared by both CTAs (*joint set), or after those, the next two positions,
+// one per CTA (when B plus the top-p rows exceeds the GPU's CTA slots, one
+// row per CTA as without pairs).
+__device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < 4) sh.ptot[tid] = 0;
   __syncthreads();
@@ -936,8 +988,21 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B) {
     atomicAdd(&sh.ptot[3], n3);
   }
   __syncthreads();
-  if (sh.ptot[0] == B || sh.ptot[1] == B || sh.ptot[2] == B || sh.ptot[3] == B) return blockIdx.x;
-  const int want = blockIdx.x;
+  int want = blockIdx.x;
+  *joint = false;
+  if (a.pairs) {
+    const int item = blockIdx.x >> 1, np = sh.ptot[0];
+    if (B + np > a.slots) {  // no room to share: one row per CTA
+      if (want >= B) return -1;
+    } else if (item < np) {
+      want = item;
+      *joint = true;
+    } else {
+      want = np + 2 * (item - np) + (int)st_crank();
+      if (want >= B) return -1;
+    }
+  }
+  if (sh.ptot[0] == B || sh.ptot[1] == B || sh.ptot[2] == B || sh.ptot[3] == B) return want;
   int base[4];
   base[0] = 0;
   base[1] = sh.ptot[0];
@@ -986,7 +1051,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // every CTA of this grid has started: a programmatic dependent launch (the
   // pending-row pass) may begin launching
   asm volatile("griddepcontrol.launch_dependents;");
-  const int row = st_pick_row(sh, a, (int)gridDim.x);
+  bool joint;
+  const int row = st_pick_row(sh, a, a.pairs ? a.rows : (int)gridDim.x, &joint);
+  if (row < 0) return;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const double T = a.temperature[row];
@@ -995,6 +1062,16 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const double U = a.uniforms[row];
   const int V = a.V;
   const bool shard = a.records != nullptr;
+  const int crank = joint ? (int)st_crank() : 0;
+  if (joint) {
+    // a top-p row is shared when both halves stream at least one chunk and
+    // the row takes the streaming path; otherwise the first CTA takes it alone
+    const bool share = T >= kMinTemperature && !isinf(T) && !(k >= 1 && k < V) && P < 1.0 && V > kChunk && !shard;
+    if (!share) {
+      if (crank == 1) return;
+      joint = false;
+    }
+  }
   if (!(T >= 0.0) || isinf(T)) {  // negative, NaN or infinite temperature
     if (tid == 0) {
       if (shard) st_record_empty(a, row, MS_ROW_BAD_TEMPERATURE);
@@ -1039,6 +1116,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   r.V = V;
   r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
   r.nchunks = (V + kChunk - 1) / kChunk;
+  r.cb = joint && crank == 1 ? r.nchunks / 2 : 0;
+  r.ce = joint && crank == 0 ? r.nchunks / 2 : r.nchunks;
   r.nfull = r.tma ? V / kChunk : 0;
   if (tid < kStages) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
@@ -1438,9 +1517,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   float vmax_t = -INFINITY;  // NaN once a NaN has been seen
   hist_clear();
   if (tid == 0) {
-    for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_keep);
+    for (int c = r.cb; c < r.cb + kStages && c < r.ce; ++c) st_issue<DT>(sh, r, c, c - r.cb, pol_keep);
   }
-  for (int c = 0, s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
+  for (int c = r.cb, s = 0; c < r.ce; ++c, s = s == kStages - 1 ? 0 : s + 1) {
     if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
     ph ^= 1u << s;
     float x[8];
@@ -1449,22 +1528,54 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     vmax_t = st_maxn(vmax_t, cm);
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
     if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
-    if (c == 0) set_anchor(block_max_f<kStThreads>(cm, sh.redf));
+    if (c == r.cb) {
+      float g = block_max_f<kStThreads>(cm, sh.redf);
+      if (joint) {  // one anchor for both halves: the larger first-chunk maximum
+        if (tid == 0) st_peer_f32(st_peer(&sh.xch.j1_g), g);
+        st_cluster_sync();
+        g = fmaxf(g, sh.xch.j1_g);
+      }
+      set_anchor(g);
+    }
     if (G > -INFINITY) hist8(x, g0, cm);  // block-uniform
     __syncthreads();  // every thread is done with stage s
-    if (tid == 0 && c + kStages < r.nchunks) {
+    if (tid == 0 && c + kStages < r.ce) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       st_issue<DT>(sh, r, c + kStages, s, pol_keep);
     }
   }
   ok = __syncthreads_and(ok) != 0;
   float vmax;
-  if (!finish_max(vmax_t, vmax)) return;
-  for (int u = tid; u < nu; u += kStThreads) {
+  int nhigh_all = sh.nhigh;
+  if (!joint) {
+    if (!finish_max(vmax_t, vmax)) return;
+  } else {
+    // both halves: NaN / +inf, failed copies, the maximum, the high lists
+    const bool badc = __syncthreads_or(st_bad(vmax_t)) != 0;
+    const float vm = block_max_f<kStThreads>(vmax_t, sh.redf);
+    if (tid == 0) {
+      st_peer_u32(st_peer(&sh.xch.j2_flags), (badc ? 1u : 0u) | (ok ? 0u : 2u));
+      st_peer_f32(st_peer(&sh.xch.j2_vmax), vm);
+      st_peer_u32(st_peer(&sh.xch.j2_nhigh), (uint32_t)sh.nhigh);
+    }
+    st_cluster_sync();
+    const uint32_t pf = sh.xch.j2_flags;
+    vmax = fmaxf(vm, sh.xch.j2_vmax);
+    nhigh_all += sh.xch.j2_nhigh;
+    const int stop = (badc || !ok || pf != 0u) ? 1 : !(vmax > -INFINITY) ? 2 : !(fabs((double)vmax) * cl < 1e37) ? 1 : 0;
+    if (stop) {  // both CTAs stop here
+      if (crank == 0 && tid == 0) {
+        if (stop == 2) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);  // every logit -inf (sampler.py:46-47)
+        else a.status[row] = kRowPending;
+      }
+      return;
+    }
+  }
+  for (int u = r.cb * kStWarps + tid; u < r.ce * kStWarps; u += kStThreads) {
     const float mu = sh.w.n.m[u];
     sh.w.n.f[u] = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
   }
-  if (!(G > -INFINITY) || sh.nhigh > kHighCap) {
+  if (!(G > -INFINITY) || nhigh_all > kHighCap) {
     // chunk 0 held no finite logit, or many values lie far above its max:
     // histogram pass (L2) anchored at the row maximum, nothing above it
     __syncthreads();
@@ -1473,8 +1584,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
       hist8(x, g0, st_max8n(x));
     });
+    if (joint) {
+      if (tid == 0) st_peer_u32(st_peer(&sh.xch.j2b_flags), ok ? 0u : 1u);
+      st_cluster_sync();
+      ok = ok && sh.xch.j2b_flags == 0u;
+    }
     if (!ok) {
-      if (tid == 0) a.status[row] = kRowPending;
+      if (crank == 0 && tid == 0) a.status[row] = kRowPending;
       return;
     }
   }
@@ -1483,7 +1599,20 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const int nh = min(sh.nhigh, kHighCap);
   double hs = 0.0;
   for (int i = tid; i < nh; i += kStThreads) hs += unit_w(key_to_float(sh.w.n.hkey[i]), sh.w.n.hidx[i]);
-  const double H = block_sum<kStThreads>(hs, sh.redd);
+  double H = block_sum<kStThreads>(hs, sh.redd);
+  if (joint) {
+    // one histogram and one high-list mass for both halves: each CTA copies
+    // its histogram into the partner's idle stages and adds the partner's copy
+    const uint4 *h4 = reinterpret_cast<const uint4 *>(hq);
+    const uint32_t dst = st_peer(sh.stage[0]);
+    for (int i = tid; i < kQSlots / 4; i += kStThreads) st_peer_v4(dst + 16u * (uint32_t)i, h4[i]);
+    if (tid == 0) st_peer_f64(st_peer(&sh.xch.j3_H), H);
+    st_cluster_sync();
+    const uint32_t *rcv = reinterpret_cast<const uint32_t *>(sh.stage[0]);
+    for (int i = tid; i < kQSlots; i += kStThreads) hq[i] += rcv[i];
+    H = crank == 0 ? H + sh.xch.j3_H : sh.xch.j3_H + H;  // the same sum in both CTAs
+    __syncthreads();
+  }
   // the bracket [i_lo, i_hi] of indices (-1 = the high list, kSBins + 1 =
   // the tail): where the estimated running mass crosses P*total -/+
   // kHistTol*total.
@@ -1589,8 +1718,44 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       } while (inb);
     }
   });
-  const int n = sh.ncand;  // st_pass ended with a barrier
-  if (__syncthreads_or(!ok || gover)) {  // a crowded bracket: generic kernel
+  int n = sh.ncand;  // st_pass ended with a barrier
+  const bool failc = __syncthreads_or(!ok || gover) != 0;  // a crowded bracket: generic kernel
+  double zpeer = 0.0;
+  if (joint) {
+    if (tid == 0) {
+      st_peer_u32(st_peer(&sh.xch.j4_n), (uint32_t)n);
+      st_peer_u32(st_peer(&sh.xch.j4_flags), failc ? 1u : 0u);
+    }
+    st_cluster_sync();
+    const int np = sh.xch.j4_n;
+    if (failc || sh.xch.j4_flags != 0u || n + np > kSortCap) {  // both CTAs stop here
+      if (crank == 0 && tid == 0) a.status[row] = kRowPending;
+      return;
+    }
+    if (crank == 1) {
+      // hand the second half to the first CTA: its bracket entries after the
+      // first CTA's, its units' maxima, scales and masses above the bracket,
+      // and its share of the total
+      const double zc = st_bsum(sh, rf, zacc);
+      const uint32_t gk_p = st_peer(sh.w.n.x.g.key), gi_p = st_peer(sh.w.n.x.g.idx);
+      for (int i = tid; i < n; i += kStThreads) {
+        st_peer_u32(gk_p + 4u * (uint32_t)(np + i), sh.w.n.x.g.key[i]);
+        st_peer_u32(gi_p + 4u * (uint32_t)(np + i), (uint32_t)sh.w.n.x.g.idx[i]);
+      }
+      const uint32_t m_p = st_peer(sh.w.n.m), s_p = st_peer(sh.w.n.s), f_p = st_peer(sh.w.n.f);
+      for (int u = r.cb * kStWarps + tid; u < r.ce * kStWarps; u += kStThreads) {
+        st_peer_f32(m_p + 4u * (uint32_t)u, sh.w.n.m[u]);
+        st_peer_f32(s_p + 4u * (uint32_t)u, sh.w.n.s[u]);
+        st_peer_f32(f_p + 4u * (uint32_t)u, sh.w.n.f[u]);
+      }
+      if (tid == 0) st_peer_f64(st_peer(&sh.xch.j5_z), zc);
+      st_cluster_sync();
+      return;
+    }
+    st_cluster_sync();
+    n += np;
+    zpeer = sh.xch.j5_z;
+  } else if (failc) {
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
@@ -1598,6 +1763,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
   double total, above_tot;
   st_bsum2(sh, rf, zacc, as, total, above_tot);
+  total += zpeer;  // the second half's share, when the row was shared
   const double pz = P * total;
   if (above_tot > 0.0 && above_tot >= pz) {  // the crossing lies above the bracket
     if (tid == 0) a.status[row] = kRowPending;
