@@ -69,6 +69,32 @@ def test_config_rows_vs_reference(sampler, name):
     assert np.array_equal(tok[strict], want[strict]), (tok, want)
 
 
+@pytest.mark.parametrize("bf16", [False, True])
+def test_pair_mode_batches(sampler, bf16):
+    """Batches of at most one row per SM run the streaming kernel as clusters
+    of two CTAs: top-p rows are shared by both CTAs (each streams half the
+    row), the other rows go two to a cluster.  A mixed batch, and a batch of
+    top-p-only rows at high temperature (large brackets), against the oracle."""
+    from miniserve_b200 import workloads
+    b = workloads.config3(3)
+    x = b.logits[:140]
+    if bf16:
+        x = (x.view(np.uint32) >> 16).astype(np.uint16)  # truncated to bf16 bits
+    tok, prob, st = gpu_sample(sampler, x, b.temperature[:140], b.top_k[:140], b.top_p[:140],
+                               b.uniforms[:140], bf16=bf16)
+    compare(tok, prob, st, x, b.temperature[:140], b.top_k[:140], b.top_p[:140], b.uniforms[:140],
+            bf16=bf16, label="pair mode mixed B=140")
+    rng = np.random.default_rng(9)
+    T = 1.0 + 0.5 * rng.random(96)
+    K = np.zeros(96, np.int32)
+    P = 0.6 + 0.39 * rng.random(96)
+    xr = b.logits[200:296]
+    if bf16:
+        xr = (xr.view(np.uint32) >> 16).astype(np.uint16)
+    tok, prob, st = gpu_sample(sampler, xr, T, K, P, b.uniforms[200:296], bf16=bf16)
+    compare(tok, prob, st, xr, T, K, P, b.uniforms[200:296], bf16=bf16, label="pair mode top-p B=96")
+
+
 def test_config3_full_batch(sampler):
     from miniserve_b200 import workloads
     b = workloads.config3(3)
