@@ -432,12 +432,61 @@ __global__ void ms_json_feed_kernel(uint32_t *states, int64_t B, const uint8_t *
 // packs the 32 answers into one word.  row_status bits: 1 = some token makes
 // the reference raise (its bit is 0), 2 = some token opens or closes more
 // containers than JStackTok holds (its bit is 0).
+// Rows in the same parse state get the same mask.  Row b's representative is
+// the first row whose state is identical (header and the first `depth` stack
+// bits); it is written as (rep + 1) << 8 into row_status[b], whose low byte
+// collects the row's flags later.  Batches above kJsonDedupMax rows skip the
+// search (every row its own representative).
+constexpr int kJsonDedupMax = 1024;
+__device__ __forceinline__ bool j_same_state(const uint32_t *x, const uint32_t *y) {
+  for (int i = 0; i < kJsonHeaderWords; ++i)
+    if (x[i] != y[i]) return false;
+  const int depth = (int)x[2];  // JState::depth
+  const int words = depth >> 5, rem = depth & 31;
+  for (int i = 0; i < words; ++i)
+    if (x[kJsonHeaderWords + i] != y[kJsonHeaderWords + i]) return false;
+  return rem == 0 || ((x[kJsonHeaderWords + words] ^ y[kJsonHeaderWords + words]) & ((1u << rem) - 1u)) == 0u;
+}
+__global__ void ms_json_dedup_kernel(const uint32_t *states, int64_t B, int32_t *row_status) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int64_t rep = b;
+  if (B <= kJsonDedupMax) {
+    const uint32_t *x = states + b * kJsonStateWords;
+    for (int64_t c = 0; c < b; ++c) {
+      if (j_same_state(x, states + c * kJsonStateWords)) {
+        rep = c;
+        break;
+      }
+    }
+  }
+  row_status[b] = (int32_t)((rep + 1) << 8);
+}
+
+// Rows that share a representative take its mask; every row's status keeps
+// only its flags.  One CTA per row.
+__global__ void ms_json_mask_copy_kernel(uint32_t *mask, int64_t mask_ld, int64_t nwords, int32_t *row_status) {
+  const int64_t row = blockIdx.x;
+  const int32_t v = row_status[row];
+  const int64_t rep = (int64_t)(v >> 8) - 1;
+  if (rep != row) {
+    const uint32_t *src = mask + rep * mask_ld;
+    uint32_t *dst = mask + row * mask_ld;
+    for (int64_t i = threadIdx.x; i < nwords; i += blockDim.x) dst[i] = src[i];
+  }
+  // the representative's low byte (its flags) is final; this kernel only
+  // clears high bytes
+  if (threadIdx.x == 0) row_status[row] = (rep != row ? row_status[rep] : v) & 0xFF;
+}
+
 __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32_t *states, JsonVocab voc,
                                                                     uint32_t *mask, int64_t mask_ld,
                                                                     int32_t *row_status) {
   __shared__ uint32_t sbits[kJsonStackWords];
   __shared__ int flags;
   const int row = blockIdx.y;
+  // a row in the same state as an earlier row: ms_json_mask_copy_kernel fills it
+  if ((row_status[row] >> 8) - 1 != row) return;
   const uint32_t *g = states + (int64_t)row * kJsonStateWords;
   JState st0;
   j_load_state(g, sbits, st0);
@@ -474,7 +523,7 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
   }
   if (my_flags) atomicOr(&flags, my_flags);
   __syncthreads();
-  if (threadIdx.x == 0 && flags) atomicOr(row_status + row, flags);  // row_status zeroed by the caller
+  if (threadIdx.x == 0 && flags) atomicOr(row_status + row, flags);  // low byte: the flags
 }
 
 }  // namespace ms

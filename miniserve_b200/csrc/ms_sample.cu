@@ -249,17 +249,23 @@ int build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_byte
   if (!states || !vocab_bytes || !vocab_off || !mask || !row_status) return MS_E_INVALID;
   if ((packed == nullptr) != (lens == nullptr) || (reinterpret_cast<uintptr_t>(packed) & 15u)) return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(row_status, 0, (size_t)B * sizeof(int32_t), s);
+  // rows in the same parse state share one mask: representatives first
+  ms::ms_json_dedup_kernel<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(states, B, row_status);
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
-  // about eight CTAs per SM over all rows; every warp of a CTA at least one word
+  // about 32 CTAs per SM over all rows (about 8 per SM when a quarter of the
+  // rows are representatives); every warp of a CTA at least one word
   const int64_t nwords = (V + 31) / 32;
-  int64_t x = (1184 + B - 1) / B;
+  int64_t x = (4736 + B - 1) / B;
   x = x < 1 ? 1 : x;
   const int64_t xmax = (nwords + ms::kJsonThreads / 32 - 1) / (ms::kJsonThreads / 32);
   x = x > xmax ? xmax : x;
   ms::JsonVocab voc{vocab_bytes, vocab_off, V, reinterpret_cast<const uint4 *>(packed), lens};
   ms::ms_json_mask_kernel<<<dim3((unsigned)x, (unsigned)B), ms::kJsonThreads, 0, s>>>(states, voc, mask, mask_ld,
                                                                                        row_status);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  ms::ms_json_mask_copy_kernel<<<(unsigned)B, 256, 0, s>>>(mask, mask_ld, nwords, row_status);
   e = cudaGetLastError();
   return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }

@@ -109,6 +109,30 @@ def test_advance_matches_init(torch):
     np.testing.assert_array_equal(m1.cpu().numpy(), m2.cpu().numpy())
 
 
+def test_rows_in_one_state_share_a_mask(torch):
+    """Rows in the same parse state share one mask computation (a dedup pass);
+    rows whose states differ only in the container stack, or only in deep
+    levels of it, keep their own masks.  Every row equals its single-row
+    build."""
+    from miniserve_b200 import workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    vocab = workloads.json_vocab(4, 12000)
+    base = ['{"a": [1, "x', '{"a": {"b": "x', '[[[[{"k": [', '[[{[{"k": [', '[{[[{"k": [', "[1, 2", "[1, 2",
+            '{"a": [1, "x', "", "tru", '"\\u00', "[" * 40 + "{" + '"k": ', "[" * 39 + "{[" + '"k": ']
+    prefixes = [base[i % len(base)] for i in range(3 * len(base))]
+    b = JsonMaskBuilder(vocab)
+    m, st = b.build(b.init(prefixes))
+    torch.cuda.synchronize()
+    m = m.cpu().numpy()
+    st = st.cpu().numpy()
+    for i, p in enumerate(prefixes[:len(base)]):
+        m1, st1 = b.build(b.init([p]))
+        torch.cuda.synchronize()
+        for j in range(i, len(prefixes), len(base)):
+            np.testing.assert_array_equal(m[j], m1.cpu().numpy()[0], err_msg=repr(p))
+            assert st[j] == st1.cpu().numpy()[0]
+
+
 def test_packed_matches_unpacked(torch):
     """The fixed-width vocabulary path gives the same masks and statuses as the
     variable-length one, tokens longer than 16 bytes included."""
