@@ -107,16 +107,22 @@ int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64
  *      [nranks][B][rec_words] (e.g. ncclAllGather)
  *   3. every rank: ms_shard_merge -> the same tokens on every rank
  *
- * Record of one row (32-bit words, rec_words = 2 + 2*kmax): [0] candidate
+ * Record of one row (32-bit words, rec_words = 4 + 2*kmax): [0] candidate
  * count m <= kmax, [1] MS_ROW_* bits, [2, 2+kmax) order keys of the slice's
  * top-m values (value descending, index ascending), [2+kmax, 2+2*kmax) their
- * global token ids.  Rows the scheme cannot sample exactly (top_k off or
- * above kmax with temperature > 0, top_k >= Vloc, tie blocks beyond the
- * candidate buffer, non-finite logits) come back with MS_ROW_UNSUPPORTED or
- * MS_ROW_NONFINITE and token -1; the caller samples those rows from their
- * full vocabulary (ms_sample on the gathered row).  Greedy rows
- * (temperature 0 or top_k 1) and top-k rows (2 <= top_k <= kmax) are exact.
- * Same reference semantics as ms_sample (miniserve/sampler.py:23-68).
+ * global token ids, [2+2*kmax, 4+2*kmax) a float64 (low word first): for rows
+ * without top-k, the slice's sum of exp((v - m) / T) over its finite logits,
+ * m the slice maximum (0 otherwise).  Greedy rows (temperature 0 or top_k 1)
+ * and top-k rows (2 <= top_k <= kmax) are exact.  Top-p rows without top-k
+ * (kmax >= 2 < Vloc) are exact when the nucleus lies among the candidates:
+ * its crossing value above the kmax-th largest value of every slice whose
+ * record is full.  Rows the scheme cannot sample exactly (top_k above kmax,
+ * top_k >= Vloc, top_p >= 1 without top-k, a nucleus reaching past the
+ * candidates, tie blocks beyond the candidate buffer, non-finite logits)
+ * come back with MS_ROW_UNSUPPORTED or MS_ROW_NONFINITE and token -1; the
+ * caller samples those rows from their full vocabulary (ms_sample on the
+ * gathered row).  Same reference semantics as ms_sample
+ * (miniserve/sampler.py:23-68).
  *
  * kmax: 1..256, the same on every rank.  mask: optional bitmask of the slice
  * ([B, mask_ld] u32, bit i = local token i).
@@ -125,7 +131,7 @@ int ms_shard_candidates(const void *logits, int dtype, int64_t B, int64_t Vloc, 
                         int64_t V, const double *temperature, const int32_t *top_k, const uint32_t *mask,
                         int64_t mask_ld, int32_t kmax, uint32_t *records, ms_stream_t stream);
 
-/* 32-bit words of one row's record for a given kmax (2 + 2*kmax). */
+/* 32-bit words of one row's record for a given kmax (4 + 2*kmax). */
 int64_t ms_shard_record_words(int32_t kmax);
 
 /*

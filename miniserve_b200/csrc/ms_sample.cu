@@ -163,7 +163,7 @@ int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64
                      tokens, probs, row_status, stream, true);
 }
 
-int64_t ms_shard_record_words(int32_t kmax) { return 2 + 2 * (int64_t)kmax; }
+int64_t ms_shard_record_words(int32_t kmax) { return 4 + 2 * (int64_t)kmax; }
 
 int ms_shard_candidates(const void *logits, int dtype, int64_t B, int64_t Vloc, int64_t ld, int64_t v0,
                         int64_t V, const double *temperature, const int32_t *top_k, const uint32_t *mask,

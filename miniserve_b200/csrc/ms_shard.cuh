@@ -1,10 +1,14 @@
 // Merge step of vocab-sharded sampling: one 256-thread CTA per row reads the
-// all-gathered candidate records of every rank ([nranks][B][2 + 2*kmax]
+// all-gathered candidate records of every rank ([nranks][B][4 + 2*kmax]
 // words), ranks the union by (value descending, global id ascending) and
 // finishes the row exactly as miniserve/sampler.py:23-68 does on the full
 // vocabulary: the global top-k set is contained in the union of the slices'
 // top-k sets, and every weight exp(l/T - max/T) is computed in float64 from
-// the exact logit (its order key).
+// the exact logit (its order key).  A top-p row without top-k is finished when
+// its nucleus lies among the candidates: the slices' totals give the row's
+// softmax total, and a crossing value above every full slice's kmax-th
+// largest value has every larger value of the row among the candidates;
+// otherwise the row is flagged MS_ROW_UNSUPPORTED.
 #pragma once
 
 #include "ms_common.cuh"
@@ -33,13 +37,16 @@ struct MergeArgs {
 };
 
 struct MgShared {
-  unsigned long long comp[kMgCap + 2];  // (key, ~id) composites, padded for paired reads
-  uint32_t key[kMgTopK];                // the top-k set in rank order
-  int id[kMgTopK];
-  int kid[kMgTopK];                     // kept ids in index order
-  double kw[kMgTopK];                   // and their weights
+  union {
+    unsigned long long comp[kMgCap + 2];  // (key, ~id) composites, padded for paired reads
+    double kw[kMgCap];                    // after the ranking: kept weights in index order
+  } u;
+  uint32_t key[kMgCap];  // candidates in rank order
+  int id[kMgCap];
+  int kid[kMgCap];       // kept ids in index order
   int off[kMgRanks + 1];
   uint32_t st;
+  float cut;             // the largest kmax-th value of a full slice
   double redd[33];
   int redi[33];
   unsigned long long redq[33];
@@ -51,11 +58,132 @@ __device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok,
   a.status[r] = st;
 }
 
+// A row without top-k (miniserve/sampler.py:35-68 with top_k off): every
+// candidate ranked; float64 weights exp(l/T - max/T); the row's total from the
+// slices' totals; the smallest rank prefix reaching top_p (crossing entry
+// kept), settled only when the crossing value lies above every full slice's
+// kmax-th largest value; the index-order draw over the kept prefix.  The
+// composites of the n candidates are in sh.u.comp.  All threads.
+__device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, size_t rw, double T, double P,
+                           double U) {
+  const int tid = threadIdx.x;
+  if (!(P < 1.0)) {  // the full softmax draw needs every logit
+    if (tid == 0) mg_write(a, row, -1, 0.0f, MS_ROW_UNSUPPORTED);
+    return;
+  }
+  // rank every candidate (all distinct composites)
+  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
+  const int npair = (n + 1) >> 1;
+  for (int i = tid; i < n; i += kMgThreads) {
+    const unsigned long long ci = sh.u.comp[i];
+    int rank = 0;
+    for (int j = 0; j < npair; ++j) {
+      const ulonglong2 q = c2[j];
+      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
+    }
+    sh.key[rank] = (uint32_t)(ci >> 32);
+    sh.id[rank] = (int)~(uint32_t)ci;
+  }
+  __syncthreads();
+  // the row's total: sum over slices of total_r * exp((m_r - max) / T), m_r a
+  // slice's maximum (its first key); the cut: a full slice's last value
+  const float vmax = key_to_float(sh.key[0]);
+  double zr = 0.0;
+  if (tid < a.nranks) {
+    const uint32_t *rec = a.records + ((size_t)tid * a.B + row) * rw;
+    const int mr = (int)min(rec[0], (uint32_t)a.kmax);
+    if (mr > 0) {
+      const unsigned long long b = (unsigned long long)rec[2 + 2 * a.kmax] |
+                                   ((unsigned long long)rec[3 + 2 * a.kmax] << 32);
+      zr = __longlong_as_double((long long)b) * exp(((double)key_to_float(rec[2]) - (double)vmax) / T);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {  // the largest last value among full slices (at most kMgRanks reads)
+    float cut = -INFINITY;
+    for (int r = 0; r < a.nranks; ++r) {
+      const uint32_t *rec = a.records + ((size_t)r * a.B + row) * rw;
+      if ((int)min(rec[0], (uint32_t)a.kmax) == a.kmax) cut = fmaxf(cut, key_to_float(rec[2 + a.kmax - 1]));
+    }
+    sh.cut = cut;
+  }
+  const double Z = block_sum<kMgThreads>(zr, sh.redd);  // ends with a barrier
+  const float cut = sh.cut;
+  // weights in rank order, a contiguous block of ranks per thread
+  const int per = (n + kMgThreads - 1) / kMgThreads;
+  const int p0 = tid * per, p1 = min(n, p0 + per);
+  const double xmax = (double)vmax / T;
+  double sw = 0.0;
+  for (int i = p0; i < p1; ++i) sw += exp((double)key_to_float(sh.key[i]) / T - xmax);
+  double ex, inc, tt;
+  block_scan<kMgThreads, double>(sw, ex, inc, tt, sh.redd);
+  const double need = P * Z;
+  int cand = 0x7FFFFFFF;
+  if (p0 < p1 && inc >= need) {  // sampler.py:54-57: cumsum >= top_p, crossing entry kept
+    double acc = ex;
+    for (int i = p0; i < p1; ++i) {
+      acc += exp((double)key_to_float(sh.key[i]) / T - xmax);
+      if (acc >= need) {
+        cand = i;
+        break;
+      }
+    }
+    if (cand == 0x7FFFFFFF) cand = p1 - 1;
+  }
+  const int j = block_min_i<kMgThreads>(cand, sh.redi);
+  if (j == 0x7FFFFFFF || !(key_to_float(sh.key[j]) > cut)) {  // the nucleus may reach past the candidates
+    if (tid == 0) mg_write(a, row, -1, 0.0f, MS_ROW_UNSUPPORTED);
+    return;
+  }
+  const int nkeep = j + 1;
+  // kept entries in index order (position = kept entries of smaller id)
+  for (int i = tid; i < nkeep; i += kMgThreads) {
+    const int my = sh.id[i];
+    int pos = 0;
+    for (int q = 0; q < nkeep; ++q) pos += sh.id[q] < my ? 1 : 0;
+    sh.kid[pos] = my;
+    sh.u.kw[pos] = exp((double)key_to_float(sh.key[i]) / T - xmax);
+  }
+  __syncthreads();
+  // index-order inverse CDF over the kept entries (sampler.py:58-68)
+  double s2 = 0.0;
+  const int q0 = tid * ((nkeep + kMgThreads - 1) / kMgThreads);
+  const int q1 = min(nkeep, q0 + (nkeep + kMgThreads - 1) / kMgThreads);
+  for (int i = q0; i < q1; ++i) s2 += sh.u.kw[i];
+  double cx, ci2, tot;
+  block_scan<kMgThreads, double>(s2, cx, ci2, tot, sh.redd);
+  if (!(U > 0.0)) {  // r == 0 stops at index 0
+    if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / tot), 0);
+    return;
+  }
+  const double target = U * tot;
+  int who = 0x7FFFFFFF;
+  if (q0 < q1 && ci2 >= target) {
+    double acc = cx;
+    for (int i = q0; i < q1; ++i) {
+      acc += sh.u.kw[i];
+      if (sh.u.kw[i] > 0.0 && acc >= target) {
+        who = i;
+        break;
+      }
+    }
+    if (who == 0x7FFFFFFF) who = q1 - 1;
+  }
+  const int w = block_min_i<kMgThreads>(who, sh.redi);
+  if (tid == 0) {
+    if (w == 0x7FFFFFFF) {  // ran past the end (sampler.py:68)
+      mg_write(a, row, a.V - 1, (float)((sh.kid[nkeep - 1] == a.V - 1 ? sh.u.kw[nkeep - 1] : 0.0) / tot), 0);
+    } else {
+      mg_write(a, row, sh.kid[w], (float)(sh.u.kw[w] / tot), 0);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   __shared__ MgShared sh;
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
-  const size_t rw = (size_t)(2 + 2 * a.kmax);
+  const size_t rw = (size_t)(4 + 2 * a.kmax);
   const double T = a.temperature[row];
   const int k = a.top_k[row];
   const double P = a.top_p[row];
@@ -84,11 +212,11 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
     const uint32_t *rec = a.records + ((size_t)r * a.B + row) * rw;
     const int mr = (int)min(rec[0], (uint32_t)a.kmax);
     for (int i = tid; i < mr; i += kMgThreads)
-      sh.comp[sh.off[r] + i] = ((unsigned long long)rec[2 + i] << 32) | (unsigned long long)(~rec[2 + a.kmax + i]);
+      sh.u.comp[sh.off[r] + i] = ((unsigned long long)rec[2 + i] << 32) | (unsigned long long)(~rec[2 + a.kmax + i]);
   }
   if (tid == 0) {
-    sh.comp[n] = 0ull;
-    sh.comp[n + 1] = 0ull;
+    sh.u.comp[n] = 0ull;
+    sh.u.comp[n + 1] = 0ull;
   }
   __syncthreads();
   if (n == 0) {  // every logit -inf
@@ -100,7 +228,7 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   }
   if (T == 0.0 || k == 1) {  // the first maximum (sampler.py:33-34, or top-k 1)
     unsigned long long best = 0ull;
-    for (int i = tid; i < n; i += kMgThreads) best = max(best, sh.comp[i]);
+    for (int i = tid; i < n; i += kMgThreads) best = max(best, sh.u.comp[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
     if ((tid & 31) == 0) sh.redq[tid >> 5] = best;
@@ -113,12 +241,16 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
     }
     return;
   }
+  if (!(k >= 2 && (int64_t)k < a.V)) {  // no top-k: the nucleus from the candidates
+    mg_nucleus(a, sh, row, n, rw, T, P, U);
+    return;
+  }
   // top-k: rank every candidate; the best min(n, k) are the row's top-k set
   const int m = min(n, k);
-  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.comp);
+  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
   const int npair = (n + 1) >> 1;
   for (int i = tid; i < n; i += kMgThreads) {
-    const unsigned long long ci = sh.comp[i];
+    const unsigned long long ci = sh.u.comp[i];
     int rank = 0;
     for (int j = 0; j < npair; ++j) {
       const ulonglong2 q = c2[j];
@@ -146,22 +278,22 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
     int pos = 0;
     for (int j = 0; j < nkeep; ++j) pos += sh.id[j] < my ? 1 : 0;
     sh.kid[pos] = my;
-    sh.kw[pos] = w;
+    sh.u.kw[pos] = w;
   }
   const double tot = block_sum<kMgThreads>(tid < nkeep ? w : 0.0, sh.redd);  // ends with a barrier
   // index-order inverse CDF (sampler.py:60-68)
   if (!(U > 0.0)) {  // r == 0 stops at index 0
-    if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.kw[0] : 0.0) / tot), 0);
+    if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / tot), 0);
     return;
   }
   const double target = U * tot;
-  const double kwv = tid < nkeep ? sh.kw[tid] : 0.0;
+  const double kwv = tid < nkeep ? sh.u.kw[tid] : 0.0;
   double cex, cinc, ctot;
   block_scan<kMgThreads, double>(kwv, cex, cinc, ctot, sh.redd);
   const int who = block_min_i<kMgThreads>((tid < nkeep && kwv > 0.0 && cinc >= target) ? tid : 0x7FFFFFFF, sh.redi);
   if (tid == 0 && who == 0x7FFFFFFF) {  // ran past the end
     const int last = nkeep - 1;
-    mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.kw[last] : 0.0) / tot), 0);
+    mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.u.kw[last] : 0.0) / tot), 0);
   }
   if (tid == who) mg_write(a, row, sh.kid[tid], (float)(kwv / tot), 0);
 }

@@ -932,18 +932,24 @@ __device__ void st_draw_units(StShared &sh, int &rf, const SampleArgs &a, const 
 enum StMode : int { kStArgmax = 0, kStTopKMode = 1, kStFull = 2, kStNucleus = 3 };
 
 // Candidate record of `row` in vocab-sharded mode: [count, status, kmax keys,
-// kmax global ids].
+// kmax global ids, total (float64, two words)].  The total, for rows without
+// top-k, is the slice's sum of exp((v - m) / T) over its finite logits, m the
+// slice maximum (the first key).
 __device__ __forceinline__ uint32_t *st_record(const SampleArgs &a, int row) {
-  return a.records + (size_t)row * (size_t)(2 + 2 * a.kmax);
+  return a.records + (size_t)row * (size_t)(4 + 2 * a.kmax);
+}
+__device__ __forceinline__ void st_record_total(const SampleArgs &a, uint32_t *rec, double total) {
+  const unsigned long long b = (unsigned long long)__double_as_longlong(total);
+  rec[2 + 2 * a.kmax] = (uint32_t)b;
+  rec[3 + 2 * a.kmax] = (uint32_t)(b >> 32);
 }
 __device__ __forceinline__ void st_record_empty(const SampleArgs &a, int row, uint32_t status) {
   uint32_t *rec = st_record(a, row);
   rec[0] = 0u;
   rec[1] = status;
+  st_record_total(a, rec, 0.0);
 }
 
-// Cost class of row r, longest first: top-p-only 0, top-k 1, full softmax 2,
-// argmax and rows finished without reading the logits 3.
 // Estimated cost class of a row, most expensive first: 0 top-p rows (two
 // passes), 1 top-k rows with k >= 128 (many candidate inserts), 2 the other
 // top-k rows and full-softmax rows, 3 argmax rows.  The first CTAs of a
@@ -1057,7 +1063,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const double T = a.temperature[row];
-  const int k = a.top_k[row];
+  int k = a.top_k[row];
   const double P = a.top_p[row];
   const double U = a.uniforms[row];
   const int V = a.V;
@@ -1088,12 +1094,22 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
   };
   int mode;
+  bool shard_sum = false;  // shard mode, no top-k: the record carries the slice's total
   if (T == 0.0 || k == 1) {
     mode = kStArgmax;
   } else if (shard) {
-    // the slice's top-k stands for the row's only when top_k cuts the whole
-    // vocabulary and fits the record
-    if (!(k >= 2 && (int64_t)k < a.Vg && k <= a.kmax && k < V && k <= kStTopK)) {
+    if (k >= 2 && (int64_t)k < a.Vg) {
+      // the slice's top-k stands for the row's when it fits the record
+      if (!(k <= a.kmax && k < V && k <= kStTopK)) {
+        leave(false);
+        return;
+      }
+    } else if (a.kmax >= 2 && a.kmax < V && a.kmax <= kStTopK && T >= kMinTemperature) {
+      // no top-k: the slice's top kmax and its softmax total, which settle a
+      // top-p row in the merge when the nucleus lies among the candidates
+      k = a.kmax;
+      shard_sum = true;
+    } else {
       leave(false);
       return;
     }
@@ -1205,6 +1221,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     bool over = false;
     bool exact_tau = false;  // tau is the k-th largest value seen (after a compaction)
     int ub = 0;  // bound on the buffer's size (its size after a sync point), the same in every thread
+    // shard_sum: this lane's running maximum and sum of weights relative to it
+    float sm = -INFINITY, ss = 0.0f;
+    StW Ws;
+    const double cls = 1.4426950408889634 / T;  // log2(e) / T
+    if (shard_sum) Ws.set_t(T);
     if (tid == 0) {
       for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_stream);
     }
@@ -1216,6 +1237,23 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       const int g0 = st_get8<DT>(sh, r, c, s, x);
       const float cm = st_max8n(x);
       rmax = st_maxn(rmax, cm);
+      if (shard_sum) {  // online softmax total (block-uniform branch)
+        const float nm = fmaxf(sm, cm);
+        if (nm > sm) {
+          ss = sm > -INFINITY ? ss * (float)exp2(((double)sm - (double)nm) * cls) : 0.0f;
+          sm = nm;
+          Ws.set_m(sm);
+        }
+        if (sm > -INFINITY) {
+          const StW2 W2(Ws);
+          f2_t a2 = W2(f2_pack(x[0], x[1]));
+#pragma unroll
+          for (int j = 1; j < 4; ++j) a2 = f2_add(a2, W2(f2_pack(x[2 * j], x[2 * j + 1])));
+          float a0, a1;
+          f2_unpack(a2, a0, a1);
+          ss += a0 + a1;
+        }
+      }
       if (!exact_tau && ((kRefreshChunks >> c) & 1u)) {
         const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
         if (bmin != 0u && key_to_float(bmin) > tau) set_tau(key_to_float(bmin), false);
@@ -1354,6 +1392,10 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       return;
     }
     if (shard) {  // the slice's top-k, in rank order, with global ids
+      // the slice's total relative to its maximum (rows without top-k)
+      const double tot = shard_sum ? st_bsum(sh, rf, sm > -INFINITY ? (double)ss * exp2(((double)sm - (double)vmax) * cls)
+                                                                     : 0.0)
+                                   : 0.0;
       const int m = st_topk_rank(sh, rf, n, k, thr);
       uint32_t *rec = st_record(a, row);
       for (int i = tid; i < m; i += kStThreads) {
@@ -1363,6 +1405,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       if (tid == 0) {
         rec[0] = (uint32_t)m;
         rec[1] = 0u;
+        st_record_total(a, rec, tot);
       }
       return;
     }

@@ -5,14 +5,16 @@ Step 1 runs ``ms_shard_candidates`` on the rank's slice: per row, the slice's
 top-k values (value descending, index ascending) with their global token ids,
 in a fixed-size record.  Step 2 all-gathers the records of every rank (NCCL
 over NVLink on GPUs; the only data that crosses the interconnect is
-``B * (2 + 2*kmax) * 4`` bytes per rank).  Step 3 runs ``ms_shard_merge`` on
+``B * (4 + 2*kmax) * 4`` bytes per rank).  Step 3 runs ``ms_shard_merge`` on
 every rank, which finishes each row exactly as miniserve's
 ``Sampler.sample`` (miniserve/sampler.py:23-68) does on the whole vocabulary:
 the row's top-k set is contained in the union of the slices' top-k sets.
 
-Rows the record cannot carry exactly (temperature > 0 with top_k off or above
-kmax, a non-finite logit, a tie block larger than the candidate buffer) come
-back flagged; for those rows only, every rank all-gathers the full logits and
+A top-p row without top-k is settled from the records too when its nucleus
+lies among the candidates (the records carry each slice's softmax total);
+rows the records cannot carry exactly (top_k above kmax, top_p >= 1 without
+top-k, a nucleus reaching past the candidates, a non-finite logit, a tie block
+larger than the candidate buffer) come back flagged; for those rows only, every rank all-gathers the full logits and
 samples them with the single-GPU kernel, so every row is exact.  All ranks see
 identical statuses, so they take the same collective steps.
 """
@@ -28,7 +30,7 @@ KMAX_LIMIT = 256
 
 def record_words(kmax: int) -> int:
     """32-bit words in one row's candidate record."""
-    return 2 + 2 * int(kmax)
+    return 4 + 2 * int(kmax)
 
 
 def shard_bounds(V: int, world: int, rank: int) -> Tuple[int, int]:
@@ -36,12 +38,22 @@ def shard_bounds(V: int, world: int, rank: int) -> Tuple[int, int]:
     return (V * rank) // world, (V * (rank + 1)) // world
 
 
-def choose_kmax(top_k: Sequence[int], temperature: Sequence[float]) -> int:
-    """Smallest record width that carries every greedy / top-k row (<= 256)."""
+KMAX_NUCLEUS = 64  # record width for top-p rows without top-k
+
+
+def choose_kmax(top_k: Sequence[int], temperature: Sequence[float],
+                top_p: Optional[Sequence[float]] = None, V: Optional[int] = None) -> int:
+    """Smallest record width that carries every greedy / top-k row (<= 256),
+    and at least KMAX_NUCLEUS when some top-p row has no top-k."""
     need = 1
-    for k, t in zip(top_k, temperature):
-        if t != 0.0 and 2 <= k <= KMAX_LIMIT:
+    ps = top_p if top_p is not None else [1.0] * len(top_k)
+    for k, t, p in zip(top_k, temperature, ps):
+        if t == 0.0 or k == 1:
+            continue
+        if 2 <= k <= KMAX_LIMIT and (V is None or k < V):
             need = max(need, int(k))
+        elif p < 1.0 and (k == 0 or (V is not None and k >= V)):
+            need = max(need, KMAX_NUCLEUS)
     return need
 
 
@@ -109,7 +121,7 @@ class ShardedSampler:
             seeds = [None] * B if seeds is None else list(seeds)
             uniforms = [uniform_for_seed(s) for s in seeds]
         U = _param(uniforms, B, torch.float64, dev)
-        kmax = choose_kmax(K.tolist(), T.tolist())
+        kmax = choose_kmax(K.tolist(), T.tolist(), P.tolist(), self.V)
         W = record_words(kmax)
         L = _lib.lib()
         mask_ptr, mask_ld = None, 0

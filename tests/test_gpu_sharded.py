@@ -31,7 +31,7 @@ def emulate(torch, x, T, K, P, U, world, bf16=False, mask=None):
     from miniserve_b200 import _lib, sharded
     L = _lib.lib()
     B, V = x.shape
-    kmax = sharded.choose_kmax(list(K), list(T))
+    kmax = sharded.choose_kmax(list(K), list(T), list(P), V)
     W = sharded.record_words(kmax)
     xt = torch.from_numpy(np.ascontiguousarray(x)).cuda()
     if bf16:
@@ -105,12 +105,14 @@ def test_bf16_and_mask_emulated(torch):
 
 
 def test_unsupported_rows_flagged_and_finished(torch):
-    """top_k off / above 256: the merge flags them; ShardedSampler finishes
-    them from the full row (world 1 here: the gather is the identity)."""
+    """top_k off with top_p 1, top_k above 256: the merge flags them;
+    ShardedSampler finishes them from the full row (world 1 here: the gather is
+    the identity)."""
     from miniserve_b200.sharded import ShardedSampler
     x, T, K, P, U = _mixed(seed=11, B=16)
     K[:4] = [0, 0, 300, 0]
     T[:4] = [0.9, 1.1, 0.7, 0.5]
+    P[:4] = [1.0, 1.0, 0.9, 1.0]
     tok, prob, st = emulate(torch, x, T, K, P, U, 2)
     assert (st[:4] & 8).all() and (tok[:4] == -1).all()
     s = ShardedSampler(x.shape[1])
@@ -118,6 +120,37 @@ def test_unsupported_rows_flagged_and_finished(torch):
     torch.cuda.synchronize()
     compare(t2.cpu().numpy(), p2.cpu().numpy().astype(np.float64), s2.cpu().numpy(), x, T, K, P, U,
             label="sharded sampler with fallback rows")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nucleus_rows_from_records(torch, world):
+    """Top-p rows without top-k: settled by the merge from the candidates and
+    the slices' totals when the nucleus lies among the candidates (most low-
+    and mid-temperature rows), flagged otherwise; every settled row matches
+    the oracle on the full row, and ShardedSampler finishes the rest."""
+    from miniserve_b200.sharded import ShardedSampler
+    rng = np.random.default_rng(21)
+    B, V = 64, 65536
+    base = -1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))
+    x = np.stack([(base[rng.permutation(V)] + rng.normal(0, 0.5, V)).astype(np.float32) for _ in range(B)])
+    T = rng.choice([0.2, 0.4, 0.7, 1.0, 1.4], B)
+    K = np.zeros(B, np.int32)
+    K[::9] = V + 5  # top_k at or above the vocabulary: off as well
+    P = 0.5 + 0.49 * rng.random(B)
+    U = rng.random(B)
+    U[3] = 0.0
+    tok, prob, st = emulate(torch, x, T, K, P, U, world)
+    settled = st == 0
+    assert settled.sum() >= B // 2, settled.sum()
+    assert np.all(st[~settled] == 8) and np.all(tok[~settled] == -1)
+    r = np.nonzero(settled)[0]
+    compare(tok[r], prob[r], st[r], x[r], T[r], K[r], P[r], U[r], label=f"nucleus from records x{world}")
+    if world == 2:
+        s = ShardedSampler(V)
+        t2, p2, s2 = s.sample(torch.from_numpy(x).cuda(), 0, T, K, P, uniforms=U)
+        torch.cuda.synchronize()
+        compare(t2.cpu().numpy(), p2.cpu().numpy().astype(np.float64), s2.cpu().numpy(), x, T, K, P, U,
+                label="sharded sampler, nucleus rows")
 
 
 def test_nccl_two_ranks(torch):

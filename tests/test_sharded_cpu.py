@@ -25,7 +25,10 @@ def test_shard_bounds_partition():
 def test_choose_kmax():
     assert sharded.choose_kmax([0, 1, 50, 20], [1.0, 1.0, 0.9, 0.0]) == 50
     assert sharded.choose_kmax([0, 300], [1.0, 1.0]) == 1
-    assert sharded.record_words(50) == 102
+    assert sharded.record_words(50) == 104
+    assert sharded.choose_kmax([0, 20], [1.0, 1.0], [0.9, 1.0], 1000) == sharded.KMAX_NUCLEUS
+    assert sharded.choose_kmax([0, 20], [1.0, 1.0], [1.0, 1.0], 1000) == 20
+    assert sharded.choose_kmax([1000, 20], [1.0, 0.0], [0.9, 1.0], 1000) == sharded.KMAX_NUCLEUS
 
 
 def _batch(B=24, V=12288, seed=5):
@@ -86,3 +89,33 @@ def test_gloo_exchange_and_decomposition():
     t_sparse = oracle.c_sample(rows, T, K, P, U)[0]
     t_full = oracle.c_sample(x, T, K, P, U)[0]
     np.testing.assert_array_equal(t_sparse, t_full)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_nucleus_decomposition(world):
+    """Top-p rows without top-k from the records alone (the merge's rule,
+    restated in numpy): whenever the rule settles a row, its token is the
+    oracle's token on the full row; low-temperature rows are settled."""
+    rng = np.random.default_rng(31)
+    B, V, kmax = 40, 12288, 64
+    base = -1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))
+    x = np.stack([(base[rng.permutation(V)] + rng.normal(0, 0.5, V)).astype(np.float32) for _ in range(B)])
+    T = rng.choice([0.2, 0.5, 0.9, 1.4], B)
+    K = np.zeros(B, np.int32)
+    P = 0.5 + 0.49 * rng.random(B)
+    U = rng.random(B)
+    recs = []
+    for r in range(world):
+        v0, v1 = sharded.shard_bounds(V, world, r)
+        recs.append(sharded_ref.np_records(x[:, v0:v1], v0, V, T, K, kmax))
+    allrec = np.stack(recs)
+    o_tok, _, _, mp, mu = oracle.c_sample(x, T, K, P, U)
+    settled = 0
+    for b in range(B):
+        t = sharded_ref.np_nucleus(allrec, b, V, kmax, T[b], P[b], U[b])
+        if t is None:
+            continue
+        settled += 1
+        if mp[b] >= 1e-6 and mu[b] >= 1e-6:
+            assert t == o_tok[b], (b, t, o_tok[b])
+    assert settled >= B // 3
