@@ -23,13 +23,15 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.dirname(HERE))
 
 import cases  # noqa: E402
+import golden_util  # noqa: E402
 from miniserve_b200 import workloads  # noqa: E402
 
 
 def _ref_sampler():
-    ref = os.environ.get("MINISERVE_REF", "/root/reference")
+    ref = golden_util.reference_root()
     sys.path.insert(0, ref)
     from miniserve.sampler import Sampler  # type: ignore
     return Sampler()

@@ -22,7 +22,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.dirname(HERE))
 
+import golden_util  # noqa: E402
 from miniserve_b200 import workloads  # noqa: E402
 
 PROBES = ['"\\u0041', '"\\u0041x', '"\\u004', '"\\uZZZZ', '"\\uZZZZx', '"ab\\', '"\\q', '[1.', '1.', '1.5', '1e',
@@ -39,7 +41,7 @@ MAX_CASE = 1000  # characters; longer config-4 prefixes are checked against the 
 
 
 def _ref():
-    ref = os.environ.get("MINISERVE_REF", "/root/reference")
+    ref = golden_util.reference_root()
     sys.path.insert(0, ref)
     from miniserve.sampler import JSONLogitsProcessor  # type: ignore
     return JSONLogitsProcessor().is_valid_prefix

@@ -25,3 +25,19 @@ def config_batch(entry):
     g = dict(entry["gen"])
     fn = getattr(workloads, g.pop("fn"))
     return fn(**g)
+
+
+def reference_root() -> str:
+    """The reference source tree: $MINISERVE_REF, else BASELINE.json's
+    reference_path (present only where the fixtures are generated)."""
+    import json
+    import os
+    env = os.environ.get("MINISERVE_REF")
+    if env:
+        return env
+    base = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "BASELINE.json")
+    try:
+        with open(base) as f:
+            return json.load(f).get("reference_path", "")
+    except (OSError, ValueError):
+        return ""

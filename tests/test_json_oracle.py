@@ -11,6 +11,7 @@ import sys
 import pytest
 
 from oracle import json_prefix as jp
+import golden_util
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -56,7 +57,7 @@ def test_pack_mask_layout():
 
 
 def test_fuzz_against_live_reference():
-    ref = os.environ.get("MINISERVE_REF", "/root/reference")
+    ref = golden_util.reference_root()
     if not os.path.exists(os.path.join(ref, "miniserve", "sampler.py")):
         pytest.skip("reference tree not present (the golden vectors pin the oracle)")
     sys.path.insert(0, ref)
