@@ -377,10 +377,12 @@ def run_workload(args, rank, world, local_rank):
         prob = torch.empty(B, dtype=torch.float32, device=dev)
         st = torch.empty(B, dtype=torch.int32, device=dev)
 
-        def build():
-            _lib.check(L.ms_build_json_mask(states.data_ptr(), B, builder.vocab_bytes.data_ptr(),
-                                            builder.vocab_off.data_ptr(), V, mask.data_ptr(), W, mst.data_ptr(),
-                                            sptr), "ms_build_json_mask")
+        def build():  # the builder's default path: fixed-width tokens in (length, bytes) order
+            _lib.check(L.ms_build_json_mask_ordered(states.data_ptr(), B, builder.vocab_bytes.data_ptr(),
+                                                    builder.vocab_off.data_ptr(), builder.packed.data_ptr(),
+                                                    builder.lens.data_ptr(), builder.order.data_ptr(), V,
+                                                    mask.data_ptr(), W, mst.data_ptr(), sptr),
+                       "ms_build_json_mask_ordered")
 
         def sample():
             _lib.check(L.ms_sample(x.data_ptr(), 0, B, V, V, T.data_ptr(), K.data_ptr(), P.data_ptr(),

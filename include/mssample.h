@@ -191,6 +191,23 @@ int ms_build_json_mask_packed(const uint32_t *states, int64_t B, const uint8_t *
                               const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens, int64_t V,
                               uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream);
 
+/* The fixed-width copy in a caller-chosen token order: position p holds
+ * token order[p] (order: int32 [V] on the device, a permutation of 0..V-1;
+ * an entry outside it packs an empty token whose bit is never set).  Sorting
+ * the vocabulary by (byte length, bytes) puts tokens that take the same
+ * automaton steps in the same warp.  An addition to the reference interface
+ * (no counterpart in miniserve/sampler.py). */
+int ms_json_pack_vocab_ordered(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V,
+                               const int32_t *order, uint32_t *packed, uint8_t *lens, ms_stream_t stream);
+/* ms_build_json_mask with ms_json_pack_vocab_ordered's tables and the same
+ * order: the same mask (in token order) and row_status.  The first
+ * ceil(V/32) words of each row are rewritten; the rest of the row is left
+ * alone. */
+int ms_build_json_mask_ordered(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                               const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens,
+                               const int32_t *order, int64_t V, uint32_t *mask, int64_t mask_ld,
+                               int32_t *row_status, ms_stream_t stream);
+
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);
 

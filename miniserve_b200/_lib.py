@@ -44,6 +44,8 @@ SIGNATURES = {
     "ms_build_json_mask": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _P]),
     "ms_json_pack_vocab": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P]),
     "ms_build_json_mask_packed": (ctypes.c_int, [_P, _I64, _P, _P, _P, _P, _I64, _P, _I64, _P, _P]),
+    "ms_json_pack_vocab_ordered": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _P]),
+    "ms_build_json_mask_ordered": (ctypes.c_int, [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P]),
     "ms_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ms_last_cuda_error": (ctypes.c_int, []),
     "ms_version": (ctypes.c_int, []),

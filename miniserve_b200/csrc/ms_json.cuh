@@ -49,7 +49,7 @@ enum : uint8_t { NP_MINUS = 0, NP_ZERO, NP_INT, NP_DOT, NP_FRAC, NP_E, NP_ESIGN,
 
 struct JState {
   uint8_t decided, mode, sub, aux;
-  uint8_t key, first, isfloat, pad;
+  uint8_t key, first, isfloat, pad;  // first: 1 once the text has a character
   int32_t depth;
   uint32_t ndig;  // integer digits of the current number (saturates)
 };
@@ -189,7 +189,7 @@ template <class Stack>
 __host__ __device__ void j_step(JState &st, Stack &stk, uint8_t c) {
   if (st.decided) return;
   if (st.first == 0) {  // the raw first character: '{' accepts any text
-    st.first = c ? c : 1;
+    st.first = 1;        // only "has the text begun" matters after it
     if (c == '{') {
       st.decided = J_TRUE;
       return;
@@ -378,24 +378,32 @@ struct JsonVocab {
   // in packed[t], its length in lens[t] (kJsonLongToken when longer)
   const uint4 *packed;
   const uint8_t *lens;
+  // optional order of the fixed-width copy (ms_json_pack_vocab_ordered):
+  // packed[p] holds token order[p]; the mask kernel sets the bit of token
+  // order[p] with an atomic OR into a row the dedup kernel zeroed
+  const int32_t *order;
 };
 
 constexpr uint8_t kJsonLongToken = 255;
 
-// One thread per token: the token's bytes zero-padded to 16 and its length.
-__global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, int64_t V, uint4 *packed,
-                                    uint8_t *lens) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= V) return;
-  const int64_t b = off[t], e = off[t + 1];
+// One thread per position p: token t = order[p] (t = p without an order) --
+// its bytes zero-padded to 16 in packed[p], its length in lens[p].  An order
+// entry outside [0, V) packs an empty token.
+__global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, int64_t V, const int32_t *order,
+                                    uint4 *packed, uint8_t *lens) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= V) return;
+  const int64_t t = order ? (int64_t)order[p] : p;
+  const bool in = t >= 0 && t < V;
+  const int64_t b = in ? off[t] : 0, e = in ? off[t + 1] : 0;
   const int64_t n = e - b;
   uint32_t w[4] = {0u, 0u, 0u, 0u};
   const int m = n < 16 ? (int)n : 16;
 #pragma unroll
   for (int i = 0; i < 16; ++i)
     if (i < m) w[i >> 2] |= (uint32_t)bytes[b + i] << (8 * (i & 3));
-  packed[t] = make_uint4(w[0], w[1], w[2], w[3]);
-  lens[t] = n <= 16 ? (uint8_t)n : kJsonLongToken;
+  packed[p] = make_uint4(w[0], w[1], w[2], w[3]);
+  lens[p] = n <= 16 ? (uint8_t)n : kJsonLongToken;
 }
 
 __device__ __forceinline__ void j_load_state(const uint32_t *g, uint32_t *sbits, JState &st) {
@@ -428,8 +436,9 @@ __global__ void ms_json_feed_kernel(uint32_t *states, int64_t B, const uint8_t *
 }
 
 // grid (X, B): CTA (x, row) builds the mask words of its share of the
-// vocabulary for `row`; lane l of a warp classifies token 32*w + l, a ballot
-// packs the 32 answers into one word.  row_status bits: 1 = some token makes
+// vocabulary for `row`; lane l of a warp classifies token 32*w + l and a
+// ballot packs the 32 answers into one word -- or, with an order, classifies
+// the token at position 32*w + l and ORs its bit into the row.  row_status bits: 1 = some token makes
 // the reference raise (its bit is 0), 2 = some token opens or closes more
 // containers than JStackTok holds (its bit is 0).
 // Rows in the same parse state get the same mask.  Row b's representative is
@@ -439,6 +448,9 @@ __global__ void ms_json_feed_kernel(uint32_t *states, int64_t B, const uint8_t *
 // search (every row its own representative).
 constexpr int kJsonDedupMax = 1024;
 __device__ __forceinline__ bool j_same_state(const uint32_t *x, const uint32_t *y) {
+  // decided: every token gets the same answer, whatever the rest of the state
+  const uint32_t dx = x[0] & 0xFFu;  // JState::decided
+  if (dx != 0u && dx == (y[0] & 0xFFu)) return true;
   for (int i = 0; i < kJsonHeaderWords; ++i)
     if (x[i] != y[i]) return false;
   const int depth = (int)x[2];  // JState::depth
@@ -447,20 +459,32 @@ __device__ __forceinline__ bool j_same_state(const uint32_t *x, const uint32_t *
     if (x[kJsonHeaderWords + i] != y[kJsonHeaderWords + i]) return false;
   return rem == 0 || ((x[kJsonHeaderWords + words] ^ y[kJsonHeaderWords + words]) & ((1u << rem) - 1u)) == 0u;
 }
-__global__ void ms_json_dedup_kernel(const uint32_t *states, int64_t B, int32_t *row_status) {
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
+// One warp per row b: lanes compare b's state with rows c < b, 32 at a time,
+// the first match is b's representative.  With `zero` (ordered vocabulary) a
+// representative's warp also clears its nwords mask words for the mask
+// kernel's atomic ORs.
+__global__ void ms_json_dedup_kernel(const uint32_t *states, int64_t B, int32_t *row_status, uint32_t *zero,
+                                     int64_t mask_ld, int64_t nwords) {
+  const int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;  // warp-uniform
   int64_t rep = b;
   if (B <= kJsonDedupMax) {
     const uint32_t *x = states + b * kJsonStateWords;
-    for (int64_t c = 0; c < b; ++c) {
-      if (j_same_state(x, states + c * kJsonStateWords)) {
-        rep = c;
+    for (int64_t c0 = 0; c0 < b; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const bool same = c < b && j_same_state(x, states + c * kJsonStateWords);
+      const uint32_t hit = __ballot_sync(0xFFFFFFFFu, same);
+      if (hit) {
+        rep = c0 + __ffs(hit) - 1;
         break;
       }
     }
   }
-  row_status[b] = (int32_t)((rep + 1) << 8);
+  if (lane == 0) row_status[b] = (int32_t)((rep + 1) << 8);
+  if (zero && rep == b) {
+    for (int64_t i = lane; i < nwords; i += 32) zero[b * mask_ld + i] = 0u;
+  }
 }
 
 // Rows that share a representative take its mask; every row's status keeps
@@ -472,7 +496,19 @@ __global__ void ms_json_mask_copy_kernel(uint32_t *mask, int64_t mask_ld, int64_
   if (rep != row) {
     const uint32_t *src = mask + rep * mask_ld;
     uint32_t *dst = mask + row * mask_ld;
-    for (int64_t i = threadIdx.x; i < nwords; i += blockDim.x) dst[i] = src[i];
+    for (int64_t i0 = threadIdx.x; i0 < nwords; i0 += 8 * (int64_t)blockDim.x) {  // 8 loads in flight
+      uint32_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t i = i0 + j * (int64_t)blockDim.x;
+        q[j] = i < nwords ? src[i] : 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int64_t i = i0 + j * (int64_t)blockDim.x;
+        if (i < nwords) dst[i] = q[j];
+      }
+    }
   }
   // the representative's low byte (its flags) is final; this kernel only
   // clears high bytes
@@ -493,13 +529,25 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
   if (threadIdx.x == 0) flags = 0;
   __syncthreads();
   const int64_t nwords = (voc.V + 31) >> 5;
+  if (st0.decided) {  // every token gets the row's answer: whole words, token order
+    const uint32_t fill = st0.decided == J_TRUE ? 0xFFFFFFFFu : 0u;
+    for (int64_t w = (int64_t)blockIdx.x * kJsonThreads + threadIdx.x; w < nwords;
+         w += (int64_t)gridDim.x * kJsonThreads) {
+      const int tail = (int)(voc.V - w * 32);  // tokens in word w
+      mask[(int64_t)row * mask_ld + w] = tail >= 32 ? fill : fill & ((1u << tail) - 1u);
+    }
+    if (st0.decided == J_RAISE && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(row_status + row, 1);
+    return;
+  }
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = (int64_t)gridDim.x * (kJsonThreads / 32);
   int my_flags = 0;
   for (int64_t w = (int64_t)blockIdx.x * (kJsonThreads / 32) + (threadIdx.x >> 5); w < nwords; w += warps_total) {
     const int64_t t = w * 32 + lane;
+    // the token at position t (ordered vocabulary), or t itself
+    const int64_t tok = t < voc.V && voc.order ? (int64_t)voc.order[t] : t;
     uint8_t r = J_FALSE;
-    if (t < voc.V) {
+    if (t < voc.V && tok >= 0 && tok < voc.V) {
       JState st = st0;
       JStackTok stk(sbits, st0.depth);
       const int nb = voc.lens ? voc.lens[t] : kJsonLongToken;
@@ -512,14 +560,18 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
           hi >>= 8;
         }
       } else {
-        const int64_t b = voc.off[t], e = voc.off[t + 1];
+        const int64_t b = voc.off[tok], e = voc.off[tok + 1];
         for (int64_t i = b; i < e && !st.decided && !stk.over; ++i) j_step(st, stk, voc.bytes[i]);
       }
       r = stk.over ? (uint8_t)J_UNDECIDED : j_finish(st, stk);
       my_flags |= r == J_RAISE ? 1 : (stk.over ? 2 : 0);
     }
-    const unsigned bits = __ballot_sync(0xFFFFFFFFu, r == J_TRUE);
-    if (lane == 0) mask[(int64_t)row * mask_ld + w] = bits;
+    if (voc.order) {
+      if (r == J_TRUE) atomicOr(mask + (int64_t)row * mask_ld + (tok >> 5), 1u << (tok & 31));
+    } else {
+      const unsigned bits = __ballot_sync(0xFFFFFFFFu, r == J_TRUE);
+      if (lane == 0) mask[(int64_t)row * mask_ld + w] = bits;
+    }
   }
   if (my_flags) atomicOr(&flags, my_flags);
   __syncthreads();

@@ -242,25 +242,28 @@ int ms_json_advance(uint32_t *states, int64_t B, const uint8_t *vocab_bytes, con
 
 namespace {
 int build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
-                    const uint32_t *packed, const uint8_t *lens, int64_t V, uint32_t *mask, int64_t mask_ld,
-                    int32_t *row_status, ms_stream_t stream) {
+                    const uint32_t *packed, const uint8_t *lens, const int32_t *order, int64_t V,
+                    uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
   if (B < 0 || B > 65535 || V < 1 || V > 0x7FFFFFFFll || mask_ld < (V + 31) / 32) return MS_E_INVALID;
   if (B == 0) return MS_OK;
   if (!states || !vocab_bytes || !vocab_off || !mask || !row_status) return MS_E_INVALID;
   if ((packed == nullptr) != (lens == nullptr) || (reinterpret_cast<uintptr_t>(packed) & 15u)) return MS_E_INVALID;
+  if (order && !packed) return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // rows in the same parse state share one mask: representatives first
-  ms::ms_json_dedup_kernel<<<(unsigned)((B + 127) / 128), 128, 0, s>>>(states, B, row_status);
+  // rows in the same parse state share one mask: representatives first (and,
+  // for the ordered vocabulary's atomic ORs, their mask words cleared)
+  const int64_t nwords = (V + 31) / 32;
+  ms::ms_json_dedup_kernel<<<(unsigned)((B + 3) / 4), 128, 0, s>>>(states, B, row_status,
+                                                                   order ? mask : nullptr, mask_ld, nwords);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
-  // about 32 CTAs per SM over all rows (about 8 per SM when a quarter of the
+  // about 64 CTAs per SM over all rows (about 16 per SM when a quarter of the
   // rows are representatives); every warp of a CTA at least one word
-  const int64_t nwords = (V + 31) / 32;
-  int64_t x = (4736 + B - 1) / B;
+  int64_t x = (9472 + B - 1) / B;
   x = x < 1 ? 1 : x;
   const int64_t xmax = (nwords + ms::kJsonThreads / 32 - 1) / (ms::kJsonThreads / 32);
   x = x > xmax ? xmax : x;
-  ms::JsonVocab voc{vocab_bytes, vocab_off, V, reinterpret_cast<const uint4 *>(packed), lens};
+  ms::JsonVocab voc{vocab_bytes, vocab_off, V, reinterpret_cast<const uint4 *>(packed), lens, order};
   ms::ms_json_mask_kernel<<<dim3((unsigned)x, (unsigned)B), ms::kJsonThreads, 0, s>>>(states, voc, mask, mask_ld,
                                                                                        row_status);
   e = cudaGetLastError();
@@ -269,31 +272,53 @@ int build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_byte
   e = cudaGetLastError();
   return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
-}  // namespace
 
-int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
-                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
-  return build_json_mask(states, B, vocab_bytes, vocab_off, nullptr, nullptr, V, mask, mask_ld, row_status, stream);
-}
-
-int ms_json_pack_vocab(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V, uint32_t *packed,
-                       uint8_t *lens, ms_stream_t stream) {
+int pack_vocab(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V, const int32_t *order,
+               uint32_t *packed, uint8_t *lens, ms_stream_t stream) {
   if (V < 1 || V > 0x7FFFFFFFll) return MS_E_INVALID;
   if (!vocab_bytes || !vocab_off || !packed || !lens || (reinterpret_cast<uintptr_t>(packed) & 15u)) {
     return MS_E_INVALID;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ms::ms_json_pack_kernel<<<(unsigned)((V + 255) / 256), 256, 0, s>>>(vocab_bytes, vocab_off, V,
+  ms::ms_json_pack_kernel<<<(unsigned)((V + 255) / 256), 256, 0, s>>>(vocab_bytes, vocab_off, V, order,
                                                                      reinterpret_cast<uint4 *>(packed), lens);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+}  // namespace
+
+int ms_build_json_mask(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes, const int64_t *vocab_off,
+                       int64_t V, uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
+  return build_json_mask(states, B, vocab_bytes, vocab_off, nullptr, nullptr, nullptr, V, mask, mask_ld,
+                         row_status, stream);
+}
+
+int ms_json_pack_vocab(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V, uint32_t *packed,
+                       uint8_t *lens, ms_stream_t stream) {
+  return pack_vocab(vocab_bytes, vocab_off, V, nullptr, packed, lens, stream);
 }
 
 int ms_build_json_mask_packed(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
                               const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens, int64_t V,
                               uint32_t *mask, int64_t mask_ld, int32_t *row_status, ms_stream_t stream) {
   if (!packed || !lens) return MS_E_INVALID;
-  return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, V, mask, mask_ld, row_status, stream);
+  return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, nullptr, V, mask, mask_ld, row_status,
+                         stream);
+}
+
+int ms_json_pack_vocab_ordered(const uint8_t *vocab_bytes, const int64_t *vocab_off, int64_t V,
+                               const int32_t *order, uint32_t *packed, uint8_t *lens, ms_stream_t stream) {
+  if (!order) return MS_E_INVALID;
+  return pack_vocab(vocab_bytes, vocab_off, V, order, packed, lens, stream);
+}
+
+int ms_build_json_mask_ordered(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                               const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens,
+                               const int32_t *order, int64_t V, uint32_t *mask, int64_t mask_ld,
+                               int32_t *row_status, ms_stream_t stream) {
+  if (!packed || !lens || !order) return MS_E_INVALID;
+  return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, order, V, mask, mask_ld, row_status,
+                         stream);
 }
 
 }  // extern "C"

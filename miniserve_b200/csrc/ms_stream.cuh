@@ -70,6 +70,7 @@ constexpr double kMinTemperature = 1e-30;       // fp32 weights need a finite lo
 
 struct StShared {
   alignas(128) unsigned char stage[kStages][kChunk * 4];
+  alignas(16) uint32_t mstage[kStages][kChunk / 32];  // the chunk's allowed-token bits (StRow::mtma)
   union {
     struct {
       uint32_t key[kCandCap];
@@ -126,6 +127,7 @@ struct StRow {
   int V;
   int esz;
   bool tma;             // 16-byte aligned row: chunks arrive by TMA
+  bool mtma;            // 16-byte aligned mask row too: whole chunks' mask words arrive with them
   int nchunks;
   int nfull;            // leading chunks delivered whole by TMA
   int cb, ce;           // the chunks this CTA streams: [cb, ce)
@@ -201,18 +203,26 @@ __device__ __forceinline__ int tma_elems(const StRow &r, int c) {
   return ne & -(16 / st_esz<DT>());
 }
 
-// thread 0: start the copy of chunk c into stage s
+// thread 0: start the copy of chunk c into stage s (and, for a whole chunk of
+// a row with an aligned mask row, of its kChunk / 32 mask words)
 template <int DT>
 __device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, int s, uint64_t pol) {
   const uint32_t bytes = (uint32_t)(tma_elems<DT>(r, c) * st_esz<DT>());
+  const uint32_t mbytes = r.mtma && c < r.nfull ? (uint32_t)(kChunk / 8) : 0u;
   const uint32_t mb = st_smem(&sh.full[s]);
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(bytes) : "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(bytes + mbytes) : "memory");
   if (bytes) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
             st_smem(sh.stage[s])),
         "l"(r.g + (int64_t)c * kChunk * st_esz<DT>()), "r"(bytes), "r"(mb), "l"(pol)
         : "memory");
+  }
+  if (mbytes) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     st_smem(sh.mstage[s])),
+                 "l"(r.mask + (int64_t)c * (kChunk / 32)), "r"(mbytes), "r"(mb)
+                 : "memory");
   }
 }
 
@@ -321,8 +331,16 @@ __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c
       x[7] = __uint_as_float(h1.y & 0xFFFF0000u);
     }
     if (r.mask) {  // each group of 4 lies in one 32-bit mask word
-      const int g0 = c * kChunk + j, g1 = g0 + 128;
-      const uint32_t m0 = __ldg(r.mask + (g0 >> 5)) >> (g0 & 31), m1 = __ldg(r.mask + (g1 >> 5)) >> (g1 & 31);
+      uint32_t m0, m1;
+      if (r.mtma) {  // the chunk's words arrived with it (kChunk is a multiple of 32)
+        const uint32_t *mw = sh.mstage[s] + (j >> 5);
+        m0 = mw[0] >> (j & 31);
+        m1 = mw[4] >> (j & 31);
+      } else {
+        const int g0 = c * kChunk + j, g1 = g0 + 128;
+        m0 = __ldg(r.mask + (g0 >> 5)) >> (g0 & 31);
+        m1 = __ldg(r.mask + (g1 >> 5)) >> (g1 & 31);
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (!((m0 >> e) & 1u)) x[e] = -INFINITY;
@@ -1131,6 +1149,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   r.mask = a.mask ? a.mask + (int64_t)row * a.mask_ld : nullptr;
   r.V = V;
   r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
+  r.mtma = r.mask && r.tma && (reinterpret_cast<uintptr_t>(r.mask) & 15u) == 0;
   r.nchunks = (V + kChunk - 1) / kChunk;
   r.cb = joint && crank == 1 ? r.nchunks / 2 : 0;
   r.ce = joint && crank == 0 ? r.nchunks / 2 : r.nchunks;

@@ -10,7 +10,7 @@ vocabulary against it and returns the [B, ceil(V/32)] bitmask that
 """
 from __future__ import annotations
 
-from typing import Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 from . import _lib
 from .sampler import _torch
@@ -30,11 +30,25 @@ def _pack_texts(texts: Sequence[str], device):
     return by, torch.tensor(off, dtype=torch.int64, device=device)
 
 
-class JsonMaskBuilder:
-    """Masks over a fixed vocabulary (a list of token strings)."""
+def length_order(vocab: Sequence[str]) -> List[int]:
+    """Token ids sorted by (UTF-8 length, bytes): a warp of the mask kernel
+    then holds tokens of one length that share their first bytes, so its lanes
+    take the same automaton steps and finish together."""
+    enc = [t.encode("utf-8") for t in vocab]
+    return sorted(range(len(enc)), key=lambda t: (len(enc[t]), enc[t]))
 
-    def __init__(self, vocab: Sequence[str], device="cuda") -> None:
+
+class JsonMaskBuilder:
+    """Masks over a fixed vocabulary (a list of token strings).
+
+    ``order``: "length" (default) evaluates the tokens in ``length_order``
+    (``ms_build_json_mask_ordered``); None keeps token order
+    (``ms_build_json_mask_packed``).  The masks are the same either way."""
+
+    def __init__(self, vocab: Sequence[str], device="cuda", order: Optional[str] = "length") -> None:
         torch = _torch()
+        if order not in (None, "length"):
+            raise ValueError(f"order must be 'length' or None, not {order!r}")
         self.device = torch.device(device)
         self.V = len(vocab)
         self.vocab_bytes, self.vocab_off = _pack_texts(vocab, self.device)
@@ -42,9 +56,17 @@ class JsonMaskBuilder:
         # fixed-width copy of the vocabulary (16 bytes a token) for the mask
         self.packed = torch.empty((self.V, 4), dtype=torch.int32, device=self.device)
         self.lens = torch.empty(self.V, dtype=torch.uint8, device=self.device)
-        rc = _lib.lib().ms_json_pack_vocab(self.vocab_bytes.data_ptr(), self.vocab_off.data_ptr(), self.V,
-                                           self.packed.data_ptr(), self.lens.data_ptr(), self._stream())
-        _lib.check(rc, "ms_json_pack_vocab")
+        self.order = None
+        if order == "length" and self.V > 0:
+            self.order = torch.tensor(length_order(vocab), dtype=torch.int32, device=self.device)
+            rc = _lib.lib().ms_json_pack_vocab_ordered(self.vocab_bytes.data_ptr(), self.vocab_off.data_ptr(),
+                                                       self.V, self.order.data_ptr(), self.packed.data_ptr(),
+                                                       self.lens.data_ptr(), self._stream())
+            _lib.check(rc, "ms_json_pack_vocab_ordered")
+        else:
+            rc = _lib.lib().ms_json_pack_vocab(self.vocab_bytes.data_ptr(), self.vocab_off.data_ptr(), self.V,
+                                               self.packed.data_ptr(), self.lens.data_ptr(), self._stream())
+            _lib.check(rc, "ms_json_pack_vocab")
 
     def _stream(self):
         return _torch().cuda.current_stream(self.device).cuda_stream
@@ -67,16 +89,25 @@ class JsonMaskBuilder:
                                         self.vocab_off.data_ptr(), self.V, t.data_ptr(), self._stream())
         _lib.check(rc, "ms_json_advance")
 
-    def build(self, states, out=None, packed: bool = True) -> Tuple["object", "object"]:
+    def build(self, states, out=None, packed: bool = True, status=None) -> Tuple["object", "object"]:
         """(mask [B, ceil(V/32)] int32, row_status [B] int32).  packed=False
         reads every token from the variable-length vocabulary instead of the
-        fixed-width copy (same result)."""
+        fixed-width copy (same result).  ``out`` / ``status``: buffers to
+        write into."""
         torch = _torch()
         B = states.shape[0]
         W = (self.V + 31) // 32
         mask = torch.empty((B, W), dtype=torch.int32, device=self.device) if out is None else out
-        status = torch.empty(B, dtype=torch.int32, device=self.device)
-        if packed:
+        if status is None:
+            status = torch.empty(B, dtype=torch.int32, device=self.device)
+        if packed and self.order is not None:
+            rc = _lib.lib().ms_build_json_mask_ordered(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
+                                                       self.vocab_off.data_ptr(), self.packed.data_ptr(),
+                                                       self.lens.data_ptr(), self.order.data_ptr(), self.V,
+                                                       mask.data_ptr(),
+                                                       mask.stride(0), status.data_ptr(), self._stream())
+            _lib.check(rc, "ms_build_json_mask_ordered")
+        elif packed:
             rc = _lib.lib().ms_build_json_mask_packed(states.data_ptr(), B, self.vocab_bytes.data_ptr(),
                                                       self.vocab_off.data_ptr(), self.packed.data_ptr(),
                                                       self.lens.data_ptr(), self.V, mask.data_ptr(), mask.stride(0),

@@ -169,3 +169,53 @@ def test_config4_masked_sampling(torch):
     compare(tok.cpu().numpy(), prob.cpu().numpy().astype(np.float64), status.cpu().numpy(), cfg.logits,
             cfg.temperature, cfg.top_k, cfg.top_p, cfg.uniforms, mask=mask.cpu().numpy().view(np.uint32),
             label="config4 masked")
+
+
+def test_ordered_matches_token_order(torch):
+    """The length-ordered vocabulary path gives the same masks and statuses as
+    token order: long tokens, a vocabulary that is not a multiple of 32, rows
+    that share a state, and an arbitrary permutation through the C ABI."""
+    from miniserve_b200 import _lib, workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    vocab = workloads.json_vocab(4, 20011)
+    rng = random.Random(7)
+    for i in range(0, len(vocab), 89):  # some long tokens (17-40 bytes)
+        vocab[i] = "".join(rng.choice('{}[]:," 0123456789.eE-truefalsn\\') for _ in range(rng.randint(17, 40)))
+    prefixes = workloads.json_prefixes(4, 64)
+    prefixes = prefixes + prefixes[:20] + ["[1, 2", "[1, 2", '{"a": "x', ""]
+    ordered = JsonMaskBuilder(vocab)
+    plain = JsonMaskBuilder(vocab, order=None)
+    assert ordered.order is not None and plain.order is None
+    s = ordered.init(prefixes)
+    m1, st1 = ordered.build(s)
+    m2, st2 = plain.build(s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(m1.cpu().numpy(), m2.cpu().numpy())
+    np.testing.assert_array_equal(st1.cpu().numpy(), st2.cpu().numpy())
+    assert sorted(ordered.order.cpu().tolist()) == list(range(len(vocab)))
+    # any permutation gives the same masks; a padded row stride too
+    V = len(vocab)
+    perm = torch.from_numpy(np.random.default_rng(3).permutation(V).astype(np.int32)).cuda()
+    packed = torch.empty((V, 4), dtype=torch.int32, device="cuda")
+    lens = torch.empty(V, dtype=torch.uint8, device="cuda")
+    L = _lib.lib()
+    sp = torch.cuda.current_stream().cuda_stream
+    _lib.check(L.ms_json_pack_vocab_ordered(ordered.vocab_bytes.data_ptr(), ordered.vocab_off.data_ptr(), V,
+                                            perm.data_ptr(), packed.data_ptr(), lens.data_ptr(), sp),
+               "ms_json_pack_vocab_ordered")
+    B = len(prefixes)
+    W = (V + 31) // 32
+    m3 = torch.full((B, W + 5), -1, dtype=torch.int32, device="cuda")
+    st3 = torch.empty(B, dtype=torch.int32, device="cuda")
+    _lib.check(L.ms_build_json_mask_ordered(s.data_ptr(), B, ordered.vocab_bytes.data_ptr(),
+                                            ordered.vocab_off.data_ptr(), packed.data_ptr(), lens.data_ptr(),
+                                            perm.data_ptr(), V, m3.data_ptr(), W + 5,
+                                            st3.data_ptr(), sp), "ms_build_json_mask_ordered")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(m3[:, :W].cpu().numpy(), m2.cpu().numpy())
+    assert (m3[:, W:].cpu().numpy() == -1).all()  # the padding is untouched
+    np.testing.assert_array_equal(st3.cpu().numpy(), st2.cpu().numpy())
+    # the ordered path refuses a missing order
+    assert L.ms_build_json_mask_ordered(s.data_ptr(), B, ordered.vocab_bytes.data_ptr(),
+                                        ordered.vocab_off.data_ptr(), packed.data_ptr(), lens.data_ptr(),
+                                        None, V, m3.data_ptr(), W + 5, st3.data_ptr(), sp) != 0
