@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
                                                                     uint32_t *mask, int64_t mask_ld,
                                                                     int32_t *row_status) {
   __shared__ uint32_t sbits[kJsonStackWords];
+  __shared__ uint8_t first_dec[256];  // the row's decision after byte c alone (0: none yet)
   __shared__ int flags;
   const int row = blockIdx.y;
   // a row in the same state as an earlier row: ms_json_mask_copy_kernel fills it
@@ -539,20 +540,35 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     if (st0.decided == J_RAISE && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(row_status + row, 1);
     return;
   }
+  // a token whose first byte already decides takes that answer: once decided
+  // the automaton ignores the rest of the text (j_step, j_finish)
+  static_assert(kJsonThreads == 256, "one thread per first byte");
+  {
+    JState st = st0;
+    JStackTok stk(sbits, st0.depth);
+    j_step(st, stk, (uint8_t)threadIdx.x);
+    first_dec[threadIdx.x] = st.decided;  // one byte never leaves the register window
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = (int64_t)gridDim.x * (kJsonThreads / 32);
   int my_flags = 0;
   for (int64_t w = (int64_t)blockIdx.x * (kJsonThreads / 32) + (threadIdx.x >> 5); w < nwords; w += warps_total) {
     const int64_t t = w * 32 + lane;
-    // the token at position t (ordered vocabulary), or t itself
-    const int64_t tok = t < voc.V && voc.order ? (int64_t)voc.order[t] : t;
+    // the token at position t (ordered vocabulary), or t itself; < 0: none
+    int64_t tok = t < voc.V ? (voc.order ? (int64_t)voc.order[t] : t) : -1;
+    if (tok >= voc.V) tok = -1;
+    const int nb = tok >= 0 && voc.lens ? voc.lens[t] : kJsonLongToken;
+    const uint4 q = tok >= 0 && voc.lens ? voc.packed[t] : make_uint4(0u, 0u, 0u, 0u);
     uint8_t r = J_FALSE;
-    if (t < voc.V && tok >= 0 && tok < voc.V) {
+    const uint8_t d = tok >= 0 && voc.lens && nb >= 1 ? first_dec[q.x & 0xFFu] : (uint8_t)J_UNDECIDED;
+    if (d != J_UNDECIDED) {
+      r = d;
+      my_flags |= d == J_RAISE ? 1 : 0;
+    } else if (tok >= 0) {
       JState st = st0;
       JStackTok stk(sbits, st0.depth);
-      const int nb = voc.lens ? voc.lens[t] : kJsonLongToken;
       if (nb != kJsonLongToken) {  // the bytes from registers, low byte first
-        const uint4 q = voc.packed[t];
         uint64_t lo = (uint64_t)q.x | ((uint64_t)q.y << 32), hi = (uint64_t)q.z | ((uint64_t)q.w << 32);
         for (int i = 0; i < nb && !st.decided && !stk.over; ++i) {
           j_step(st, stk, (uint8_t)lo);

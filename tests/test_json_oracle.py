@@ -75,3 +75,18 @@ def test_fuzz_against_live_reference():
         except (RecursionError, ValueError):
             want = jp.RAISE
         assert jp.is_valid_prefix(s) == want, repr(s)
+
+
+def test_length_order():
+    """The mask builder's evaluation order: token ids sorted by (UTF-8 byte
+    length, bytes), a permutation of the vocabulary; unknown orders are
+    refused before anything touches a device."""
+    from miniserve_b200.grammar import JsonMaskBuilder, length_order
+    vocab = ["bb", "a", "ab", "", "é", "{", "aa"]
+    order = length_order(vocab)
+    assert sorted(order) == list(range(len(vocab)))
+    keys = [(len(vocab[t].encode()), vocab[t].encode()) for t in order]
+    assert keys == sorted(keys)
+    assert order[0] == 3  # the empty token first
+    with pytest.raises(ValueError):
+        JsonMaskBuilder(vocab, device="cpu", order="alphabetical")
