@@ -41,3 +41,17 @@ def reference_root() -> str:
             return json.load(f).get("reference_path", "")
     except (OSError, ValueError):
         return ""
+
+
+def load_mask_fuzz():
+    """The 10^6-pair JSON mask fixture (tests/golden/make_mask_fuzz_golden.py):
+    (prefixes, tokens [S, N] vocabulary ids of json_vocab(4), allowed [S, N]
+    bool, raises [(state, column)])."""
+    import random
+    d = np.load(os.path.join(os.path.dirname(GOLDEN), "json_mask_fuzz.npz"))
+    n_states, n_tokens, _, seed, V = (int(v) for v in d["meta"])
+    prefixes = [str(p) for p in d["prefixes"]]
+    assert len(prefixes) == n_states
+    tokens = np.array([random.Random(seed + i).sample(range(V), n_tokens) for i in range(n_states)], np.int64)
+    allowed = np.unpackbits(d["true_bits"], axis=1)[:, :n_tokens].astype(bool)
+    return prefixes, tokens, allowed, [tuple(r) for r in d["raises"].tolist()]

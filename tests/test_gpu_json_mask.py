@@ -91,6 +91,33 @@ def test_config4_masks_vs_oracle(torch):
     assert checked > 10 * V
 
 
+def test_masks_match_reference_fuzz_fixture(torch):
+    """Miniserve's own answers for 10^6 (state, token) pairs
+    (tests/golden/json_mask_fuzz.npz: 40 parse states over the 151936-token
+    config-4 vocabulary): the GPU mask bit of every pair, in the default
+    (length-ordered) and token-ordered builds."""
+    import golden_util
+    from miniserve_b200 import workloads
+    from miniserve_b200.grammar import JsonMaskBuilder
+    prefixes, tokens, allowed, raises = golden_util.load_mask_fuzz()
+    vocab = workloads.json_vocab(4)
+    for order in ("length", None):
+        b = JsonMaskBuilder(vocab, order=order)
+        mask, st = b.build(b.init(prefixes))
+        torch.cuda.synchronize()
+        m = mask.cpu().numpy().view(np.uint32)
+        got = ((m[np.arange(len(prefixes))[:, None], tokens >> 5] >> (tokens & 31).astype(np.uint32)) & 1).astype(bool)
+        want = allowed.copy()
+        for i, j in raises:  # a raise: bit 0 and row status 1
+            want[i, j] = False
+            assert st.cpu().numpy()[i] & 1
+        if not raises:
+            assert not st.cpu().numpy().any()
+        bad = np.argwhere(got != want)
+        assert len(bad) == 0, [(prefixes[i][-30:], vocab[tokens[i, j]], bool(want[i, j])) for i, j in bad[:10]]
+    assert tokens.size == 1_000_000
+
+
 def test_advance_matches_init(torch):
     """State after prefix + sampled token == state built from the joined text."""
     from miniserve_b200 import workloads

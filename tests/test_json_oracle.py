@@ -90,3 +90,21 @@ def test_length_order():
     assert order[0] == 3  # the empty token first
     with pytest.raises(ValueError):
         JsonMaskBuilder(vocab, device="cpu", order="alphabetical")
+
+
+def test_oracle_matches_mask_fuzz_fixture():
+    """oracle/json_prefix.py against miniserve's answers for 10^6 (state,
+    token) pairs (tests/golden/json_mask_fuzz.npz)."""
+    from miniserve_b200 import workloads
+    prefixes, tokens, allowed, raises = golden_util.load_mask_fuzz()
+    vocab = workloads.json_vocab(4)
+    raised = set(raises)
+    bad = []
+    for i, p in enumerate(prefixes):
+        for j, t in enumerate(tokens[i].tolist()):
+            got = jp.is_valid_prefix(p + vocab[t])
+            want = jp.RAISE if (i, j) in raised else bool(allowed[i, j])
+            if got != want:
+                bad.append((i, vocab[t], want))
+    assert tokens.size == 1_000_000
+    assert not bad, bad[:10]
