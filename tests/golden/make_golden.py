@@ -79,7 +79,7 @@ def main():
     cfg("config2_fp32", workloads.config2(2), range(16), {"fn": "config2", "seed": 2})
     cfg("config2_bf16", workloads.config2(2, bf16=True), range(16),
         {"fn": "config2", "seed": 2, "bf16": True})
-    cfg("config3", workloads.config3(3), range(40), {"fn": "config3", "seed": 3})
+    cfg("config3", workloads.config3(3), range(512), {"fn": "config3", "seed": 3})  # the whole north-star batch
     cfg("config5", workloads.config5(5, B=4), range(4), {"fn": "config5", "seed": 5, "B": 4})
 
     with open(os.path.join(HERE, "sampler_golden.json"), "w") as f:
