@@ -455,6 +455,42 @@ __device__ __forceinline__ int st_bmin(StShared &sh, int &rf, int v) {
   __syncthreads();
   return __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? p[lane] : 0x7FFFFFFF);
 }
+// the minima of a and of b
+__device__ __forceinline__ void st_bmin2(StShared &sh, int &rf, int a, int b, int &ma, int &mb) {
+  static_assert(kStWarps <= 16, "two partials per warp in one half");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = __reduce_min_sync(0xFFFFFFFFu, a);
+  b = __reduce_min_sync(0xFFFFFFFFu, b);
+  int *p = sh.r1i[rf];
+  rf ^= 1;
+  if (lane == 0) {
+    p[warp] = a;
+    p[16 + warp] = b;
+  }
+  __syncthreads();
+  ma = __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? p[lane] : 0x7FFFFFFF);
+  mb = __reduce_min_sync(0xFFFFFFFFu, lane < kStWarps ? p[16 + lane] : 0x7FFFFFFF);
+}
+// the maximum (fmaxf: a NaN drops out) and, in *any, whether some thread's
+// flag is set
+__device__ __forceinline__ float st_bmaxf(StShared &sh, int &rf, float v, bool flag, bool *any) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  const bool wf = __any_sync(0xFFFFFFFFu, flag);
+  double *p = sh.r1d[rf];
+  rf ^= 1;
+  if (lane == 0) {
+    p[warp] = (double)v;
+    p[32 + warp] = wf ? 1.0 : 0.0;
+  }
+  __syncthreads();
+  float t = lane < kStWarps ? (float)p[lane] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t = fmaxf(t, __shfl_xor_sync(0xFFFFFFFFu, t, o));
+  if (any) *any = __any_sync(0xFFFFFFFFu, lane < kStWarps && p[32 + lane] != 0.0);
+  return t;
+}
 // exclusive and inclusive prefix sums over threads in thread order, and the total
 __device__ __forceinline__ void st_bscan(StShared &sh, int &rf, double v, double &ex, double &inc, double &tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1446,11 +1482,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   };
   // after pass 1: the row maximum, or a status written and false
   auto finish_max = [&](float vmax_t, float &vmax) -> bool {
-    if (__syncthreads_or(st_bad(vmax_t) || !ok)) {
+    bool anybad;
+    vmax = st_bmaxf(sh, rf, vmax_t, st_bad(vmax_t) || !ok, &anybad);
+    if (anybad) {
       if (tid == 0) a.status[row] = kRowPending;
       return false;
     }
-    vmax = block_max_f<kStThreads>(vmax_t, sh.redf);
     if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
       if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
       return false;
@@ -1500,7 +1537,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       kd[u] = (double)sh.w.n.s[u] * (double)fu;
       zs += kd[u];
     }
-    const double total = block_sum<kStThreads>(zs, sh.redd);  // ends with a barrier
+    const double total = st_bsum(sh, rf, zs);  // its barrier follows every kd write
     st_draw_units<DT>(sh, rf, a, r, row, nu, kd, total, U,
                       [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
     return;
@@ -1591,7 +1628,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
     if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
     if (c == r.cb) {
-      float g = block_max_f<kStThreads>(cm, sh.redf);
+      float g = st_bmaxf(sh, rf, cm, false, nullptr);
       if (joint) {  // one anchor for both halves: the larger first-chunk maximum
         if (tid == 0) st_peer_f32(st_peer(&sh.xch.j1_g), g);
         st_cluster_sync();
@@ -1613,8 +1650,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (!finish_max(vmax_t, vmax)) return;
   } else {
     // both halves: NaN / +inf, failed copies, the maximum, the high lists
-    const bool badc = __syncthreads_or(st_bad(vmax_t)) != 0;
-    const float vm = block_max_f<kStThreads>(vmax_t, sh.redf);
+    bool badc;
+    const float vm = st_bmaxf(sh, rf, vmax_t, st_bad(vmax_t), &badc);
     if (tid == 0) {
       st_peer_u32(st_peer(&sh.xch.j2_flags), (badc ? 1u : 0u) | (ok ? 0u : 2u));
       st_peer_f32(st_peer(&sh.xch.j2_vmax), vm);
@@ -1661,7 +1698,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const int nh = min(sh.nhigh, kHighCap);
   double hs = 0.0;
   for (int i = tid; i < nh; i += kStThreads) hs += unit_w(key_to_float(sh.w.n.hkey[i]), sh.w.n.hidx[i]);
-  double H = block_sum<kStThreads>(hs, sh.redd);
+  double H = st_bsum(sh, rf, hs);
   if (joint) {
     // one histogram and one high-list mass for both halves: each CTA copies
     // its histogram into the partner's idle stages and adds the partner's copy
@@ -1698,7 +1735,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       s += mb[q];
     }
     double ex, inc, tot;
-    block_scan<kStThreads, double>(s, ex, inc, tot, sh.redd);
+    st_bscan(sh, rf, s, ex, inc, tot);
     const double zh = H + tot;
     const double lo_t = P * zh - kHistTol * zh, hi_t = P * zh + kHistTol * zh;
     int clo = 0x7FFFFFFF, chi = 0x7FFFFFFF;
@@ -1709,8 +1746,10 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       if (clo == 0x7FFFFFFF && acc >= lo_t) clo = tid * kPer + q;
       if (chi == 0x7FFFFFFF && acc >= hi_t) chi = tid * kPer + q;
     }
-    i_lo = H >= lo_t ? -1 : block_min_i<kStThreads>(clo, sh.redi);
-    i_hi = H >= hi_t ? -1 : block_min_i<kStThreads>(chi, sh.redi);
+    int mlo, mhi;
+    st_bmin2(sh, rf, clo, chi, mlo, mhi);
+    i_lo = H >= lo_t ? -1 : mlo;
+    i_hi = H >= hi_t ? -1 : mhi;
     if (i_lo == 0x7FFFFFFF || i_lo > kSBins) i_lo = kSBins + 1;
     if (i_hi == 0x7FFFFFFF || i_hi > kSBins) i_hi = kSBins + 1;
   }
