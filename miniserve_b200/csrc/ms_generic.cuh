@@ -48,12 +48,10 @@ struct SampleArgs {
   int kmax = 0;
   int64_t v0 = 0;
   int64_t Vg = 0;
-  // pair mode: the streaming kernel runs as clusters of two CTAs;
-  // top-p rows are shared by the two CTAs of a cluster when the batch leaves
-  // room: B + (top-p rows) <= slots (CTAs the GPU holds at once)
+  // pair mode: the streaming kernel runs as 2 * rows CTAs in clusters of two;
+  // a top-p row takes both CTAs of a cluster, the other rows one CTA each
   int pairs = 0;
-  int slots = 0;
-  int rows = 0;  // B (pair mode)
+  int rows = 0;
 };
 
 template <int DT>

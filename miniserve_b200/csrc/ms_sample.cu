@@ -47,12 +47,9 @@ cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int de
     ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
     return cudaGetLastError();
   }
-  // pair mode: clusters of two CTAs.  Work items (a shared top-p row or two
-  // rows) number at most (B + top-p rows) / 2 + 1 <= slots / 2 + 1 when rows
-  // are shared, and one row per CTA needs B <= slots CTAs otherwise
-  const int clusters = B < a.slots / 2 + 1 ? B : a.slots / 2 + 1;
+  // pair mode: B clusters of two CTAs, enough for every row to be a top-p row
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.gridDim = dim3((unsigned)(2 * B));
   cfg.blockDim = dim3(ms::kStThreads);
   cfg.dynamicSmemBytes = sizeof(ms::StShared);
   cfg.stream = s;
@@ -78,11 +75,8 @@ cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, 
   }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // a batch of at most one row per SM runs in pair mode, where top-p rows take
-  // two CTAs each (larger batches keep the GPU's CTA slots busy without it)
   ms::SampleArgs ap = a;
-  ap.slots = 2 * sms;
-  ap.pairs = B <= sms ? 1 : 0;
+  ap.pairs = B <= (1 << 29) ? 1 : 0;
   ap.rows = B;
   cudaError_t e = launch_stream<DT>(ap, B, s, dev);
   if (e != cudaSuccess) return e;

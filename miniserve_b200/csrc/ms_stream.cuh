@@ -1,32 +1,47 @@
 // Streaming sampling kernel: one 512-thread CTA per logits row, two CTAs per
-// SM.  The row streams from HBM through a ring of shared-memory stages filled
-// by cp.async.bulk (TMA) copies, so a CTA never holds more than three 4096-
-// element chunks and every synchronisation is CTA-local.  Each warp owns one
-// "unit" of every chunk: 256 consecutive elements.
+// SM.  The row streams from HBM through a 48 KB ring of shared-memory stages
+// filled by cp.async.bulk (TMA) copies -- three 16 KB stages of fp32 or six
+// 8 KB stages of bf16, so both dtypes keep the same bytes in flight -- and
+// every synchronisation is CTA-local.  A chunk is 4096 elements; each warp
+// owns one "unit" of every chunk: 256 consecutive elements.
 //
 //   argmax rows (temperature 0, or top_k == 1)  one pass: per-thread first
 //                                                maximum, block argmax
-//   top-k rows (2 <= top_k <= kStTopK)          one pass: adaptive threshold
-//                                                + candidate buffer, exact
-//                                                finish on <= top_k entries
-//   full-softmax rows (no top-k, top_p >= 1)    one pass: per-unit maximum and
-//                                                weight sum; the draw re-reads
-//                                                one unit
-//   top-p-only rows                             pass 1 (L2 evict-last hint):
-//                                                unit maxima and an integer
-//                                                x-grid histogram anchored at
-//                                                chunk 0's maximum, which
-//                                                brackets the top-p crossing;
-//                                                pass 2 (L2): every weight, the
-//                                                per-unit mass above the
-//                                                bracket and the bracket's
-//                                                elements; exact cut, one-unit
-//                                                draw
+//   top-k rows (2 <= top_k <= kStTopK)          one pass: the candidate
+//                                                threshold is a value of chunk
+//                                                0 that the row's top-k set
+//                                                lies above unless chunk 0
+//                                                holds an unlikely share of
+//                                                it; the buffer's size proves
+//                                                it (else a second pass with
+//                                                thresholds from running
+//                                                maxima); exact finish on the
+//                                                buffer
+//   full-softmax rows (no top-k, top_p >= 1)    one pass: per-unit weight
+//                                                sums; the draw re-reads one
+//                                                unit
+//   top-p-only rows                             pass 1: every weight (the
+//                                                exact total) and the unit
+//                                                maxima.  When the largest
+//                                                unit maxima alone reach
+//                                                top_p of the total (a narrow
+//                                                nucleus) the units holding
+//                                                them are re-read and every
+//                                                value above the bound they
+//                                                give is captured: the whole
+//                                                nucleus.  Otherwise (L2) an
+//                                                x-grid histogram brackets the
+//                                                crossing, and a classifying
+//                                                pass over the units that
+//                                                reach the bracket takes the
+//                                                per-unit mass above it and
+//                                                the bracket's elements.
+//                                                Exact cut, one-unit draw.
 //
-// Every weight of a softmax row is the same function of (logit, unit):
-// W_u(v) * f_u with W_u(v) = 2^((v - m_u) log2(e) / T) in fp32 (m_u the unit
-// maximum) and f_u = 2^((m_u - max) log2(e) / T), so totals, cuts and draws
-// agree with each other to the last bit of each term.
+// Every weight of a softmax row is one function of the logit,
+// W(v) = 2^(v * log2(e)/T - a) in fp32 with a row anchor a (the maximum of the
+// first chunk holding a finite value, times log2(e)/T), so totals, cuts and
+// draws agree with each other to the last bit of each term.
 //
 // Semantics follow miniserve/sampler.py:23-68 (see ms_sample.cu).  Rows
 // outside what this kernel finishes exactly (NaN or +inf logits, top_k above
@@ -46,19 +61,28 @@ constexpr int kStThreads = 512;
 constexpr int kStWarps = kStThreads / 32;
 constexpr int kUnit = 256;                      // elements per unit: one warp's share of a chunk
 constexpr int kChunk = kStWarps * kUnit;        // elements per chunk (one TMA copy)
-constexpr int kStages = 3;
+constexpr int kRingBytes = 3 * kChunk * 4;      // the stage ring: 3 fp32 or 6 bf16 chunks
+constexpr int kMaxStages = 6;
+constexpr int kScratchBytes = 16384;            // the ring doubles as three 16 KB scratch areas after the passes
+template <int DT>
+__host__ __device__ constexpr int st_esz() {
+  return DT == MS_DTYPE_F32 ? 4 : 2;
+}
+template <int DT>
+__host__ __device__ constexpr int st_nstages() {
+#ifdef MS_BF16_STAGES
+  if (DT != MS_DTYPE_F32) return MS_BF16_STAGES;
+#endif
+  return kRingBytes / (kChunk * st_esz<DT>());
+}
 constexpr int kCandCap = 6144;                  // top-k candidate buffer entries
 constexpr int kSortCap = 4096;                  // largest set st_sort handles
 constexpr int kRankCap = 1024;                  // largest set sorted by rank counting
 constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
-// top-k loop: chunks whose warp bounds refresh tau (0-2, then every 4th) and
-// chunks that select the buffer's k-th largest (3, 11); a row has at most 64
-// chunks
-constexpr unsigned long long kRefreshChunks = 0x1111111111111117ull;
-constexpr unsigned long long kSelectChunks = (1ull << 3) | (1ull << 11);
-constexpr int kMaxUnits = 1024;                 // per-unit summaries kept per row
+constexpr int kMaxUnits = 2048;                 // per-unit summaries kept per row
 constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
-constexpr int kXBins = 4096;                    // x-grid bins per kSXRange (top-p)
+constexpr int kNarrowUnits = 128;               // top-p: the unit maxima tried as a narrow nucleus's bound
+constexpr int kXBins = 4096;                    // x-grid bins per kSXRange (top-p histogram)
 constexpr float kSXRange = 40.0f;               // units of x = logit / T
 constexpr int kUpBins = 1024;                   // grid bins above the anchor
 constexpr int kSBins = kXBins + kUpBins;        // x-grid bins in all
@@ -69,8 +93,8 @@ constexpr double kHistTol = 4e-5;               // bound on the histogram's runn
 constexpr double kMinTemperature = 1e-30;       // fp32 weights need a finite log2(e)/T
 
 struct StShared {
-  alignas(128) unsigned char stage[kStages][kChunk * 4];
-  alignas(16) uint32_t mstage[kStages][kChunk / 32];  // the chunk's allowed-token bits (StRow::mtma)
+  alignas(128) unsigned char ring[kRingBytes];
+  alignas(16) uint32_t mstage[kMaxStages][kChunk / 32];  // each chunk's allowed-token bits (StRow::mtma)
   union {
     struct {
       uint32_t key[kCandCap];
@@ -78,8 +102,7 @@ struct StShared {
     } c;  // top-k candidates
     struct {
       float m[kMaxUnits];  // unit maxima
-      float s[kMaxUnits];  // unit weight sums; after pass 3 the mass above the bracket
-      float f[kMaxUnits];  // unit scales
+      float s[kMaxUnits];  // full softmax: unit weight sums; top-p: the unit's mass above the bracket
       uint32_t hkey[kHighCap];  // values above the x-grid
       int hidx[kHighCap];
       union {
@@ -87,7 +110,7 @@ struct StShared {
         struct {
           uint32_t key[kSortCap];
           int idx[kSortCap];
-        } g;  // the bracket's elements
+        } g;  // captured elements: the nucleus, or the bracket's elements
       } x;
     } n;
   } w;
@@ -95,8 +118,7 @@ struct StShared {
   int pick[kStWarps][4];  // row ordering: per-warp class counts
   int ptot[4];
   alignas(16) uint32_t sel[4][256];  // st_select_kth: one digit histogram per round
-  unsigned long long full[kStages];
-  double redd[33];
+  unsigned long long full[kMaxStages];
   double r1d[2][64];  // one-barrier reductions (st_bsum and friends): two halves
   int r1i[2][32];
   uint32_t redu[33];
@@ -107,40 +129,50 @@ struct StShared {
   double bcast_d[4];
   int ncand;
   int nhigh;
-  struct {  // written by the partner CTA of a shared row, one slot per exchange
-    float j1_g;
-    uint32_t j2_flags;
-    float j2_vmax;
-    int j2_nhigh;
-    uint32_t j2b_flags;
-    double j3_H;
-    int j4_n;
-    uint32_t j4_flags;
-    double j5_z;
+  // a top-p row shared by the two CTAs of a cluster: each slot is written by
+  // the partner CTA (st_peer_*) before a st_cluster_sync, then read locally
+  struct {
+    float g;          // the partner's first-chunk maximum
+    double z0, t0;    // the partner's prediction sums on its first chunk, relative to g
+    uint32_t flags;   // bit 0 NaN/+inf, bit 1 a copy timed out, bit 2 a weight beyond range, bit 3 overflow
+    float vmax;       // the partner's maximum
+    double zsum;      // the partner's weight total
+    int nhigh;        // the partner's high-list entries
+    int ncand;        // the partner's captured entries
+    int kind;         // rank 0's decision (rank 1 reads it)
+    float v_lo, v_hi;
+    int tail;
   } xch;
 };
+
+// scratch area i (0..2) of the ring, free once no copy is in flight
+__device__ __forceinline__ unsigned char *st_scratch(StShared &sh, int i) { return sh.ring + kScratchBytes * i; }
+
+template <int DT>
+__device__ __forceinline__ const unsigned char *st_stage(const StShared &sh, int s) {
+  return sh.ring + s * (kChunk * st_esz<DT>());
+}
 
 // ------------------------------------------------------------- the stream
 struct StRow {
   const char *g;        // row start in global memory
   const uint32_t *mask; // row of the allowed-token bitmask, or null
   int V;
-  int esz;
   bool tma;             // 16-byte aligned row: chunks arrive by TMA
   bool mtma;            // 16-byte aligned mask row too: whole chunks' mask words arrive with them
   int nchunks;
   int nfull;            // leading chunks delivered whole by TMA
-  int cb, ce;           // the chunks this CTA streams: [cb, ce)
 };
 
 __device__ __forceinline__ uint32_t st_smem(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-// ---- clusters of two CTAs sharing a top-p row (pair mode).  Data crosses
-// between the two CTAs only as stores into the partner's shared memory
-// followed by st_cluster_sync, which every thread of both CTAs reaches at the
-// same points of the shared row's code.
+// ---- clusters of two CTAs sharing a top-p row.  Data crosses between the
+// two CTAs only as stores into the partner's shared memory followed by
+// st_cluster_sync, which every thread of both CTAs reaches at the same points
+// of the shared row's code; the first one comes before any such store, so
+// both CTAs have started.
 __device__ __forceinline__ uint32_t st_crank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -189,11 +221,6 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
-template <int DT>
-__host__ __device__ constexpr int st_esz() {
-  return DT == MS_DTYPE_F32 ? 4 : 2;
-}
-
 // Elements of chunk c delivered by TMA (a multiple of 16 bytes); elements past
 // them (at most 3 fp32 / 7 bf16 at the row's end) are read from global memory.
 template <int DT>
@@ -214,7 +241,7 @@ __device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, in
   if (bytes) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-            st_smem(sh.stage[s])),
+            st_smem(st_stage<DT>(sh, s))),
         "l"(r.g + (int64_t)c * kChunk * st_esz<DT>()), "r"(bytes), "r"(mb), "l"(pol)
         : "memory");
   }
@@ -258,15 +285,16 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
                                         float x[4]) {
   const int ne = min(kChunk, r.V - c * kChunk);
   const int nt = tma_elems<DT>(r, c);
+  const unsigned char *st = st_stage<DT>(sh, s);
   if (j + 4 <= nt) {
     if (DT == MS_DTYPE_F32) {
-      const float4 f = reinterpret_cast<const float4 *>(sh.stage[s])[j >> 2];
+      const float4 f = reinterpret_cast<const float4 *>(st)[j >> 2];
       x[0] = f.x;
       x[1] = f.y;
       x[2] = f.z;
       x[3] = f.w;
     } else {
-      const uint2 h = reinterpret_cast<const uint2 *>(sh.stage[s])[j >> 2];
+      const uint2 h = reinterpret_cast<const uint2 *>(st)[j >> 2];
       x[0] = __uint_as_float(h.x << 16);
       x[1] = __uint_as_float(h.x & 0xFFFF0000u);
       x[2] = __uint_as_float(h.y << 16);
@@ -279,9 +307,8 @@ __device__ __forceinline__ void st_get4(const StShared &sh, const StRow &r, int 
       if (jj >= ne) {
         x[e] = -INFINITY;
       } else if (jj < nt) {
-        x[e] = DT == MS_DTYPE_F32
-                   ? reinterpret_cast<const float *>(sh.stage[s])[jj]
-                   : __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(sh.stage[s])[jj] << 16);
+        x[e] = DT == MS_DTYPE_F32 ? reinterpret_cast<const float *>(st)[jj]
+                                  : __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(st)[jj] << 16);
       } else {
         const int64_t gi = (int64_t)c * kChunk + jj;
         x[e] = DT == MS_DTYPE_F32
@@ -307,8 +334,9 @@ template <int DT>
 __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c, int s, float x[8]) {
   const int j = (threadIdx.x >> 5) * kUnit + (threadIdx.x & 31) * 4;
   if (c < r.nfull) {  // the whole chunk is in the stage (block-uniform)
+    const unsigned char *st = st_stage<DT>(sh, s);
     if (DT == MS_DTYPE_F32) {
-      const float4 *p = reinterpret_cast<const float4 *>(sh.stage[s]);
+      const float4 *p = reinterpret_cast<const float4 *>(st);
       const float4 f0 = p[j >> 2], f1 = p[(j + 128) >> 2];
       x[0] = f0.x;
       x[1] = f0.y;
@@ -319,7 +347,7 @@ __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c
       x[6] = f1.z;
       x[7] = f1.w;
     } else {
-      const uint2 *p = reinterpret_cast<const uint2 *>(sh.stage[s]);
+      const uint2 *p = reinterpret_cast<const uint2 *>(st);
       const uint2 h0 = p[j >> 2], h1 = p[(j + 128) >> 2];
       x[0] = __uint_as_float(h0.x << 16);
       x[1] = __uint_as_float(h0.x & 0xFFFF0000u);
@@ -353,6 +381,51 @@ __device__ __forceinline__ int st_get8(const StShared &sh, const StRow &r, int c
   }
   return c * kChunk + j;
 }
+
+// The same 8 elements of unit u (x[0..3] at u*kUnit + lane*4, x[4..7] 128
+// further on) read from global memory, masked tokens and positions past the
+// row as -inf.  Returns the global index of x[0].
+template <int DT>
+__device__ __forceinline__ int st_load_unit(const StRow &r, int u, float x[8]) {
+  const int j0 = u * kUnit + (threadIdx.x & 31) * 4;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int j = j0 + 128 * h;
+    float *y = x + 4 * h;
+    if (r.tma && j + 4 <= r.V) {
+      if (DT == MS_DTYPE_F32) {
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(r.g) + (j >> 2));
+        y[0] = f.x;
+        y[1] = f.y;
+        y[2] = f.z;
+        y[3] = f.w;
+      } else {
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(r.g) + (j >> 2));
+        y[0] = __uint_as_float(v.x << 16);
+        y[1] = __uint_as_float(v.x & 0xFFFF0000u);
+        y[2] = __uint_as_float(v.y << 16);
+        y[3] = __uint_as_float(v.y & 0xFFFF0000u);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int jj = j + e;
+        y[e] = jj >= r.V ? -INFINITY
+               : DT == MS_DTYPE_F32
+                   ? __ldg(reinterpret_cast<const float *>(r.g) + jj)
+                   : __uint_as_float((uint32_t)__ldg(reinterpret_cast<const unsigned short *>(r.g) + jj) << 16);
+      }
+    }
+    if (r.mask && j < r.V) {  // j..j+3 lie in one mask word
+      const uint32_t mw = __ldg(r.mask + (j >> 5)) >> (j & 31);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (!((mw >> e) & 1u)) y[e] = -INFINITY;
+    }
+  }
+  return j0;
+}
+
 // Maxima that let a NaN through (max.NaN), so one running maximum both finds
 // the row's largest value and flags a NaN; a row holding NaN or +inf
 // (st_bad) leaves the fast paths.
@@ -370,6 +443,12 @@ __device__ __forceinline__ float st_max8n(const float *x) {
   return st_max3n(st_max3n(x[0], x[1], x[2]), st_max3n(x[3], x[4], x[5]), st_maxn(x[6], x[7]));
 }
 __device__ __forceinline__ bool st_bad(float running_max) { return !(running_max < INFINITY); }
+// the warp's maximum (a NaN drops out)
+__device__ __forceinline__ float st_warp_max(float v) {
+  float r;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
 
 // x[e] for a run-time e without indexing the array (which would put it in
 // local memory)
@@ -383,31 +462,169 @@ __device__ __forceinline__ float st_pick8(const float *x, int e) {
 // global index of x[e] given that of x[0]
 __device__ __forceinline__ int st_gidx(int g0, int e) { return e < 4 ? g0 + e : g0 + 124 + e; }
 
-// One pass over the row.  `body(x[8], g0, u)` sees this thread's 8 values of
-// each chunk (st_get8 layout; u = the warp's unit number, index order).
-// Returns false when a copy timed out.  `ph` carries the stages' phase
-// parities across passes.
-template <int DT, class Body>
-__device__ bool st_pass(StShared &sh, const StRow &r, uint64_t pol, uint32_t &ph, Body body) {
-  const int tid = threadIdx.x;
+// Wait for the copies of chunks [c, ce) still in flight after an early exit
+// from st_stream (chunk c sits in stage (c - c0) % stages).
+template <int DT>
+__device__ bool st_drain(StShared &sh, int c0, int c, int ce, uint32_t &ph) {
+  constexpr int S = st_nstages<DT>();
   bool ok = true;
-  if (tid == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int c = r.cb; c < r.cb + kStages && c < r.ce; ++c) st_issue<DT>(sh, r, c, c - r.cb, pol);
+  for (int c2 = c; c2 < ce; ++c2) {
+    const int s2 = (c2 - c0) % S;
+    if (!st_wait(sh, s2, (ph >> s2) & 1u)) ok = false;
+    ph ^= 1u << s2;
   }
-  for (int c = r.cb, s = 0; c < r.ce; ++c, s = s == kStages - 1 ? 0 : s + 1) {
-    if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
-    ph ^= 1u << s;
-    float x[8];
-    const int g0 = st_get8<DT>(sh, r, c, s, x);
-    body(x, g0, c * kStWarps + (tid >> 5));
-    __syncthreads();  // every thread is done with stage s
-    if (tid == 0 && c + kStages < r.ce) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      st_issue<DT>(sh, r, c + kStages, s, pol);
+  return ok;
+}
+
+struct StNoAfter {
+  __device__ __forceinline__ bool operator()(int, int) const { return false; }
+};
+
+// One pass over chunks [c0, c1) of the row: `body(x[8], g0, u, c)` sees this
+// thread's 8 values of chunk c (st_get8 layout; u = the warp's unit number,
+// index order).  With COUNT, body returns this thread's flag, and after the
+// chunk's barrier and the refill of its stage, `after(c, n)` (n = threads
+// whose flag was set) runs in every thread and may end the pass early by
+// returning true.  Returns false when a copy timed out.  `ph` carries the
+// stages' phase parities across passes.  With `issued`, the copies of the
+// first chunks are already under way (st_peek).
+template <int DT, bool COUNT, class Body, class After>
+__device__ __forceinline__ bool st_stream(StShared &sh, const StRow &r, int c0, int c1, uint64_t pol, uint32_t &ph,
+                                          Body body, After after, bool issued = false) {
+  constexpr int S = st_nstages<DT>();
+  const int tid = threadIdx.x;
+  if (tid == 0 && !issued) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int c = c0; c < c0 + S && c < c1; ++c) st_issue<DT>(sh, r, c, c - c0, pol);
+  }
+  bool ok = true;
+#ifdef MS_STREAM_UNROLL
+  for (int cb = c0; cb < c1; cb += S) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const int c = cb + s;
+      if (c >= c1) break;
+#else
+  {
+#pragma unroll 1
+    for (int c = c0, s = 0; c < c1; ++c, s = s == S - 1 ? 0 : s + 1) {
+#endif
+      if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
+      ph ^= 1u << s;
+      float x[8];
+      const int g0 = st_get8<DT>(sh, r, c, s, x);
+      const int u = c * kStWarps + (tid >> 5);
+      int n = 0;
+      if constexpr (COUNT) {
+        n = __syncthreads_count(body(x, g0, u, c));
+      } else {
+        body(x, g0, u, c);
+        __syncthreads();  // every thread is done with stage s
+      }
+      if (tid == 0 && c + S < c1) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        st_issue<DT>(sh, r, c + S, s, pol);
+      }
+      if constexpr (COUNT) {
+        if (after(c, n)) {  // block-uniform
+          if (!st_drain<DT>(sh, c0, c + 1, min(c1, c + S + 1), ph)) ok = false;
+          return __syncthreads_and(ok) != 0;
+        }
+      }
     }
   }
   return __syncthreads_and(ok) != 0;
+}
+
+// Start a pass over chunks [c0, c1) (their first copies) and read chunk c0
+// into x[8] without consuming it: st_stream(..., issued = true) then takes the
+// same copies.  Returns false when the copy timed out.  All threads.
+template <int DT>
+__device__ __forceinline__ bool st_peek(StShared &sh, const StRow &r, int c0, int c1, uint64_t pol, uint32_t ph,
+                                        float x[8]) {
+  constexpr int S = st_nstages<DT>();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int c = c0; c < c0 + S && c < c1; ++c) st_issue<DT>(sh, r, c, c - c0, pol);
+  }
+  const bool ok = st_wait(sh, 0, ph & 1u);
+  st_get8<DT>(sh, r, c0, 0, x);
+  return ok;
+}
+
+// The m-th largest (1 <= m <= kChunk) of the values held in x[8] by every
+// thread, to its leading 16 bits (a lower bound on it, as a key): two rounds
+// of 8-bit digits over the keys in registers.  All threads.
+__device__ uint32_t st_sample_kth(StShared &sh, const float *x, int m) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint32_t key[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) key[e] = fkey(x[e]);
+  __syncthreads();  // no warp still scans the histograms of an earlier selection
+  (&sh.sel[0][0])[tid] = 0u;
+  __syncthreads();
+  uint32_t prefix = 0;
+  int rem = m;
+#pragma unroll
+  for (int d = 0; d < 2; ++d) {
+    const int shift = 24 - 8 * d;
+    uint32_t *h = sh.sel[d];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const bool in = d == 0 || (key[e] >> 24) == prefix;
+      const uint32_t digit = (key[e] >> shift) & 255u;
+      // keys share leading digits heavily: the first active lane's digit
+      // takes one atomic for every lane that holds it
+      const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
+      if (act) {
+        const int first = __ffs(act) - 1;
+        const uint32_t lead = __shfl_sync(0xFFFFFFFFu, digit, first);
+        const unsigned same = __ballot_sync(0xFFFFFFFFu, in && digit == lead);
+        if (lane == first) {
+          atomicAdd(&h[lead], (uint32_t)__popc(same));
+        } else if (in && digit != lead) {
+          atomicAdd(&h[digit], 1u);
+        }
+      }
+    }
+    __syncthreads();
+    // every warp: the digit whose running count from the top reaches rem;
+    // lane l holds digits 255 - 8l - q, q = 0..7
+    const uint4 *h4 = reinterpret_cast<const uint4 *>(h);
+    const uint4 lo = h4[(248 - 8 * lane) >> 2], hi = h4[((248 - 8 * lane) >> 2) + 1];
+    const uint32_t c8[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
+    uint32_t s8 = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s8 += c8[q];
+    uint32_t incl = s8;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - s8;
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= (uint32_t)rem && excl < (uint32_t)rem);
+    uint32_t dig = 0, before = 0;
+    if (hit && lane == __ffs(hit) - 1) {
+      uint32_t acc = excl;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (acc + c8[q] >= (uint32_t)rem) {
+          dig = 255u - (uint32_t)(8 * lane + q);
+          before = acc;
+          break;
+        }
+        acc += c8[q];
+      }
+    }
+    // no hit only for m above the values held, which callers exclude
+    const int src = hit ? __ffs(hit) - 1 : 0;
+    dig = __shfl_sync(0xFFFFFFFFu, dig, src);
+    before = __shfl_sync(0xFFFFFFFFu, before, src);
+    rem -= (int)before;
+    prefix = (prefix << 8) | dig;
+  }
+  return prefix << 16;
 }
 
 __device__ __forceinline__ float warp_sum_f(float v) {
@@ -710,7 +927,7 @@ __device__ void st_draw_sorted(StShared &sh, int &rf, const SampleArgs &a, int r
 // All threads.
 __device__ void st_rank_sort(StShared &sh, uint32_t *key, int *idx, int n, bool by_index) {
   const int tid = threadIdx.x;
-  unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
+  unsigned long long *comp = reinterpret_cast<unsigned long long *>(st_scratch(sh, 0));
   // larger composite = earlier in the target order; all distinct (indices are)
   for (int i = tid; i < n; i += kStThreads) {
     const unsigned long long ni = (unsigned long long)(~(uint32_t)idx[i]);
@@ -790,7 +1007,7 @@ __device__ __forceinline__ uint32_t st_topk_bound_nb(StShared &sh, float rmax, i
 // returns m.  The idle transfer stages hold scratch.  All threads.
 __device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
   const int tid = threadIdx.x;
-  unsigned long long *comp = reinterpret_cast<unsigned long long *>(sh.stage[0]);
+  unsigned long long *comp = reinterpret_cast<unsigned long long *>(st_scratch(sh, 0));
   // (key, ~index) composites: larger = earlier in rank order, all distinct
   auto compose = [&](int i) -> unsigned long long {
     return ((unsigned long long)sh.w.c.key[i] << 32) | (unsigned long long)(~(uint32_t)sh.w.c.idx[i]);
@@ -842,7 +1059,7 @@ __device__ void st_finish_small(StShared &sh, int &rf, const SampleArgs &a, int 
     if (first != 0x7FFFFFFF) nkeep = first + 1;
   }
   // kept entries in index order: position = kept entries of smaller index
-  double *dw = reinterpret_cast<double *>(sh.stage[1]);
+  double *dw = reinterpret_cast<double *>(st_scratch(sh, 1));
   int *didx = sh.w.c.idx + kStTopK;
   if (tid < nkeep) {
     const int my = sh.w.c.idx[tid];
@@ -1005,10 +1222,10 @@ __device__ __forceinline__ void st_record_empty(const SampleArgs &a, int row, ui
 }
 
 // Estimated cost class of a row, most expensive first: 0 top-p rows (two
-// passes), 1 top-k rows with k >= 128 (many candidate inserts), 2 the other
-// top-k rows and full-softmax rows, 3 argmax rows.  The first CTAs of a
-// launch land one per SM, so the top-p rows (fewer than the SMs in a typical
-// batch) also avoid sharing an SM with each other.
+// passes when the nucleus is wide), 1 top-k rows with k >= 128 (many
+// candidate inserts), 2 the other top-k rows and full-softmax rows, 3 argmax
+// rows.  The first CTAs of a launch land one per SM, so the top-p rows (fewer
+// than the SMs in a typical batch) also avoid sharing an SM with each other.
 __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
   const double T = a.temperature[r];
   const int k = a.top_k[r];
@@ -1021,12 +1238,13 @@ __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
 // the CTAs launched first take the longest rows and the batch ends with short
 // ones; -1 for none.  Every CTA computes the same order from the per-row
 // parameters.  One CTA per row: CTA i takes position i.  Pair mode (clusters
-// of two CTAs): cluster i takes work item i - the i-th top-p row,
-// shared by both CTAs (*joint set), or after those, the next two positions,
-// one per CTA (when B plus the top-p rows exceeds the GPU's CTA slots, one
-// row per CTA as without pairs).
+// of two CTAs, 2B CTAs launched): cluster i takes work item i -- the i-th
+// top-p row, shared by both CTAs (*joint set), or after those, the next two
+// positions, one per CTA; the clusters past the work take none.
 __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  *joint = false;
+  if (!a.pairs && (int)blockIdx.x >= B) return -1;
   if (tid < 4) sh.ptot[tid] = 0;
   __syncthreads();
   int n0 = 0, n1 = 0, n2 = 0, n3 = 0;
@@ -1049,12 +1267,9 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
   }
   __syncthreads();
   int want = blockIdx.x;
-  *joint = false;
   if (a.pairs) {
     const int item = blockIdx.x >> 1, np = sh.ptot[0];
-    if (B + np > a.slots) {  // no room to share: one row per CTA
-      if (want >= B) return -1;
-    } else if (item < np) {
+    if (item < np) {
       want = item;
       *joint = true;
     } else {
@@ -1104,6 +1319,18 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
   return sh.bcast_i[0];
 }
 
+// top-k adaptive pass: chunks whose warp bounds refresh tau (0-2, then every
+// 4th) and chunks that select the buffer's k-th largest (3, 11)
+__device__ __forceinline__ bool st_refresh_chunk(int c) { return c < 3 || (c & 3) == 0; }
+__device__ __forceinline__ bool st_select_chunk(int c) { return c == 3 || c == 11; }
+
+// W(v) for two values at once: 2^(v * c - a) (packed fma, two ex2)
+__device__ __forceinline__ f2_t st_w2(f2_t v, f2_t C, f2_t NA) {
+  float z0, z1;
+  f2_unpack(f2_fma(v, C, NA), z0, z1);
+  return f2_pack(st_ex2(z0), st_ex2(z1));
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) {
   extern __shared__ __align__(128) unsigned char st_raw[];
@@ -1114,6 +1341,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   bool joint;
   const int row = st_pick_row(sh, a, a.pairs ? a.rows : (int)gridDim.x, &joint);
   if (row < 0) return;
+  const int crank = joint ? (int)st_crank() : 0;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const double T = a.temperature[row];
@@ -1122,18 +1350,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   const double U = a.uniforms[row];
   const int V = a.V;
   const bool shard = a.records != nullptr;
-  const int crank = joint ? (int)st_crank() : 0;
-  if (joint) {
-    // a top-p row is shared when both halves stream at least one chunk and
-    // the row takes the streaming path; otherwise the first CTA takes it alone
-    const bool share = T >= kMinTemperature && !isinf(T) && !(k >= 1 && k < V) && P < 1.0 && V > kChunk && !shard;
-    if (!share) {
-      if (crank == 1) return;
-      joint = false;
-    }
-  }
   if (!(T >= 0.0) || isinf(T)) {  // negative, NaN or infinite temperature
-    if (tid == 0) {
+    if (tid == 0 && crank == 0) {
       if (shard) st_record_empty(a, row, MS_ROW_BAD_TEMPERATURE);
       else write_row(a, row, -1, 0.0f, MS_ROW_BAD_TEMPERATURE);
     }
@@ -1142,7 +1360,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // a row this kernel does not finish: the generic kernel takes it, or in
   // sharded mode its record says why (nonfinite: a NaN / +inf logit)
   auto leave = [&](bool nonfinite) {
-    if (tid == 0) {
+    if (tid == 0 && crank == 0) {
       if (shard) st_record_empty(a, row, nonfinite ? MS_ROW_NONFINITE : MS_ROW_UNSUPPORTED);
       else a.status[row] = kRowPending;
     }
@@ -1180,17 +1398,14 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     return;
   }
   StRow r;
-  r.esz = DT == MS_DTYPE_F32 ? 4 : 2;
-  r.g = reinterpret_cast<const char *>(a.logits) + (int64_t)row * a.ld * r.esz;
+  r.g = reinterpret_cast<const char *>(a.logits) + (int64_t)row * a.ld * st_esz<DT>();
   r.mask = a.mask ? a.mask + (int64_t)row * a.mask_ld : nullptr;
   r.V = V;
   r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
   r.mtma = r.mask && r.tma && (reinterpret_cast<uintptr_t>(r.mask) & 15u) == 0;
   r.nchunks = (V + kChunk - 1) / kChunk;
-  r.cb = joint && crank == 1 ? r.nchunks / 2 : 0;
-  r.ce = joint && crank == 0 ? r.nchunks / 2 : r.nchunks;
   r.nfull = r.tma ? V / kChunk : 0;
-  if (tid < kStages) {
+  if (tid < st_nstages<DT>()) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
   }
   if (tid < kStWarps) sh.wbound[tid] = 0u;
@@ -1212,17 +1427,20 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // larger chunk maximum moves the thread's best to its first occurrence
     float tm = -INFINITY, tnan = -INFINITY;
     int ti = 0x7FFFFFFF;
-    ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int) {
-      const float cm = st_max8n(x);
-      tnan = st_maxn(tnan, cm);
-      if (cm > tm) {  // rare after the first chunks
-        int e = 7;
+    ok = st_stream<DT, false>(
+        sh, r, 0, r.nchunks, pol_stream, ph,
+        [&](const float *x, int g0, int, int) {
+          const float cm = st_max8n(x);
+          tnan = st_maxn(tnan, cm);
+          if (cm > tm) {  // rare after the first chunks
+            int e = 7;
 #pragma unroll
-        for (int q = 6; q >= 0; --q) e = x[q] == cm ? q : e;
-        tm = cm;
-        ti = st_gidx(g0, e);
-      }
-    });
+            for (int q = 6; q >= 0; --q) e = x[q] == cm ? q : e;
+            tm = cm;
+            ti = st_gidx(g0, e);
+          }
+        },
+        StNoAfter());
     const bool bad = st_bad(tnan);
     uint32_t bk = tm > -INFINITY ? fkey(tm) : 0u;
     int bi = tm > -INFINITY ? ti : 0x7FFFFFFF;
@@ -1261,10 +1479,19 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
 
   // ================================================================= top-k
   if (mode == kStTopKMode) {
-    // Candidates are values >= tau (> when strict).  tau rises to lower
-    // bounds of the row's k-th largest value (st_topk_bound: with a barrier on
-    // chunk 0, barrier-free every 4th chunk after); ties at tau stay
-    // candidates.  A warp with no value at or above tau skips the insert.
+    // Candidates are values >= tau (> when strict); ties at tau stay
+    // candidates.  A lane with no value at or above tau skips the insert.
+    //
+    // First pass: tau is the m-th largest value of chunk 0 (to 16 bits).
+    // Chunk 0 holds lam = k * n0 / V of the row's top-k set on average; with
+    // m = lam + 4 sqrt(lam) + 4 the row's k-th largest value lies below tau
+    // only when chunk 0 holds m members of that set (a Poisson tail below
+    // 1e-4 for a row in random order).  Every value >= tau is a candidate, so
+    // at least k candidates prove that tau is low enough; with fewer, a
+    // second pass starts over with tau rising to lower bounds of the k-th
+    // largest from the lanes' running maxima (st_topk_bound) and the buffer's
+    // k-th largest (chunks 3 and 11).  A buffer that could overflow is cut to
+    // its entries at or above its k-th largest either way.
     float tau = -INFINITY;
     float tf = -FLT_MAX;  // candidates: x >= tf (the next float above tau when strict; -inf never)
     auto set_tau = [&](float t, bool strict) {
@@ -1275,129 +1502,145 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const int jw = (k + kStWarps - 1) / kStWarps;  // <= 16
     bool over = false;
     bool exact_tau = false;  // tau is the k-th largest value seen (after a compaction)
+    bool compacted = false;
     int ub = 0;  // bound on the buffer's size (its size after a sync point), the same in every thread
     // shard_sum: this lane's running maximum and sum of weights relative to it
     float sm = -INFINITY, ss = 0.0f;
     StW Ws;
     const double cls = 1.4426950408889634 / T;  // log2(e) / T
     if (shard_sum) Ws.set_t(T);
-    if (tid == 0) {
-      for (int c = 0; c < kStages && c < r.nchunks; ++c) st_issue<DT>(sh, r, c, c, pol_stream);
+    const int n0 = min(kChunk, V);
+    int msamp = k;
+    if (r.nchunks > 1) {
+      const double lam = (double)k * (double)n0 / (double)V;
+      msamp = (int)ceil(lam + 4.0 * sqrt(lam) + 4.0);
     }
-    int c = 0;
-    for (int s = 0; c < r.nchunks; ++c, s = s == kStages - 1 ? 0 : s + 1) {
-      if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
-      ph ^= 1u << s;
-      float x[8];
-      const int g0 = st_get8<DT>(sh, r, c, s, x);
-      const float cm = st_max8n(x);
-      rmax = st_maxn(rmax, cm);
-      if (shard_sum) {  // online softmax total (block-uniform branch)
-        const float nm = fmaxf(sm, cm);
-        if (nm > sm) {
-          ss = sm > -INFINITY ? ss * (float)exp2(((double)sm - (double)nm) * cls) : 0.0f;
-          sm = nm;
-          Ws.set_m(sm);
-        }
-        if (sm > -INFINITY) {
-          const StW2 W2(Ws);
-          f2_t a2 = W2(f2_pack(x[0], x[1]));
-#pragma unroll
-          for (int j = 1; j < 4; ++j) a2 = f2_add(a2, W2(f2_pack(x[2 * j], x[2 * j + 1])));
-          float a0, a1;
-          f2_unpack(a2, a0, a1);
-          ss += a0 + a1;
-        }
-      }
-      if (!exact_tau && ((kRefreshChunks >> c) & 1u)) {
-        const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
-        if (bmin != 0u && key_to_float(bmin) > tau) set_tau(key_to_float(bmin), false);
-      }
-      // insert: only lanes holding a candidate, one shared atomic per lane for
-      // all its entries.  The buffer holds at most kCandCap - kChunk entries
-      // before each chunk, so it cannot overflow.
-      int cnt = 0;
-      if (cm >= tf) {  // NaN never
-        unsigned m = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m |= (x[e] >= tf ? 1u : 0u) << e;
-        cnt = __popc(m);
-        int pos = atomicAdd(&sh.ncand, cnt);  // positions only
-        do {
-          const int e = __ffs(m) - 1;
-          m &= m - 1;
-          sh.w.c.key[pos] = fkey(st_pick8(x, e));
-          sh.w.c.idx[pos] = st_gidx(g0, e);
-          ++pos;
-        } while (m);
-      }
-      // barrier: stage s is free and the buffer settled; every inserting lane
-      // added at most 8 entries
-      ub += 8 * __syncthreads_count(cnt > 0);
-      // refill stage s first, so the copy runs under a select or compaction
-      if (tid == 0 && c + kStages < r.nchunks) {
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        st_issue<DT>(sh, r, c + kStages, s, pol_stream);
-      }
-      const bool sel_pt = (kSelectChunks >> c) & 1u;
-      if (sel_pt || ub > kCandCap - kChunk) {
-        // a sync point: every thread reads the exact size before any inserts again
-        const int n0 = sh.ncand;
+    msamp = min(msamp, n0);
+    for (int attempt = 0;; ++attempt) {
+      const bool sampled = attempt == 0;
+      if (!sampled) {  // start over
+        tau = -INFINITY;
+        tf = -FLT_MAX;
+        rmax = -INFINITY;
+        over = exact_tau = compacted = false;
+        ub = 0;
+        sm = -INFINITY;
+        ss = 0.0f;
         __syncthreads();
-        ub = n0;
-        // early on (chunks 3 and 11) the buffer's k-th largest, to 16 leading
-        // bits (two digit rounds; a lower bound within 2^-7 of it), is a far
-        // tighter tau than the warp bound and cuts the inserts of the rest of
-        // the row; entries below it stay in the buffer, dead
-        if (sel_pt && n0 >= 2 * k && n0 <= kCandCap - kChunk) {
-          int above;
-          set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, n0, k, &above, 2)), false);
-          exact_tau = true;
-        }
-        // shrink to the entries >= the buffer's k-th largest (ties kept) when
-        // the next chunk could overflow the buffer
-        if (n0 > kCandCap - kChunk) {
-          int above;
-          const uint32_t kk = st_select_kth(sh, sh.w.c.key, n0, k, &above);
-          uint32_t kv[kCandCap / kStThreads];
-          int iv[kCandCap / kStThreads];
-          int nk = 0;
-          for (int i = tid; i < n0; i += kStThreads) {
-            if (sh.w.c.key[i] >= kk) {
-              kv[nk] = sh.w.c.key[i];
-              iv[nk] = sh.w.c.idx[i];
-              ++nk;
+        if (tid < kStWarps) sh.wbound[tid] = 0u;
+        if (tid == 0) sh.ncand = 0;
+        __syncthreads();
+      }
+      ok = st_stream<DT, true>(
+          sh, r, 0, r.nchunks, pol_stream, ph,
+          [&](const float *x, int g0, int, int c) -> int {
+            const float cm = st_max8n(x);
+            rmax = st_maxn(rmax, cm);
+            if (shard_sum) {  // online softmax total (block-uniform branch)
+              const float nm = fmaxf(sm, cm);
+              if (nm > sm) {
+                ss = sm > -INFINITY ? ss * (float)exp2(((double)sm - (double)nm) * cls) : 0.0f;
+                sm = nm;
+                Ws.set_m(sm);
+              }
+              if (sm > -INFINITY) {
+                const StW2 W2(Ws);
+                f2_t a2 = W2(f2_pack(x[0], x[1]));
+#pragma unroll
+                for (int j = 1; j < 4; ++j) a2 = f2_add(a2, W2(f2_pack(x[2 * j], x[2 * j + 1])));
+                float a0, a1;
+                f2_unpack(a2, a0, a1);
+                ss += a0 + a1;
+              }
             }
-          }
-          int kex, kin, ktot;
-          block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
-          for (int q = 0; q < nk; ++q) {
-            sh.w.c.key[kex + q] = kv[q];
-            sh.w.c.idx[kex + q] = iv[q];
-          }
-          if (tid == 0) sh.ncand = ktot;
-          __syncthreads();
-          ub = ktot;
-          set_tau(key_to_float(kk), true);  // >= k entries >= kk are held: a later equal value ranks below
-          exact_tau = true;
-          if (ktot > kCandCap - kChunk) over = true;  // heavy ties
-        }
+            if (sampled) {
+              if (c == 0) {  // block-uniform: the threshold from chunk 0's values
+                const uint32_t tk = st_sample_kth(sh, x, msamp);
+                if (tk > kNegInfKey) set_tau(key_to_float(tk), false);
+              }
+            } else if (!exact_tau && st_refresh_chunk(c)) {
+              const uint32_t bmin = c == 0 ? st_topk_bound(sh, rmax, jw) : st_topk_bound_nb(sh, rmax, jw);
+              if (bmin != 0u && key_to_float(bmin) > tau) set_tau(key_to_float(bmin), false);
+            }
+            // insert: only lanes holding a candidate, one shared atomic per
+            // lane for all its entries.  The buffer holds at most
+            // kCandCap - kChunk entries before each chunk, so it cannot overflow.
+            int cnt = 0;
+            if (cm >= tf) {  // NaN never
+              unsigned m = 0;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) m |= (x[e] >= tf ? 1u : 0u) << e;
+              cnt = __popc(m);
+              int pos = atomicAdd(&sh.ncand, cnt);  // positions only
+              do {
+                const int e = __ffs(m) - 1;
+                m &= m - 1;
+                sh.w.c.key[pos] = fkey(st_pick8(x, e));
+                sh.w.c.idx[pos] = st_gidx(g0, e);
+                ++pos;
+              } while (m);
+            }
+            return cnt > 0;
+          },
+          [&](int c, int nins) -> bool {
+            // every inserting lane added at most 8 entries
+            ub += 8 * nins;
+            const bool sel_pt = !sampled && !exact_tau && st_select_chunk(c);
+            if (sel_pt || ub > kCandCap - kChunk) {
+              // a sync point: every thread reads the exact size before any inserts again
+              const int nb = sh.ncand;
+              __syncthreads();
+              ub = nb;
+              // early on (chunks 3 and 11) the buffer's k-th largest, to 16
+              // leading bits (two digit rounds; a lower bound within 2^-7 of
+              // it), is a far tighter tau than the warp bound and cuts the
+              // inserts of the rest of the row; entries below it stay in the
+              // buffer, dead
+              if (sel_pt && nb >= 2 * k && nb <= kCandCap - kChunk) {
+                int above;
+                set_tau(key_to_float(st_select_kth(sh, sh.w.c.key, nb, k, &above, 2)), false);
+                exact_tau = true;
+              }
+              // shrink to the entries >= the buffer's k-th largest (ties kept)
+              // when the next chunk could overflow the buffer
+              if (nb > kCandCap - kChunk) {
+                int above;
+                const uint32_t kk = st_select_kth(sh, sh.w.c.key, nb, k, &above);
+                uint32_t kv[kCandCap / kStThreads];
+                int iv[kCandCap / kStThreads];
+                int nk = 0;
+                for (int i = tid; i < nb; i += kStThreads) {
+                  if (sh.w.c.key[i] >= kk) {
+                    kv[nk] = sh.w.c.key[i];
+                    iv[nk] = sh.w.c.idx[i];
+                    ++nk;
+                  }
+                }
+                int kex, kin, ktot;
+                block_scan<kStThreads, int>(nk, kex, kin, ktot, sh.redi);
+                for (int q = 0; q < nk; ++q) {
+                  sh.w.c.key[kex + q] = kv[q];
+                  sh.w.c.idx[kex + q] = iv[q];
+                }
+                if (tid == 0) sh.ncand = ktot;
+                __syncthreads();
+                ub = ktot;
+                set_tau(key_to_float(kk), true);  // >= k entries >= kk are held: a later equal value ranks below
+                exact_tau = compacted = true;
+                if (ktot > kCandCap - kChunk) over = true;  // heavy ties
+              }
+            }
+            return over;
+          });
+      const bool bad = st_bad(rmax);
+      if (__syncthreads_or(bad || !ok || over)) {
+        leave(__syncthreads_or(bad) != 0);
+        return;
       }
-      if (over) break;
-    }
-    if (over) {
-      // copies of chunks c+1 .. c+kStages are in flight: let them land
-      // before this CTA's shared memory is released
-      for (int c2 = c + 1; c2 < r.nchunks && c2 <= c + kStages; ++c2) {
-        const int s2 = c2 % kStages;
-        if (!st_wait(sh, s2, (ph >> s2) & 1u)) ok = false;
-        ph ^= 1u << s2;
-      }
-    }
-    const bool bad = st_bad(rmax);
-    if (__syncthreads_or(bad || !ok || over)) {
-      leave(__syncthreads_or(bad) != 0);
-      return;
+      // fewer than k values at or above the sampled threshold: the row's
+      // top-k set may reach below it
+      if (sampled && !compacted && tau > -INFINITY && sh.ncand < k) continue;
+      break;
     }
     const float vmax = block_max_f<kStThreads>(rmax, sh.redf);
     if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
@@ -1468,90 +1711,33 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     return;
   }
 
-  // ====================================================== softmax over all
-  StW W;
-  W.set_t(T);
+  // ========================================================== softmax rows
+  // W(v) = 2^(v * cw - aw): cw = log2(e) / T rounded once, aw = G * cw with G
+  // the maximum of the first chunk holding a finite value (the row maximum on
+  // the rare second try, when a later value would give a weight beyond
+  // 2^60).  A rounding of cw scales every exponent alike; one of aw scales
+  // every weight alike and cancels in every ratio.
   const double cl = 1.4426950408889634 / T;  // log2(e) / T
+  const float cw = (float)cl;
+  float G = -INFINITY, aw = 0.0f, v_ovf = INFINITY;
+  auto set_anchor = [&](float g) {
+    G = g;
+    aw = g * cw;
+    v_ovf = (float)((double)g + 60.0 / cl);
+  };
+  auto W = [&](float v) -> float { return st_ex2(fmaf(v, cw, -aw)); };  // -inf weighs 0
+  const bool topp = mode == kStNucleus;
   const int nu = r.nchunks * kStWarps;
-  double *kd = reinterpret_cast<double *>(sh.stage[1]);  // per-unit kept mass (stages idle after the passes)
-  auto unit_w = [&](float v, int gi) -> double {         // float64 weight of element gi, relative to the max
-    const int u = gi / kUnit;
-    StW Wu = W;
-    Wu.set_m(sh.w.n.m[u]);
-    return (double)Wu(v) * (double)sh.w.n.f[u];
-  };
-  // after pass 1: the row maximum, or a status written and false
-  auto finish_max = [&](float vmax_t, float &vmax) -> bool {
-    bool anybad;
-    vmax = st_bmaxf(sh, rf, vmax_t, st_bad(vmax_t) || !ok, &anybad);
-    if (anybad) {
-      if (tid == 0) a.status[row] = kRowPending;
-      return false;
-    }
-    if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
-      if (tid == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
-      return false;
-    }
-    if (!(fabs((double)vmax) * cl < 1e37)) {  // max * log2(e)/T beyond fp32 range
-      if (tid == 0) a.status[row] = kRowPending;
-      return false;
-    }
-    return true;
-  };
 
-  if (mode == kStFull) {
-    // one pass (HBM): per-unit maximum m_u and weight sum s_u = sum W_u(v)
-    float vmax_t = -INFINITY;  // NaN once a NaN has been seen
-    ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int, int u) {
-      f2_t X[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) X[j] = f2_pack(x[2 * j], x[2 * j + 1]);
-      const float cm = st_max8n(x);
-      vmax_t = st_maxn(vmax_t, cm);
-      const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
-      float mu = -INFINITY, su = 0.0f;
-      if (km != 0u) {  // warp-uniform
-        mu = key_to_float(km);
-        StW Wu = W;
-        Wu.set_m(mu);
-        const StW2 W2(Wu);
-        f2_t s2 = W2(X[0]);
-#pragma unroll
-        for (int j = 1; j < 4; ++j) s2 = f2_add(s2, W2(X[j]));
-        float a0, a1;
-        f2_unpack(s2, a0, a1);
-        su = warp_sum_f(a0 + a1);
-      }
-      if (lane == 0) {
-        sh.w.n.m[u] = mu;
-        sh.w.n.s[u] = su;
-      }
-    });
-    float vmax;
-    if (!finish_max(vmax_t, vmax)) return;
-    double zs = 0.0;
-    for (int u = tid; u < nu; u += kStThreads) {
-      const float mu = sh.w.n.m[u];
-      const float fu = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
-      sh.w.n.f[u] = fu;
-      kd[u] = (double)sh.w.n.s[u] * (double)fu;
-      zs += kd[u];
-    }
-    const double total = st_bsum(sh, rf, zs);  // its barrier follows every kd write
-    st_draw_units<DT>(sh, rf, a, r, row, nu, kd, total, U,
-                      [&](float v, int gi) -> double { return v > -INFINITY ? unit_w(v, gi) : 0.0; });
-    return;
-  }
-
-  // ============================================================ top-p only
-  // x-grid coordinate t = (G - v) * xs + kUpBins + 1: kXBins bins per
-  // kSXRange units of x = logit / T, anchored at G (the maximum of chunk 0, or
-  // the row maximum on the fallback pass).  t < 1: more than kUpBins bins
-  // above G, kept exactly in the high list (index 0).  Index floor(t) in
-  // 1..kSBins: a grid bin; kSBins + 1: the tail (and masked tokens).  hq[i] holds the
-  // fixed-point sum of kQScale * e^-((t - i) * dx) over the elements of index
-  // i, so index i carries mass e^-((i - 1 - kUpBins) * dx) * hq[i] / kQScale
-  // relative to G.  The histogram only places the bracket: pass 2 checks the
+  // Top-p histogram.  x-grid coordinate t = (Gh - v) * xs + kUpBins + 1:
+  // kXBins bins per kSXRange units of x = logit / T, anchored at Gh (the
+  // weights' anchor G when built in pass 1, else the row maximum).  t < 1:
+  // more than kUpBins bins above Gh, kept exactly in the high list (index 0).
+  // Index floor(t) in 1..kSBins: a grid bin; kSBins + 1: the tail (and masked
+  // tokens).  hq[i] holds the fixed-point sum of kQScale * e^-((t - i) * dx)
+  // over the elements of index i, so index i carries mass
+  // e^-((i - 1 - kUpBins) * dx) * hq[i] / kQScale relative to Gh.  The
+  // histogram only places the bracket: the classifying pass checks the
   // crossing exactly, and a bracket that misses it leaves the row pending.
   const float xs = (float)((double)kXBins / ((double)kSXRange * T));
   const float dx = kSXRange / (float)kXBins;
@@ -1559,9 +1745,18 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // round(kQScale * e^-(fr*dx)) + 2^23 as a float (quadratic, error (fr*dx)^3/6 < 1.6e-7)
   const float q0 = 8388608.0f + kQScale, q1 = -kQScale * dx, q2 = 0.5f * kQScale * dx * dx;
   uint32_t *hq = sh.w.n.x.hq;
-  float G = -INFINITY;
+  float Gh = -INFINITY;
   float v_high = INFINITY;  // no value at or below it lies above the grid (t < 1)
   float v_tail = INFINITY;  // every value at or below it lies in the tail (t >= kSBins + 1)
+  auto set_hist_anchor = [&](float g) {
+    Gh = g;
+    v_high = __double2float_rd((double)g + (double)(kUpBins - 1) / (double)xs);
+    v_tail = __double2float_rd((double)g - (double)kXBins / (double)xs);
+  };
+  auto hist_clear = [&]() {  // the caller's next barrier orders it
+    for (int i = tid; i < kQSlots; i += kStThreads) hq[i] = 0u;
+    if (tid == 0) sh.nhigh = 0;
+  };
   // Histogram of this lane's 8 values (x[4..7] sit 128 after x[0..3]), cm
   // their maximum, in packed pairs.  Only grid bins 1..kSBins take mass:
   // values above the grid (t < 1) are kept exactly in the high list, and the
@@ -1570,7 +1765,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (__any_sync(0xFFFFFFFFu, cm > v_high)) {  // rare: some value may lie above the grid
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        if (fmaf(G - x[e], xs, t_off) < 1.0f) {
+        if (fmaf(Gh - x[e], xs, t_off) < 1.0f) {
           const int pos = atomicAdd(&sh.nhigh, 1);
           if (pos < kHighCap) {
             sh.w.n.hkey[pos] = fkey(x[e]);
@@ -1580,7 +1775,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
     }
     if (!__any_sync(0xFFFFFFFFu, cm > v_tail)) return;  // the warp's values all lie in the tail
-    const f2_t G2 = f2_pack(G, G), XS2 = f2_pack(xs, xs), OFF2 = f2_pack(t_off, t_off);
+    const f2_t G2 = f2_pack(Gh, Gh), XS2 = f2_pack(xs, xs), OFF2 = f2_pack(t_off, t_off);
     const f2_t M2 = f2_pack(8388608.0f, 8388608.0f);
     const f2_t Q0 = f2_pack(q0, q0), Q1 = f2_pack(q1, q1), Q2 = f2_pack(q2, q2);
 #pragma unroll
@@ -1595,130 +1790,256 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       float tb0, tb1, qa, qb;
       f2_unpack(TB, tb0, tb1);
       f2_unpack(f2_fma(f2_fma(FR, Q2, Q1), FR, Q0), qa, qb);
-      // grid bins only: the high list's index 0 and the tail carry no histogram mass
       const uint32_t i0 = __float_as_uint(tb0) - 0x4B000000u, i1 = __float_as_uint(tb1) - 0x4B000000u;
       if (i0 - 1u < (uint32_t)kSBins) atomicAdd(&hq[i0], __float_as_uint(qa) - 0x4B000000u);
       if (i1 - 1u < (uint32_t)kSBins) atomicAdd(&hq[i1], __float_as_uint(qb) - 0x4B000000u);
     }
   };
-  auto set_anchor = [&](float g) {
-    G = g;
-    v_high = __double2float_rd((double)g + (double)(kUpBins - 1) / (double)xs);
-    v_tail = __double2float_rd((double)g - (double)kXBins / (double)xs);
-  };
-  auto hist_clear = [&]() {
-    for (int i = tid; i < kQSlots; i += kStThreads) hq[i] = 0u;
-    if (tid == 0) sh.nhigh = 0;
-    __syncthreads();
-  };
 
-  // pass 1 (HBM, kept in L2): unit maxima, histogram anchored at chunk 0's max
-  float vmax_t = -INFINITY;  // NaN once a NaN has been seen
-  hist_clear();
-  if (tid == 0) {
-    for (int c = r.cb; c < r.cb + kStages && c < r.ce; ++c) st_issue<DT>(sh, r, c, c - r.cb, pol_keep);
-  }
-  for (int c = r.cb, s = 0; c < r.ce; ++c, s = s == kStages - 1 ? 0 : s + 1) {
-    if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
-    ph ^= 1u << s;
-    float x[8];
-    const int g0 = st_get8<DT>(sh, r, c, s, x);
-    const float cm = st_max8n(x);
-    vmax_t = st_maxn(vmax_t, cm);
-    const uint32_t km = __reduce_max_sync(0xFFFFFFFFu, cm > -INFINITY ? fkey(cm) : 0u);
-    if (lane == 0) sh.w.n.m[c * kStWarps + (tid >> 5)] = km != 0u ? key_to_float(km) : -INFINITY;
-    if (c == r.cb) {
-      float g = st_bmaxf(sh, rf, cm, false, nullptr);
-      if (joint) {  // one anchor for both halves: the larger first-chunk maximum
-        if (tid == 0) st_peer_f32(st_peer(&sh.xch.j1_g), g);
-        st_cluster_sync();
-        g = fmaxf(g, sh.xch.j1_g);
-      }
-      set_anchor(g);
-    }
-    if (G > -INFINITY) hist8(x, g0, cm);  // block-uniform
-    __syncthreads();  // every thread is done with stage s
-    if (tid == 0 && c + kStages < r.ce) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      st_issue<DT>(sh, r, c + kStages, s, pol_keep);
-    }
-  }
-  ok = __syncthreads_and(ok) != 0;
-  float vmax;
-  int nhigh_all = sh.nhigh;
-  if (!joint) {
-    if (!finish_max(vmax_t, vmax)) return;
-  } else {
-    // both halves: NaN / +inf, failed copies, the maximum, the high lists
-    bool badc;
-    const float vm = st_bmaxf(sh, rf, vmax_t, st_bad(vmax_t), &badc);
-    if (tid == 0) {
-      st_peer_u32(st_peer(&sh.xch.j2_flags), (badc ? 1u : 0u) | (ok ? 0u : 2u));
-      st_peer_f32(st_peer(&sh.xch.j2_vmax), vm);
-      st_peer_u32(st_peer(&sh.xch.j2_nhigh), (uint32_t)sh.nhigh);
-    }
-    st_cluster_sync();
-    const uint32_t pf = sh.xch.j2_flags;
-    vmax = fmaxf(vm, sh.xch.j2_vmax);
-    nhigh_all += sh.xch.j2_nhigh;
-    const int stop = (badc || !ok || pf != 0u) ? 1 : !(vmax > -INFINITY) ? 2 : !(fabs((double)vmax) * cl < 1e37) ? 1 : 0;
-    if (stop) {  // both CTAs stop here
-      if (crank == 0 && tid == 0) {
-        if (stop == 2) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);  // every logit -inf (sampler.py:46-47)
-        else a.status[row] = kRowPending;
-      }
-      return;
-    }
-  }
-  for (int u = r.cb * kStWarps + tid; u < r.ce * kStWarps; u += kStThreads) {
-    const float mu = sh.w.n.m[u];
-    sh.w.n.f[u] = mu > -INFINITY ? (float)exp2(((double)mu - (double)vmax) * cl) : 0.0f;
-  }
-  if (!(G > -INFINITY) || nhigh_all > kHighCap) {
-    // chunk 0 held no finite logit, or many values lie far above its max:
-    // histogram pass (L2) anchored at the row maximum, nothing above it
-    __syncthreads();
-    set_anchor(vmax);
-    hist_clear();
-    ok = st_pass<DT>(sh, r, pol_keep, ph, [&](const float *x, int g0, int) {
-      hist8(x, g0, st_max8n(x));
-    });
-    if (joint) {
-      if (tid == 0) st_peer_u32(st_peer(&sh.xch.j2b_flags), ok ? 0u : 1u);
-      st_cluster_sync();
-      ok = ok && sh.xch.j2b_flags == 0u;
-    }
-    if (!ok) {
-      if (crank == 0 && tid == 0) a.status[row] = kRowPending;
-      return;
-    }
-  }
-  __syncthreads();
-  // the high list: exact weights
-  const int nh = min(sh.nhigh, kHighCap);
-  double hs = 0.0;
-  for (int i = tid; i < nh; i += kStThreads) hs += unit_w(key_to_float(sh.w.n.hkey[i]), sh.w.n.hidx[i]);
-  double H = st_bsum(sh, rf, hs);
+  // A top-p row shared by a cluster: this CTA streams chunks [c0, c1) (the
+  // first CTA the first half).  The two halves meet at cluster barriers: the
+  // anchor and the wide prediction, the pass-1 totals, the second half's unit
+  // maxima and histogram, the first CTA's decision, and the classifying
+  // pass's entries; every decision between barriers is computed in both CTAs
+  // from the same exchanged values, so both reach the same barriers or leave
+  // at the same point, and only the first CTA writes the row's result.
+  int c0 = 0, c1 = r.nchunks;
   if (joint) {
-    // one histogram and one high-list mass for both halves: each CTA copies
-    // its histogram into the partner's idle stages and adds the partner's copy
-    const uint4 *h4 = reinterpret_cast<const uint4 *>(hq);
-    const uint32_t dst = st_peer(sh.stage[0]);
-    for (int i = tid; i < kQSlots / 4; i += kStThreads) st_peer_v4(dst + 16u * (uint32_t)i, h4[i]);
-    if (tid == 0) st_peer_f64(st_peer(&sh.xch.j3_H), H);
-    st_cluster_sync();
-    const uint32_t *rcv = reinterpret_cast<const uint32_t *>(sh.stage[0]);
-    for (int i = tid; i < kQSlots; i += kStThreads) hq[i] += rcv[i];
-    H = crank == 0 ? H + sh.xch.j3_H : sh.xch.j3_H + H;  // the same sum in both CTAs
-    __syncthreads();
+    if (r.nchunks < 2) {  // too short to share: the first CTA takes it alone
+      if (crank == 1) return;
+      joint = false;
+    } else {
+      c0 = crank == 0 ? 0 : r.nchunks / 2;
+      c1 = crank == 0 ? r.nchunks / 2 : r.nchunks;
+      st_cluster_sync();  // both CTAs have started before either stores into the other
+    }
   }
-  // the bracket [i_lo, i_hi] of indices (-1 = the high list, kSBins + 1 =
-  // the tail): where the estimated running mass crosses P*total -/+
-  // kHistTol*total.
-  int i_lo, i_hi;
-  {
+  float vmax = -INFINITY;
+  double zsum = 0.0;  // the row's total of W
+  // top-p: a wide nucleus predicted at the first chunk(s), whose histogram
+  // pass 1 builds too (when the chunk's unit maxima carry under 0.8 top_p of
+  // its mass, the row's largest values rarely reach top_p of the total)
+  bool wide = false;
+  for (int attempt = 0;; ++attempt) {
+    if (attempt > 0) set_anchor(vmax);  // no weight above 1
+    wide = false;
+    if (topp) hist_clear();
+    double zl = 0.0;           // this lane's total
+    float vmax_t = -INFINITY;  // NaN once a NaN has been seen
+    bool ovf = false;
+    const uint64_t pol1 = topp ? pol_keep : pol_stream;
+    // the first chunk first: the anchor, and for top-p rows the prediction
+    {
+      float x[8];
+      if (!st_peek<DT>(sh, r, c0, c1, pol1, ph, x)) ok = false;
+      const float cm = st_max8n(x);
+      float g = G;
+      if (!(G > -INFINITY)) {
+        g = st_bmaxf(sh, rf, cm, false, nullptr);  // its barrier also orders hist_clear
+      } else {
+        __syncthreads();
+      }
+      // the prediction sums relative to g: the chunk's weight and its units' maxima's
+      double z0 = 0.0, t0 = 0.0;
+      if (topp && g > -INFINITY) {  // block-uniform
+        const float gw = g * cw;
+        float part = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part += st_ex2(fmaf(x[e], cw, -gw));
+        const float mu = st_warp_max(cm);
+        st_bsum2(sh, rf, (double)part, lane == 0 ? (double)st_ex2(fmaf(mu, cw, -gw)) : 0.0, z0, t0);
+      }
+      if (joint) {
+        // one anchor for both halves (the larger first-chunk maximum) and the
+        // prediction sums of both halves rescaled to it
+        if (tid == 0) {
+          st_peer_f32(st_peer(&sh.xch.g), g);
+          st_peer_f64(st_peer(&sh.xch.z0), z0);
+          st_peer_f64(st_peer(&sh.xch.t0), t0);
+        }
+        st_cluster_sync();
+        const float gp = sh.xch.g;
+        const float gm = fmaxf(g, gp);
+        if (gm > -INFINITY) {
+          const double fa = g > -INFINITY ? exp2(((double)g - (double)gm) * cl) : 0.0;
+          const double fb = gp > -INFINITY ? exp2(((double)gp - (double)gm) * cl) : 0.0;
+          const double za = z0 * fa, zb = sh.xch.z0 * fb, ta = t0 * fa, tb = sh.xch.t0 * fb;
+          z0 = crank == 0 ? za + zb : zb + za;  // rank order: the same bits in both CTAs
+          t0 = crank == 0 ? ta + tb : tb + ta;
+        }
+        g = gm;
+        if (!(g > -INFINITY)) {
+          // neither half starts with a finite value: the first CTA takes the
+          // row alone, from a fresh start (the copies under way land first)
+          if (!st_drain<DT>(sh, c0, c0, min(c1, c0 + st_nstages<DT>()), ph)) ok = false;
+          if (crank == 1) return;
+          joint = false;
+          c0 = 0;
+          c1 = r.nchunks;
+          --attempt;
+          continue;
+        }
+      }
+      if (!(G > -INFINITY) && g > -INFINITY) set_anchor(g);
+      if (topp && G > -INFINITY) {
+        wide = t0 < 0.8 * P * z0;
+        if (wide) set_hist_anchor(G);
+      }
+    }
+    // per chunk: the weights' total (anchored once a finite value is seen)
+    // and the unit's maximum (top-p) or weight sum (full softmax)
+    auto weigh = [&](const float *x, float cm, int u) {
+      vmax_t = st_maxn(vmax_t, cm);
+      if (!(G > -INFINITY)) {  // block-uniform: no finite value seen yet (never in a shared row)
+        const float g = st_bmaxf(sh, rf, cm, false, nullptr);
+        if (g > -INFINITY) set_anchor(g);
+      }
+      float part = 0.0f;
+      if (G > -INFINITY) {
+        ovf = ovf || cm > v_ovf;  // NaN never
+        const f2_t C = f2_pack(cw, cw), NA = f2_pack(-aw, -aw);
+        f2_t s2 = st_w2(f2_pack(x[0], x[1]), C, NA);
+#pragma unroll
+        for (int j = 1; j < 4; ++j) s2 = f2_add(s2, st_w2(f2_pack(x[2 * j], x[2 * j + 1]), C, NA));
+        float a0, a1;
+        f2_unpack(s2, a0, a1);
+        part = a0 + a1;
+        zl += (double)part;
+      }
+      if (topp) {
+        const float mu = st_warp_max(cm);
+        if (lane == 0) sh.w.n.m[u] = mu;
+      } else {
+        const float su = warp_sum_f(part);
+        if (lane == 0) sh.w.n.s[u] = su;
+      }
+    };
+    if (wide) {
+      ok = st_stream<DT, false>(
+               sh, r, c0, c1, pol1, ph,
+               [&](const float *x, int g0, int u, int) {
+                 const float cm = st_max8n(x);
+                 weigh(x, cm, u);
+                 hist8(x, g0, cm);
+               },
+               StNoAfter(), true) &&
+           ok;
+    } else {
+      ok = st_stream<DT, false>(
+               sh, r, c0, c1, pol1, ph, [&](const float *x, int, int u, int) { weigh(x, st_max8n(x), u); },
+               StNoAfter(), true) &&
+           ok;
+    }
+    bool anyovf = __syncthreads_or(ovf) != 0;
+    bool anybad;
+    float vm = st_bmaxf(sh, rf, vmax_t, st_bad(vmax_t) || !ok, &anybad);
+    double zs = st_bsum(sh, rf, zl);
+    if (joint) {  // both halves' flags, maxima, totals and high-list sizes
+      if (tid == 0) {
+        st_peer_u32(st_peer(&sh.xch.flags), (anybad ? 1u : 0u) | (anyovf ? 4u : 0u));
+        st_peer_f32(st_peer(&sh.xch.vmax), vm);
+        st_peer_f64(st_peer(&sh.xch.zsum), zs);
+        st_peer_u32(st_peer(&sh.xch.nhigh), (uint32_t)sh.nhigh);
+      }
+      st_cluster_sync();
+      const uint32_t pf = sh.xch.flags;
+      anybad = anybad || (pf & 1u) != 0u;
+      anyovf = anyovf || (pf & 4u) != 0u;
+      vm = fmaxf(vm, sh.xch.vmax);
+      zs = crank == 0 ? zs + sh.xch.zsum : sh.xch.zsum + zs;
+    }
+    vmax = vm;
+    if (anybad) {
+      if (tid == 0 && crank == 0) a.status[row] = kRowPending;
+      return;
+    }
+    if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
+      if (tid == 0 && crank == 0) write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
+      return;
+    }
+    if (!(fabs((double)vmax) * cl < 1e37) || (anyovf && attempt > 0)) {  // beyond fp32 range
+      if (tid == 0 && crank == 0) a.status[row] = kRowPending;
+      return;
+    }
+    if (anyovf) continue;
+    zsum = zs;
+    break;
+  }
+
+  if (!topp) {  // the draw over the unit sums (sampler.py:60-68)
+    double *kd = reinterpret_cast<double *>(st_scratch(sh, 1));
+    double zs = 0.0;
+    for (int u = tid; u < nu; u += kStThreads) {
+      kd[u] = (double)sh.w.n.s[u];
+      zs += kd[u];
+    }
+    const double total = st_bsum(sh, rf, zs);  // its barrier follows every kd write
+    st_draw_units<DT>(sh, rf, a, r, row, nu, kd, total, U, [&](float v, int) -> double { return (double)W(v); });
+    return;
+  }
+
+  // ============================================================ top-p only
+  // weights relative to the row maximum: rw(v) = W(v) * fG <= 1
+  const double fG = 1.0 / (double)W(vmax);
+  auto rw = [&](float v) -> double { return (double)W(v) * fG; };
+  const double total = zsum * fG;
+  const double pz = P * total;
+  uint32_t *gk = sh.w.n.x.g.key;
+  int *gi = sh.w.n.x.g.idx;
+  int n = 0;               // captured entries
+  bool narrow = false;     // the captured entries are every value at or above a bound below the nucleus
+  double above_tot = 0.0;  // wide: the mass above the bracket
+  bool tail_bracketed = false;  // wide: the bracket reaches the tail, so no cut keeps every token
+  int nhigh_all = sh.nhigh;  // high-list entries of both halves (rank 0: its list holds both)
+
+  // a shared row: the second half's unit maxima, histogram and high list go
+  // to the first CTA (its ring is idle: the histogram lands there)
+  if (joint) {
+    nhigh_all = crank == 0 ? sh.nhigh + sh.xch.nhigh : sh.xch.nhigh + sh.nhigh;
+    if (crank == 1) {
+      const uint32_t m_p = st_peer(sh.w.n.m);
+      for (int u = c0 * kStWarps + tid; u < c1 * kStWarps; u += kStThreads)
+        st_peer_f32(m_p + 4u * (uint32_t)u, sh.w.n.m[u]);
+      if (wide) {
+        const uint4 *h4 = reinterpret_cast<const uint4 *>(hq);
+        const uint32_t dst = st_peer(st_scratch(sh, 0));
+        for (int i = tid; i < kQSlots / 4; i += kStThreads) st_peer_v4(dst + 16u * (uint32_t)i, h4[i]);
+        const int n0h = sh.xch.nhigh, n1h = min(sh.nhigh, kHighCap);
+        const uint32_t hk_p = st_peer(sh.w.n.hkey), hi_p = st_peer(sh.w.n.hidx);
+        for (int i = tid; i < n1h && n0h + i < kHighCap; i += kStThreads) {
+          st_peer_u32(hk_p + 4u * (uint32_t)(n0h + i), sh.w.n.hkey[i]);
+          st_peer_u32(hi_p + 4u * (uint32_t)(n0h + i), (uint32_t)sh.w.n.hidx[i]);
+        }
+      }
+    }
+    st_cluster_sync();
+    if (crank == 0 && wide) {
+      const uint32_t *rcv = reinterpret_cast<const uint32_t *>(st_scratch(sh, 0));
+      for (int i = tid; i < kQSlots; i += kStThreads) hq[i] += rcv[i];
+      if (tid == 0) sh.nhigh = nhigh_all;
+      __syncthreads();
+    }
+  }
+
+  // the bracket [i_lo, i_hi] of histogram indices (-1 = the high list,
+  // kSBins + 1 = the tail) where the estimated running mass crosses
+  // P*total -/+ kHistTol*total, as values: above <=> v > v_lo; in the bracket
+  // <=> v_hi < v <= v_lo (t < bound <=> v > Gh - (bound - t_off) / xs).  The
+  // classifying pass is the arbiter: a value near a bin edge may land on
+  // either side of the histogram's split, which moves only the estimate; the
+  // exact checks below catch a bracket that misses the crossing.  First CTA
+  // (or a CTA alone).
+  float v_lo = INFINITY, v_hi = -INFINITY;
+  auto bracket = [&]() {
+    __syncthreads();
+    // the high list: exact weights
+    const int nh = min(sh.nhigh, kHighCap);
+    double hs = 0.0;
+    for (int i = tid; i < nh; i += kStThreads) hs += rw(key_to_float(sh.w.n.hkey[i]));
+    const double H = st_bsum(sh, rf, hs);
+    int i_lo, i_hi;
     constexpr int kPer = kQSlots / kStThreads;
-    const double rG = exp2(((double)G - (double)vmax) * cl);  // anchor weight / max weight
+    const double rG = exp2(((double)Gh - (double)vmax) * cl);  // anchor weight / max weight
     double mb[kPer];
     double s = 0.0;
     // bin i's weight e^-((i - 1 - kUpBins) dx) * rG / kQScale: one exp for the
@@ -1752,129 +2073,238 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     i_hi = H >= hi_t ? -1 : mhi;
     if (i_lo == 0x7FFFFFFF || i_lo > kSBins) i_lo = kSBins + 1;
     if (i_hi == 0x7FFFFFFF || i_hi > kSBins) i_hi = kSBins + 1;
-  }
-  // the bracket as values: above <=> v > v_lo; in the bracket <=> v_hi < v <= v_lo
-  // (t < bound <=> v > G - (bound - t_off) / xs).  Pass 2 is the arbiter: a
-  // value near a bin edge may land on either side of the histogram's split,
-  // which moves only the estimate; the exact checks below catch a bracket
-  // that misses the crossing.
-  auto t_to_v = [&](double tb) -> float { return (float)((double)G - (tb - (double)t_off) / (double)xs); };
-  const float v_lo = i_lo < 0 ? INFINITY : t_to_v((double)i_lo);
-  const float v_hi = i_hi < 0 ? t_to_v(1.0) : (i_hi > kSBins ? -INFINITY : t_to_v((double)(i_hi + 1)));
-  // pass 2 (L2): every weight once: per-unit mass above the bracket (into
-  // s_u), the exact total, and the bracket's elements
-  if (tid == 0) sh.ncand = 0;
-  __syncthreads();
-  bool gover = false;
-  double zacc = 0.0;
-  ok = st_pass<DT>(sh, r, pol_stream, ph, [&](const float *x, int g0, int u) {
-    const float mu = sh.w.n.m[u];
-    if (!(mu > -INFINITY)) {  // no finite value in the unit (warp-uniform)
-      if (lane == 0) sh.w.n.s[u] = 0.0f;
-      return;
+    auto t_to_v = [&](double tb) -> float { return (float)((double)Gh - (tb - (double)t_off) / (double)xs); };
+    v_lo = i_lo < 0 ? INFINITY : t_to_v((double)i_lo);
+    v_hi = i_hi < 0 ? t_to_v(1.0) : (i_hi > kSBins ? -INFINITY : t_to_v((double)(i_hi + 1)));
+    tail_bracketed = i_hi > kSBins;
+  };
+
+  // kind: 0 a narrow nucleus (the first CTA finishes it alone), 1 wide with
+  // the histogram of pass 1, 2 wide without a usable histogram
+  int kind = 2;
+  if (crank == 0) {
+    // the bracket from pass 1's histogram first: the narrow attempt's
+    // captures share its memory
+    if (wide && nhigh_all <= kHighCap) {
+      kind = 1;
+      bracket();
     }
-    StW Wu = W;
-    Wu.set_m(mu);
-    const StW2 W2(Wu);
-    const float fu = sh.w.n.f[u];
-    // the total: every lane adds its own weights (no warp reduction)
-    if (!(mu > v_hi)) {  // nothing above or in the bracket (warp-uniform): weights only
-      f2_t a2 = W2(f2_pack(x[0], x[1]));
-#pragma unroll
-      for (int j = 1; j < 4; ++j) a2 = f2_add(a2, W2(f2_pack(x[2 * j], x[2 * j + 1])));
-      float a0, a1;
-      f2_unpack(a2, a0, a1);
-      zacc += (double)(a0 + a1) * (double)fu;
-      if (lane == 0) sh.w.n.s[u] = 0.0f;
-      return;
+    // ---- a narrow nucleus: if the kNarrowUnits largest unit maxima, in
+    // (value desc) order, reach top_p of the total by the j-th one, every
+    // value at or above the j-th maximum holds at least that mass, so the
+    // nucleus (sampler.py:50-57) lies at or above it -- and only the units
+    // whose maximum reaches it hold such values
+    uint32_t *uk = reinterpret_cast<uint32_t *>(st_scratch(sh, 2));
+    for (int u = tid; u < nu; u += kStThreads) {
+      const float mu = sh.w.n.m[u];
+      uk[u] = mu > -INFINITY ? fkey(mu) : 0u;
     }
-    float all = 0.0f, above = 0.0f;
-    uint32_t inb = 0u;  // bit e: x[e] lies in the bracket
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float xa = x[2 * j], xb = x[2 * j + 1];
-      float wa, wb;
-      f2_unpack(W2(f2_pack(xa, xb)), wa, wb);  // -inf weighs 0
-      all += wa + wb;
-      const bool aa = xa > v_lo, ab = xb > v_lo;
-      above += (aa ? wa : 0.0f) + (ab ? wb : 0.0f);
-      inb |= ((uint32_t)(xa > v_hi) & (uint32_t)!aa) << (2 * j);
-      inb |= ((uint32_t)(xb > v_hi) & (uint32_t)!ab) << (2 * j + 1);
-    }
-    above = warp_sum_f(above);
-    zacc += (double)all * (double)fu;
-    if (lane == 0) sh.w.n.s[u] = above;
-    if (inb) {  // the lane's bracket entries: one atomic for all of them
-      int pos = atomicAdd(&sh.ncand, __popc(inb));
-      do {
-        const int e = __ffs(inb) - 1;
-        inb &= inb - 1;
-        if (pos < kSortCap) {
-          sh.w.n.x.g.key[pos] = fkey(st_pick8(x, e));
-          sh.w.n.x.g.idx[pos] = st_gidx(g0, e);
-        } else {
-          gover = true;
+    __syncthreads();
+    int above;
+    const uint32_t kth = st_select_kth(sh, uk, nu, min(kNarrowUnits, nu), &above, 2);
+    uint32_t *sk = reinterpret_cast<uint32_t *>(st_scratch(sh, 1) + 8192);
+    int *su = reinterpret_cast<int *>(st_scratch(sh, 1) + 8192 + 4 * 4 * kNarrowUnits);
+    int cnt = 0;
+    for (int u = tid; u < nu; u += kStThreads) cnt += (uk[u] >= kth && uk[u] != 0u) ? 1 : 0;
+    int ex, ng;
+    st_bscan_i(sh, rf, cnt, ex, ng);
+    if (ng <= 4 * kNarrowUnits) {  // block-uniform; more: ties in the leading bits, take the wide path
+      for (int u = tid; u < nu; u += kStThreads) {
+        if (uk[u] >= kth && uk[u] != 0u) {
+          sk[ex] = uk[u];
+          su[ex] = u;
+          ++ex;
         }
-        ++pos;
-      } while (inb);
+      }
+      __syncthreads();
+      st_rank_sort(sh, sk, su, ng, false);  // (maximum desc, unit asc); thread i holds entry i below
+      const double wm = tid < ng ? rw(key_to_float(sk[tid])) : 0.0;
+      double wex, winc, wtot;
+      st_bscan(sh, rf, wm, wex, winc, wtot);
+      const int first = st_bmin(sh, rf, (tid < ng && winc >= pz) ? tid : 0x7FFFFFFF);
+      if (first != 0x7FFFFFFF) {
+        const uint32_t kb = sk[first];
+        const float vb = key_to_float(kb);
+        const int nvis = st_bmin(sh, rf, (tid < ng && sk[tid] < kb) ? tid : ng);  // the units reaching vb
+        if (tid == 0) sh.ncand = 0;
+        __syncthreads();
+        bool gover = false;
+        for (int i = tid >> 5; i < nvis; i += kStWarps) {
+          float x[8];
+          const int g0 = st_load_unit<DT>(r, su[i], x);
+          unsigned m = 0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) m |= (x[e] >= vb ? 1u : 0u) << e;
+          if (m) {  // the lane's entries: one atomic for all of them
+            int pos = atomicAdd(&sh.ncand, __popc(m));
+            do {
+              const int e = __ffs(m) - 1;
+              m &= m - 1;
+              if (pos < kSortCap) {
+                gk[pos] = fkey(st_pick8(x, e));
+                gi[pos] = st_gidx(g0, e);
+              } else {
+                gover = true;
+              }
+              ++pos;
+            } while (m);
+          }
+        }
+        if (!__syncthreads_or(gover)) {
+          narrow = true;
+          n = sh.ncand;
+        }
+      }
     }
-  });
-  int n = sh.ncand;  // st_pass ended with a barrier
-  const bool failc = __syncthreads_or(!ok || gover) != 0;  // a crowded bracket: generic kernel
-  double zpeer = 0.0;
-  if (joint) {
-    if (tid == 0) {
-      st_peer_u32(st_peer(&sh.xch.j4_n), (uint32_t)n);
-      st_peer_u32(st_peer(&sh.xch.j4_flags), failc ? 1u : 0u);
+    if (narrow) kind = 0;
+  }
+  if (joint) {  // the first CTA's decision
+    if (crank == 0 && tid == 0) {
+      st_peer_u32(st_peer(&sh.xch.kind), (uint32_t)kind);
+      st_peer_f32(st_peer(&sh.xch.v_lo), v_lo);
+      st_peer_f32(st_peer(&sh.xch.v_hi), v_hi);
     }
     st_cluster_sync();
-    const int np = sh.xch.j4_n;
-    if (failc || sh.xch.j4_flags != 0u || n + np > kSortCap) {  // both CTAs stop here
-      if (crank == 0 && tid == 0) a.status[row] = kRowPending;
-      return;
-    }
     if (crank == 1) {
-      // hand the second half to the first CTA: its bracket entries after the
-      // first CTA's, its units' maxima, scales and masses above the bracket,
-      // and its share of the total
-      const double zc = st_bsum(sh, rf, zacc);
-      const uint32_t gk_p = st_peer(sh.w.n.x.g.key), gi_p = st_peer(sh.w.n.x.g.idx);
-      for (int i = tid; i < n; i += kStThreads) {
-        st_peer_u32(gk_p + 4u * (uint32_t)(np + i), sh.w.n.x.g.key[i]);
-        st_peer_u32(gi_p + 4u * (uint32_t)(np + i), (uint32_t)sh.w.n.x.g.idx[i]);
+      kind = (int)sh.xch.kind;
+      v_lo = sh.xch.v_lo;
+      v_hi = sh.xch.v_hi;
+    }
+    if (kind == 0 && crank == 1) return;
+  }
+
+  if (!narrow) {
+    // ---- a wide nucleus
+    if (kind == 2) {
+      // no histogram from pass 1 (a narrow nucleus was predicted), or many
+      // values lie far above its anchor: a histogram pass (L2) anchored at
+      // the row maximum, nothing above it
+      __syncthreads();
+      set_hist_anchor(vmax);
+      hist_clear();
+      __syncthreads();
+      ok = st_stream<DT, false>(
+          sh, r, c0, c1, pol_keep, ph, [&](const float *x, int g0, int, int) { hist8(x, g0, st_max8n(x)); },
+          StNoAfter());
+      if (joint) {  // the second half's histogram and copy status to the first CTA
+        // first both passes end: the histogram lands in the first CTA's
+        // stage ring, idle only then
+        if (tid == 0) st_peer_u32(st_peer(&sh.xch.flags), ok ? 0u : 2u);
+        st_cluster_sync();
+        if (crank == 1) {
+          const uint4 *h4 = reinterpret_cast<const uint4 *>(hq);
+          const uint32_t dst = st_peer(st_scratch(sh, 0));
+          for (int i = tid; i < kQSlots / 4; i += kStThreads) st_peer_v4(dst + 16u * (uint32_t)i, h4[i]);
+        }
+        st_cluster_sync();
+        ok = ok && sh.xch.flags == 0u;
+        if (crank == 0 && ok) {
+          const uint32_t *rcv = reinterpret_cast<const uint32_t *>(st_scratch(sh, 0));
+          for (int i = tid; i < kQSlots; i += kStThreads) hq[i] += rcv[i];
+        }
       }
-      const uint32_t m_p = st_peer(sh.w.n.m), s_p = st_peer(sh.w.n.s), f_p = st_peer(sh.w.n.f);
-      for (int u = r.cb * kStWarps + tid; u < r.ce * kStWarps; u += kStThreads) {
-        st_peer_f32(m_p + 4u * (uint32_t)u, sh.w.n.m[u]);
-        st_peer_f32(s_p + 4u * (uint32_t)u, sh.w.n.s[u]);
-        st_peer_f32(f_p + 4u * (uint32_t)u, sh.w.n.f[u]);
+      if (!ok) {
+        if (tid == 0 && crank == 0) a.status[row] = kRowPending;
+        return;
       }
-      if (tid == 0) st_peer_f64(st_peer(&sh.xch.j5_z), zc);
+      if (crank == 0) bracket();
+      if (joint) {
+        if (crank == 0 && tid == 0) {
+          st_peer_f32(st_peer(&sh.xch.v_lo), v_lo);
+          st_peer_f32(st_peer(&sh.xch.v_hi), v_hi);
+        }
+        st_cluster_sync();
+        if (crank == 1) {
+          v_lo = sh.xch.v_lo;
+          v_hi = sh.xch.v_hi;
+        }
+      }
+    }
+    // classifying pass (L2): this CTA's units reaching the bracket: per-unit
+    // mass above it (into s_u) and the bracket's elements
+    if (tid == 0) sh.ncand = 0;
+    __syncthreads();
+    bool gover = false;
+    ok = st_stream<DT, false>(
+        sh, r, c0, c1, pol_stream, ph,
+        [&](const float *x, int g0, int u, int) {
+          if (!(sh.w.n.m[u] > v_hi)) {  // nothing above or in the bracket (warp-uniform)
+            if (lane == 0) sh.w.n.s[u] = 0.0f;
+            return;
+          }
+          float above = 0.0f;
+          uint32_t inb = 0u;  // bit e: x[e] lies in the bracket
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float xa = x[2 * j], xb = x[2 * j + 1];
+            const bool aa = xa > v_lo, ab = xb > v_lo;
+            above += (aa ? W(xa) : 0.0f) + (ab ? W(xb) : 0.0f);
+            inb |= ((uint32_t)(xa > v_hi) & (uint32_t)!aa) << (2 * j);
+            inb |= ((uint32_t)(xb > v_hi) & (uint32_t)!ab) << (2 * j + 1);
+          }
+          above = warp_sum_f(above);
+          if (lane == 0) sh.w.n.s[u] = above;
+          if (inb) {  // the lane's bracket entries: one atomic for all of them
+            int pos = atomicAdd(&sh.ncand, __popc(inb));
+            do {
+              const int e = __ffs(inb) - 1;
+              inb &= inb - 1;
+              if (pos < kSortCap) {
+                gk[pos] = fkey(st_pick8(x, e));
+                gi[pos] = st_gidx(g0, e);
+              } else {
+                gover = true;
+              }
+              ++pos;
+            } while (inb);
+          }
+        },
+        StNoAfter());
+    n = sh.ncand;  // st_stream ended with a barrier
+    bool fail = __syncthreads_or(!ok || gover) != 0;  // a crowded bracket: generic kernel
+    if (joint) {
+      // entry counts and failures of both halves; then the second half's
+      // entries (after the first's), and its units' masses, to the first CTA
+      if (tid == 0) {
+        st_peer_u32(st_peer(&sh.xch.ncand), (uint32_t)n);
+        st_peer_u32(st_peer(&sh.xch.flags), fail ? 8u : 0u);
+      }
       st_cluster_sync();
+      const int np_ = (int)sh.xch.ncand;
+      fail = fail || sh.xch.flags != 0u || n + np_ > kSortCap;
+      if (fail) {  // both CTAs stop here
+        if (tid == 0 && crank == 0) a.status[row] = kRowPending;
+        return;
+      }
+      if (crank == 1) {
+        const uint32_t gk_p = st_peer(gk), gi_p = st_peer(gi);
+        for (int i = tid; i < n; i += kStThreads) {
+          st_peer_u32(gk_p + 4u * (uint32_t)(np_ + i), gk[i]);
+          st_peer_u32(gi_p + 4u * (uint32_t)(np_ + i), (uint32_t)gi[i]);
+        }
+        const uint32_t s_p = st_peer(sh.w.n.s);
+        for (int u = c0 * kStWarps + tid; u < c1 * kStWarps; u += kStThreads)
+          st_peer_f32(s_p + 4u * (uint32_t)u, sh.w.n.s[u]);
+      }
+      st_cluster_sync();
+      if (crank == 1) return;
+      n += np_;
+    } else if (fail) {
+      if (tid == 0) a.status[row] = kRowPending;
       return;
     }
-    st_cluster_sync();
-    n += np;
-    zpeer = sh.xch.j5_z;
-  } else if (failc) {
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
+    double as = 0.0;
+    for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u];
+    above_tot = st_bsum(sh, rf, as) * fG;
+    if (above_tot > 0.0 && above_tot >= pz) {  // the crossing lies above the bracket
+      if (tid == 0) a.status[row] = kRowPending;
+      return;
+    }
   }
-  double as = 0.0;
-  for (int u = tid; u < nu; u += kStThreads) as += (double)sh.w.n.s[u] * (double)sh.w.n.f[u];
-  double total, above_tot;
-  st_bsum2(sh, rf, zacc, as, total, above_tot);
-  total += zpeer;  // the second half's share, when the row was shared
-  const double pz = P * total;
-  if (above_tot > 0.0 && above_tot >= pz) {  // the crossing lies above the bracket
-    if (tid == 0) a.status[row] = kRowPending;
-    return;
-  }
-  uint32_t *gk = sh.w.n.x.g.key;
-  int *gi = sh.w.n.x.g.idx;
-  // The cut: the first bracket entry in (value desc, index asc) order whose
+
+  // The cut: the first captured entry in (value desc, index asc) order whose
   // running mass, after above_tot, reaches P*total (miniserve/sampler.py:50-57)
-  // -- (ck, ci); or none, when the bracket's mass falls short.
+  // -- (ck, ci); or none, when the captured mass falls short.
   const double need = pz - above_tot;
   // the first of m sorted entries whose running mass from `base` reaches
   // need, or 0x7FFFFFFF
@@ -1882,14 +2312,14 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const int per = (m + kStThreads - 1) / kStThreads;
     const int p0 = tid * per, p1 = min(m, p0 + per);
     double sw = 0.0;
-    for (int i = p0; i < p1; ++i) sw += unit_w(key_to_float(sk[i]), si[i]);
+    for (int i = p0; i < p1; ++i) sw += rw(key_to_float(sk[i]));
     double ex, inc, tt;
     st_bscan(sh, rf, sw, ex, inc, tt);
     int cand = 0x7FFFFFFF;
     if (p0 < p1 && base + inc >= need) {
       double acc = base + ex;
       for (int i = p0; i < p1; ++i) {
-        acc += unit_w(key_to_float(sk[i]), si[i]);
+        acc += rw(key_to_float(sk[i]));
         if (acc >= need) {
           cand = i;
           break;
@@ -1903,7 +2333,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   int ci = 0x7FFFFFFF;
   int state = 2;  // 0: the cut found, 1: none, 2: not resolved yet
   if (n > kRankCap / 4) {
-    // A large bracket: 256 key buckets with fixed-point masses place the
+    // A large set: 256 key buckets with fixed-point masses place the
     // crossing within a window of buckets, and only the window is sorted.
     // Bucket b holds keys kmin + [b << bsh, (b + 1) << bsh).
     int lo_i = 0x7FFFFFFF, hi_i = 0x7FFFFFFF;
@@ -1917,12 +2347,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // w * qs < 2^18 for every entry: qs from the top key's weight, with a
     // margin far above the weights' rounding
     const double qs = 262144.0 / (exp2(((double)key_to_float(kmax) - (double)vmax) * cl) * 1.001);
-    uint32_t *bcnt = reinterpret_cast<uint32_t *>(sh.stage[0]);  // [256] entries, [256] mass
+    uint32_t *bcnt = reinterpret_cast<uint32_t *>(st_scratch(sh, 0));  // [256] entries, [256] mass
     for (int q = tid; q < 512; q += kStThreads) bcnt[q] = 0u;
     __syncthreads();
     for (int i = tid; i < n; i += kStThreads) {
       const int bk = (int)((gk[i] - kmin) >> bsh);
-      const double w = unit_w(key_to_float(gk[i]), gi[i]);
+      const double w = rw(key_to_float(gk[i]));
       atomicAdd(&bcnt[bk], 1u);
       atomicAdd(&bcnt[256 + bk], (uint32_t)fmin(w * qs, 524288.0));  // floor: w*qs - 1 < q <= w*qs
     }
@@ -1932,7 +2362,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // crossing bucket b* (highest b whose exact mass reaches need) satisfies
     // b_lo <= b* <= b_hi with b_lo = highest b with C(b) >= T and b_hi =
     // highest b with C(b) + N(b) >= T.
-    const double T = need * qs;
+    const double Tq = need * qs;
     uint32_t cq[8], cn[8], sq = 0, sn = 0;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -1957,13 +2387,13 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     for (int q = 0; q < 8; ++q) {
       cacc += (double)cq[q];
       nacc += (double)cn[q];
-      if (blo < 0 && cacc >= T) blo = 255 - 8 * lane - q;
-      if (bhi < 0 && cacc + nacc >= T) bhi = 255 - 8 * lane - q;
+      if (blo < 0 && cacc >= Tq) blo = 255 - 8 * lane - q;
+      if (bhi < 0 && cacc + nacc >= Tq) bhi = 255 - 8 * lane - q;
     }
     blo = __reduce_max_sync(0xFFFFFFFFu, blo);  // highest bucket: lowest lane's first hit
     bhi = __reduce_max_sync(0xFFFFFFFFu, bhi);
     if (bhi < 0) {
-      state = 1;  // even the largest possible bracket mass falls short of need
+      state = 1;  // even the largest possible captured mass falls short of need
     } else {
       const int wlo = max(blo, 0);
       // exact mass above the window, and the window's entries gathered
@@ -1971,15 +2401,15 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       int wc = 0;
       for (int i = tid; i < n; i += kStThreads) {
         const int bk = (int)((gk[i] - kmin) >> bsh);
-        if (bk > bhi) am += unit_w(key_to_float(gk[i]), gi[i]);
+        if (bk > bhi) am += rw(key_to_float(gk[i]));
         else if (bk >= wlo) ++wc;
       }
       const double A = st_bsum(sh, rf, am);
       int wex, m;
       st_bscan_i(sh, rf, wc, wex, m);
       if (A < need && m <= kRankCap) {  // otherwise the buckets misled: sort everything
-        uint32_t *wk = reinterpret_cast<uint32_t *>(sh.stage[1] + 8192);
-        int *wi = reinterpret_cast<int *>(sh.stage[1] + 12288);
+        uint32_t *wk = reinterpret_cast<uint32_t *>(st_scratch(sh, 1) + 8192);
+        int *wi = reinterpret_cast<int *>(st_scratch(sh, 1) + 12288);
         for (int i = tid; i < n; i += kStThreads) {
           const int bk = (int)((gk[i] - kmin) >> bsh);
           if (bk <= bhi && bk >= wlo) {
@@ -1996,12 +2426,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
           ci = wi[pc];
           state = 0;
         } else if (blo < 0) {
-          state = 1;  // the window reaches the bracket's bottom: its mass falls short
+          state = 1;  // the window reaches the captured set's bottom: its mass falls short
         }
       }
     }
   }
-  if (state == 2) {  // a small bracket, or the buckets misled: sort it all
+  if (state == 2) {  // a small set, or the buckets misled: sort it all
     if (n <= kRankCap) {
       st_rank_sort(sh, gk, gi, n, false);
     } else {
@@ -2016,35 +2446,37 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       state = 1;
     }
   }
-  if (state == 1 && i_hi <= kSBins) {  // the crossing lies below the bracket
+  // no cut: with the tail bracketed the running sum never reaches top_p and
+  // every token is kept; otherwise the crossing lies below the captured set
+  // (for a narrow nucleus only through rounding at the bound)
+  if (state == 1 && !tail_bracketed) {
     if (tid == 0) a.status[row] = kRowPending;
     return;
   }
-  // no cut with the tail bracketed: the running sum never reaches top_p, every
-  // token is kept
   const float vc = state == 1 ? -INFINITY : key_to_float(ck);
   const int ic = state == 1 ? 0x7FFFFFFF : ci;
-  // kept mass per unit: above the bracket (s_u) plus the unit's kept bracket
-  // entries, those summed as 2^-50 fixed point (exact and order-free)
-  unsigned long long *ex64 = reinterpret_cast<unsigned long long *>(sh.stage[2]);
+  // kept mass per unit: above the bracket (wide: s_u) plus the unit's kept
+  // captured entries, those summed as 2^-50 fixed point (exact and order-free)
+  unsigned long long *ex64 = reinterpret_cast<unsigned long long *>(st_scratch(sh, 2));
   for (int u = tid; u < nu; u += kStThreads) ex64[u] = 0ull;
   __syncthreads();
   for (int i = tid; i < n; i += kStThreads) {
     if (state == 1 || gk[i] > ck || (gk[i] == ck && gi[i] <= ci)) {  // at or before the cut
-      const double w = unit_w(key_to_float(gk[i]), gi[i]);  // <= 1
+      const double w = rw(key_to_float(gk[i]));  // <= 1
       atomicAdd(&ex64[gi[i] / kUnit], (unsigned long long)(w * 0x1p50));
     }
   }
   __syncthreads();
+  double *kd = reinterpret_cast<double *>(st_scratch(sh, 1));
   double tk = 0.0;
   for (int u = tid; u < nu; u += kStThreads) {
-    kd[u] = (double)sh.w.n.s[u] * (double)sh.w.n.f[u] + (double)ex64[u] * 0x1p-50;
+    kd[u] = (narrow ? 0.0 : (double)sh.w.n.s[u] * fG) + (double)ex64[u] * 0x1p-50;
     tk += kd[u];
   }
   const double tot_keep = st_bsum(sh, rf, tk);
   st_draw_units<DT>(sh, rf, a, r, row, nu, kd, tot_keep, U, [&](float v, int g) -> double {
     if (!(v > -INFINITY) || !(v > vc || (v == vc && g <= ic))) return 0.0;
-    return unit_w(v, g);
+    return rw(v);
   });
 }
 }  // namespace ms
