@@ -78,7 +78,7 @@ __device__ __forceinline__ void write_row(const SampleArgs &a, int r, int64_t to
 // MASS:  weight exp(x - max) (top-p in exp units, miniserve/sampler.py:50-57).
 // Returns the cut describing that prefix; `base` itself when thr is never
 // reached (the reference then keeps everything it iterated over).
-template <int DT, bool MASS>
+template <int DT, bool MASS, int NT = kGenThreads>
 __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dmax, double inv_t,
                           GenShared &sh) {
   const int tid = threadIdx.x;
@@ -92,12 +92,12 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
     const int bits = level == 2 ? 10 : 11;
     const int nb = 1 << bits;
     const uint32_t dmask = (uint32_t)nb - 1u;
-    for (int b = tid; b < kBins; b += kGenThreads) {
+    for (int b = tid; b < kBins; b += NT) {
       sh.cnt[b] = 0u;
       sh.mass[b] = 0.0;
     }
     __syncthreads();
-    for (int i = tid; i < V; i += kGenThreads) {
+    for (int i = tid; i < V; i += NT) {
       uint32_t key = row.key(i);
       if (key <= kNegInfKey || !kept(base, key, i)) continue;
       if (level > 0 && (key >> (sh_ + bits)) != prefix) continue;
@@ -106,15 +106,15 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
       if (MASS) atomicAdd(&sh.mass[d], weight_of(key_to_float(key), dmax, inv_t));
     }
     __syncthreads();
-    // positions run from the highest digit down; each thread owns nb/1024
-    const int per = nb / kGenThreads;  // 2 or 1
+    // positions run from the highest digit down; each thread owns nb/NT
+    const int per = nb / NT;  // 1, 2 or 4
     double s = 0.0;
     for (int j = 0; j < per; ++j) {
       int d = nb - 1 - (tid * per + j);
       s += MASS ? sh.mass[d] : (double)sh.cnt[d];
     }
     double excl, incl, tot;
-    block_scan<kGenThreads, double>(s, excl, incl, tot, sh.redd);
+    block_scan<NT, double>(s, excl, incl, tot, sh.redd);
     const double rel = thr - above_w;
     int cand = 0x7FFFFFFF;
     double acc = excl, before = 0.0;
@@ -129,7 +129,7 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
         break;
       }
     }
-    int pos = block_min_i<kGenThreads>(cand, sh.redi);
+    int pos = block_min_i<NT>(cand, sh.redi);
     if (pos == 0x7FFFFFFF) return base;  // never reached: keep the whole base set
     if (cand == pos) {
       sh.bcast_d[0] = before;
@@ -155,7 +155,7 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
   if ((uint32_t)need >= last_cnt) return Cut{tau, base_cut};
   // find the index of the need-th tie in index order
   int running = 0;
-  for (int t0 = 0; t0 < V; t0 += kTile) {
+  for (int t0 = 0; t0 < V; t0 += (NT * kItems)) {
     int c = 0;
     const int i0 = t0 + tid * kItems;
 #pragma unroll
@@ -167,7 +167,7 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
       }
     }
     int excl_i, incl_i, tot_i;
-    block_scan<kGenThreads, int>(c, excl_i, incl_i, tot_i, sh.redi);
+    block_scan<NT, int>(c, excl_i, incl_i, tot_i, sh.redi);
     if (running + tot_i >= need) {
       if (running + excl_i < need && need <= running + incl_i) {
         int acc2 = running + excl_i;
@@ -191,19 +191,19 @@ __device__ Cut gen_select(const RowRef<DT> &row, Cut base, double thr, double dm
   return Cut{tau, base_cut};  // unreachable when counts are consistent
 }
 
-template <int DT>
+template <int DT, int NT = kGenThreads>
 __device__ double gen_total(const RowRef<DT> &row, Cut c, double dmax, double inv_t, GenShared &sh) {
   double s = 0.0;
-  for (int i = threadIdx.x; i < row.V; i += kGenThreads) {
+  for (int i = threadIdx.x; i < row.V; i += NT) {
     uint32_t key = row.key(i);
     if (key > kNegInfKey && kept(c, key, i)) s += weight_of(key_to_float(key), dmax, inv_t);
   }
-  return block_sum<kGenThreads>(s, sh.redd);
+  return block_sum<NT>(s, sh.redd);
 }
 
 // Index-order inverse CDF over the kept set (miniserve/sampler.py:62-68):
 // the first index whose running weight reaches u * total; V-1 when none does.
-template <int DT>
+template <int DT, int NT = kGenThreads>
 __device__ void gen_draw(const RowRef<DT> &row, Cut c, double total, double u, double dmax,
                          double inv_t, const SampleArgs &a, int r, uint32_t flags, GenShared &sh) {
   const int tid = threadIdx.x;
@@ -218,7 +218,7 @@ __device__ void gen_draw(const RowRef<DT> &row, Cut c, double total, double u, d
   }
   const double target = u * total;
   double running = 0.0;
-  for (int t0 = 0; t0 < V; t0 += kTile) {
+  for (int t0 = 0; t0 < V; t0 += (NT * kItems)) {
     double w[kItems];
     double s = 0.0;
     const int i0 = t0 + tid * kItems;
@@ -229,9 +229,9 @@ __device__ void gen_draw(const RowRef<DT> &row, Cut c, double total, double u, d
       s += w[j];
     }
     double excl, incl, tot;
-    block_scan<kGenThreads, double>(s, excl, incl, tot, sh.redd);
+    block_scan<NT, double>(s, excl, incl, tot, sh.redd);
     int cand = (s > 0.0 && running + incl >= target) ? tid : 0x7FFFFFFF;
-    int who = block_min_i<kGenThreads>(cand, sh.redi);
+    int who = block_min_i<NT>(cand, sh.redi);
     if (who != 0x7FFFFFFF) {
       if (tid == who) {
         double cum = running + excl;
@@ -262,7 +262,7 @@ __device__ void gen_draw(const RowRef<DT> &row, Cut c, double total, double u, d
   if (tid == 0) write_row(a, r, V - 1, (float)(wt(V - 1) / total), (int32_t)flags);
 }
 
-template <int DT>
+template <int DT, int NT = kGenThreads>
 __device__ void gen_row(const SampleArgs &a, int r, GenShared &sh) {
   const int tid = threadIdx.x;
   RowRef<DT> row;
@@ -274,7 +274,7 @@ __device__ void gen_row(const SampleArgs &a, int r, GenShared &sh) {
   // ---- pass 1: max (first index on ties), valid count, non-finite flags
   uint32_t flags = 0, bk = 0u, nvalid = 0;
   int bi = 0x7FFFFFFF;
-  for (int i = tid; i < a.V; i += kGenThreads) {
+  for (int i = tid; i < a.V; i += NT) {
     uint32_t u = clean_bits(raw_bits<DT>(row.row, i), mask_allows(row.mask_row, i), flags);
     uint32_t key = bits_to_key(u);
     if (key > bk) {
@@ -292,10 +292,11 @@ __device__ void gen_row(const SampleArgs &a, int r, GenShared &sh) {
     sh.redu[tid >> 5] = flags;
   }
   __syncthreads();
-  if (tid < 32) {
-    uint32_t k2 = sh.bkey[tid];
-    int i2 = sh.bidx[tid];
-    uint32_t f2 = sh.redu[tid];
+  if (tid < 32) {  // one slot per warp: NT / 32 of them hold values
+    constexpr int NW = NT / 32;
+    uint32_t k2 = tid < NW ? sh.bkey[tid] : 0u;
+    int i2 = tid < NW ? sh.bidx[tid] : 0x7FFFFFFF;
+    uint32_t f2 = tid < NW ? sh.redu[tid] : 0u;
     warp_argmax(k2, i2);
     f2 = __reduce_or_sync(0xFFFFFFFFu, f2);
     if (tid == 0) {
@@ -309,7 +310,7 @@ __device__ void gen_row(const SampleArgs &a, int r, GenShared &sh) {
   const int max_idx = sh.bidx[0];
   flags = (uint32_t)sh.bcast_i[2];
   __syncthreads();
-  nvalid = block_sum_u32<kGenThreads>(nvalid, sh.redu);
+  nvalid = block_sum_u32<NT>(nvalid, sh.redu);
 
   const double T = a.temperature[r];
   const int k = a.top_k[r];
@@ -346,13 +347,13 @@ __device__ void gen_row(const SampleArgs &a, int r, GenShared &sh) {
   const double dmax = (double)key_to_float(max_key);
   const double inv_t = 1.0 / T;
   Cut c = cut_all();
-  if (keff > 1) c = gen_select<DT, false>(row, c, (double)keff, dmax, inv_t, sh);
-  double total = gen_total<DT>(row, c, dmax, inv_t, sh);
+  if (keff > 1) c = gen_select<DT, false, NT>(row, c, (double)keff, dmax, inv_t, sh);
+  double total = gen_total<DT, NT>(row, c, dmax, inv_t, sh);
   if (p < 1.0) {
-    c = gen_select<DT, true>(row, c, p * total, dmax, inv_t, sh);
-    total = gen_total<DT>(row, c, dmax, inv_t, sh);
+    c = gen_select<DT, true, NT>(row, c, p * total, dmax, inv_t, sh);
+    total = gen_total<DT, NT>(row, c, dmax, inv_t, sh);
   }
-  gen_draw<DT>(row, c, total, u, dmax, inv_t, a, r, flags, sh);
+  gen_draw<DT, NT>(row, c, total, u, dmax, inv_t, a, r, flags, sh);
 }
 
 // rows: optional device list of row indices with its device count; when null

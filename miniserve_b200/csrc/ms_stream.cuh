@@ -2089,70 +2089,73 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       kind = 1;
       bracket();
     }
-    // ---- a narrow nucleus: if the kNarrowUnits largest unit maxima, in
-    // (value desc) order, reach top_p of the total by the j-th one, every
-    // value at or above the j-th maximum holds at least that mass, so the
-    // nucleus (sampler.py:50-57) lies at or above it -- and only the units
-    // whose maximum reaches it hold such values
-    uint32_t *uk = reinterpret_cast<uint32_t *>(st_scratch(sh, 2));
-    for (int u = tid; u < nu; u += kStThreads) {
-      const float mu = sh.w.n.m[u];
-      uk[u] = mu > -INFINITY ? fkey(mu) : 0u;
-    }
-    __syncthreads();
-    int above;
-    const uint32_t kth = st_select_kth(sh, uk, nu, min(kNarrowUnits, nu), &above, 2);
-    uint32_t *sk = reinterpret_cast<uint32_t *>(st_scratch(sh, 1) + 8192);
-    int *su = reinterpret_cast<int *>(st_scratch(sh, 1) + 8192 + 4 * 4 * kNarrowUnits);
-    int cnt = 0;
-    for (int u = tid; u < nu; u += kStThreads) cnt += (uk[u] >= kth && uk[u] != 0u) ? 1 : 0;
-    int ex, ng;
-    st_bscan_i(sh, rf, cnt, ex, ng);
-    if (ng <= 4 * kNarrowUnits) {  // block-uniform; more: ties in the leading bits, take the wide path
+    // (skipped when pass 1 built the histogram: a wide nucleus was predicted)
+    if (kind != 1) {
+      // ---- a narrow nucleus: if the kNarrowUnits largest unit maxima, in
+      // (value desc) order, reach top_p of the total by the j-th one, every
+      // value at or above the j-th maximum holds at least that mass, so the
+      // nucleus (sampler.py:50-57) lies at or above it -- and only the units
+      // whose maximum reaches it hold such values
+      uint32_t *uk = reinterpret_cast<uint32_t *>(st_scratch(sh, 2));
       for (int u = tid; u < nu; u += kStThreads) {
-        if (uk[u] >= kth && uk[u] != 0u) {
-          sk[ex] = uk[u];
-          su[ex] = u;
-          ++ex;
-        }
+        const float mu = sh.w.n.m[u];
+        uk[u] = mu > -INFINITY ? fkey(mu) : 0u;
       }
       __syncthreads();
-      st_rank_sort(sh, sk, su, ng, false);  // (maximum desc, unit asc); thread i holds entry i below
-      const double wm = tid < ng ? rw(key_to_float(sk[tid])) : 0.0;
-      double wex, winc, wtot;
-      st_bscan(sh, rf, wm, wex, winc, wtot);
-      const int first = st_bmin(sh, rf, (tid < ng && winc >= pz) ? tid : 0x7FFFFFFF);
-      if (first != 0x7FFFFFFF) {
-        const uint32_t kb = sk[first];
-        const float vb = key_to_float(kb);
-        const int nvis = st_bmin(sh, rf, (tid < ng && sk[tid] < kb) ? tid : ng);  // the units reaching vb
-        if (tid == 0) sh.ncand = 0;
-        __syncthreads();
-        bool gover = false;
-        for (int i = tid >> 5; i < nvis; i += kStWarps) {
-          float x[8];
-          const int g0 = st_load_unit<DT>(r, su[i], x);
-          unsigned m = 0;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) m |= (x[e] >= vb ? 1u : 0u) << e;
-          if (m) {  // the lane's entries: one atomic for all of them
-            int pos = atomicAdd(&sh.ncand, __popc(m));
-            do {
-              const int e = __ffs(m) - 1;
-              m &= m - 1;
-              if (pos < kSortCap) {
-                gk[pos] = fkey(st_pick8(x, e));
-                gi[pos] = st_gidx(g0, e);
-              } else {
-                gover = true;
-              }
-              ++pos;
-            } while (m);
+      int above;
+      const uint32_t kth = st_select_kth(sh, uk, nu, min(kNarrowUnits, nu), &above, 2);
+      uint32_t *sk = reinterpret_cast<uint32_t *>(st_scratch(sh, 1) + 8192);
+      int *su = reinterpret_cast<int *>(st_scratch(sh, 1) + 8192 + 4 * 4 * kNarrowUnits);
+      int cnt = 0;
+      for (int u = tid; u < nu; u += kStThreads) cnt += (uk[u] >= kth && uk[u] != 0u) ? 1 : 0;
+      int ex, ng;
+      st_bscan_i(sh, rf, cnt, ex, ng);
+      if (ng <= 4 * kNarrowUnits) {  // block-uniform; more: ties in the leading bits, take the wide path
+        for (int u = tid; u < nu; u += kStThreads) {
+          if (uk[u] >= kth && uk[u] != 0u) {
+            sk[ex] = uk[u];
+            su[ex] = u;
+            ++ex;
           }
         }
-        if (!__syncthreads_or(gover)) {
-          narrow = true;
-          n = sh.ncand;
+        __syncthreads();
+        st_rank_sort(sh, sk, su, ng, false);  // (maximum desc, unit asc); thread i holds entry i below
+        const double wm = tid < ng ? rw(key_to_float(sk[tid])) : 0.0;
+        double wex, winc, wtot;
+        st_bscan(sh, rf, wm, wex, winc, wtot);
+        const int first = st_bmin(sh, rf, (tid < ng && winc >= pz) ? tid : 0x7FFFFFFF);
+        if (first != 0x7FFFFFFF) {
+          const uint32_t kb = sk[first];
+          const float vb = key_to_float(kb);
+          const int nvis = st_bmin(sh, rf, (tid < ng && sk[tid] < kb) ? tid : ng);  // the units reaching vb
+          if (tid == 0) sh.ncand = 0;
+          __syncthreads();
+          bool gover = false;
+          for (int i = tid >> 5; i < nvis; i += kStWarps) {
+            float x[8];
+            const int g0 = st_load_unit<DT>(r, su[i], x);
+            unsigned m = 0;
+  #pragma unroll
+            for (int e = 0; e < 8; ++e) m |= (x[e] >= vb ? 1u : 0u) << e;
+            if (m) {  // the lane's entries: one atomic for all of them
+              int pos = atomicAdd(&sh.ncand, __popc(m));
+              do {
+                const int e = __ffs(m) - 1;
+                m &= m - 1;
+                if (pos < kSortCap) {
+                  gk[pos] = fkey(st_pick8(x, e));
+                  gi[pos] = st_gidx(g0, e);
+                } else {
+                  gover = true;
+                }
+                ++pos;
+              } while (m);
+            }
+          }
+          if (!__syncthreads_or(gover)) {
+            narrow = true;
+            n = sh.ncand;
+          }
         }
       }
     }

@@ -52,6 +52,39 @@ def _param(x, B: int, dtype, device):
     return t.to(device)
 
 
+def check_mask(mask, B: int, V: int, device) -> Tuple[int, int]:
+    """(pointer, row stride in words) of an allowed-token bitmask, after the
+    checks the kernels rely on: a CUDA int32/uint32 tensor on the logits'
+    device, [B, >= ceil(V/32)] with unit column stride (the kernels read
+    32-bit words at row * stride)."""
+    torch = _torch()
+    if not isinstance(mask, torch.Tensor) or mask.dtype not in (torch.int32, torch.uint32) or not mask.is_cuda:
+        raise TypeError("mask must be a CUDA int32/uint32 tensor")
+    if mask.device != device:
+        raise ValueError(f"mask is on {mask.device}, logits on {device}")
+    if mask.dim() != 2 or mask.shape[0] != B or mask.shape[1] * 32 < V or mask.stride(1) != 1:
+        raise ValueError("mask must be [B, >= ceil(V/32)] with unit column stride")
+    return mask.data_ptr(), mask.stride(0)
+
+
+def check_out(out, B: int, device):
+    """Caller-supplied (tokens int64, probs float32, status int32) buffers: each
+    a contiguous [B] tensor on the logits' device (the kernel writes them
+    through raw pointers)."""
+    torch = _torch()
+    try:
+        tokens, probs, status = out
+    except (TypeError, ValueError):
+        raise TypeError("out must be a (tokens, probs, status) tuple") from None
+    for name, t, dt in (("tokens", tokens, torch.int64), ("probs", probs, torch.float32),
+                        ("status", status, torch.int32)):
+        if not isinstance(t, torch.Tensor) or t.dtype != dt:
+            raise TypeError(f"out {name} must be a {dt} tensor")
+        if t.device != device or t.shape != (B,) or not t.is_contiguous():
+            raise ValueError(f"out {name} must be a contiguous [{B}] tensor on {device}")
+    return tokens, probs, status
+
+
 class Sampler:
     """Convert logit scores to token ids on the GPU (miniserve/sampler.py:20-68).
 
@@ -132,17 +165,13 @@ class Sampler:
         U = _param(uniforms, B, torch.float64, dev)
         mask_ptr, mask_ld = None, 0
         if mask is not None:
-            if mask.dtype not in (torch.int32, torch.uint32) or not mask.is_cuda:
-                raise TypeError("mask must be a CUDA int32/uint32 tensor")
-            if mask.dim() != 2 or mask.shape[0] != B or mask.shape[1] * 32 < V or mask.stride(1) != 1:
-                raise ValueError("mask must be [B, >= ceil(V/32)] with unit column stride")
-            mask_ptr, mask_ld = mask.data_ptr(), mask.stride(0)
+            mask_ptr, mask_ld = check_mask(mask, B, V, dev)
         if out is None:
             tokens = torch.empty(B, dtype=torch.int64, device=dev)
             probs = torch.empty(B, dtype=torch.float32, device=dev)
             status = torch.empty(B, dtype=torch.int32, device=dev)
         else:
-            tokens, probs, status = out
+            tokens, probs, status = check_out(out, B, dev)
         with torch.cuda.device(dev):
             stream = torch.cuda.current_stream(dev).cuda_stream
             fn = _lib.lib().ms_sample if self.path == "fast" else _lib.lib().ms_sample_generic

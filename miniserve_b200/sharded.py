@@ -23,7 +23,7 @@ from __future__ import annotations
 from typing import Optional, Sequence, Tuple
 
 from . import _lib
-from .sampler import Sampler, _param, _torch, uniform_for_seed
+from .sampler import Sampler, _param, _torch, check_mask, uniform_for_seed
 
 KMAX_LIMIT = 256
 
@@ -126,7 +126,7 @@ class ShardedSampler:
         L = _lib.lib()
         mask_ptr, mask_ld = None, 0
         if mask is not None:
-            mask_ptr, mask_ld = mask.data_ptr(), mask.stride(0)
+            mask_ptr, mask_ld = check_mask(mask, B, Vloc, dev)
         records = torch.empty((B, W), dtype=torch.int32, device=dev)
         tokens = torch.empty(B, dtype=torch.int64, device=dev)
         probs = torch.empty(B, dtype=torch.float32, device=dev)
