@@ -874,53 +874,6 @@ __device__ void st_sort(uint32_t *key, int *idx, int n, bool by_index) {
   }
 }
 
-// Index-order inverse CDF over m entries already sorted by index, weight w(i)
-// (zero = not kept).  total is the kept set's weight.  Writes the row.
-template <class W>
-__device__ void st_draw_sorted(StShared &sh, int &rf, const SampleArgs &a, int row, const int *idx, int m,
-                               double total, double U, W w) {
-  const int tid = threadIdx.x;
-  if (!(U > 0.0)) {  // r == 0 stops at index 0 (miniserve/sampler.py:66)
-    if (tid == 0) write_row(a, row, 0, (float)((m > 0 && idx[0] == 0 ? w(0) : 0.0) / total), 0);
-    return;
-  }
-  const double target = U * total;
-  const int per = (m + kStThreads - 1) / kStThreads;
-  const int p0 = tid * per, p1 = min(m, p0 + per);
-  double s = 0.0;
-  for (int i = p0; i < p1; ++i) s += w(i);
-  double ex, inc, tot;
-  st_bscan(sh, rf, s, ex, inc, tot);
-  const int who = st_bmin(sh, rf, (s > 0.0 && inc >= target) ? tid : 0x7FFFFFFF);
-  if (who == 0x7FFFFFFF) {  // ran past the end (miniserve/sampler.py:68)
-    if (tid == 0)
-      write_row(a, row, a.V - 1, (float)((m > 0 && idx[m - 1] == a.V - 1 ? w(m - 1) : 0.0) / total), 0);
-    return;
-  }
-  if (tid == who) {
-    double acc = ex;
-    int tok = -1, last = -1;
-    double wt = 0.0, wl = 0.0;
-    for (int i = p0; i < p1; ++i) {
-      const double wi = w(i);
-      if (wi <= 0.0) continue;
-      acc += wi;
-      last = idx[i];
-      wl = wi;
-      if (acc >= target) {
-        tok = idx[i];
-        wt = wi;
-        break;
-      }
-    }
-    if (tok < 0) {
-      tok = last;
-      wt = wl;
-    }
-    write_row(a, row, tok, (float)(wt / total), 0);
-  }
-}
-
 // Sort n <= kRankCap entries (key, idx) into (key desc, idx asc) order, or
 // into index order when by_index (keys carried along), by counting for each
 // entry the entries that precede it.  Stage 0 (idle) holds the composites.
@@ -1004,8 +957,10 @@ __device__ __forceinline__ uint32_t st_topk_bound_nb(StShared &sh, float rmax, i
 // descending then index ascending (the stable sort of
 // miniserve/sampler.py:37-44).  Keys below thr cannot rank in that set.  The
 // best m = min(k, entries) land in sh.w.c.key/idx[0..m) in rank order;
-// returns m.  The idle transfer stages hold scratch.  All threads.
-__device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
+// returns m.  The entries at or above thr gather at positions taken from
+// sh.nhigh (zero on entry), then each counts the entries before it.  The
+// idle transfer stages hold scratch.  All threads.
+__device__ int st_topk_rank(StShared &sh, int n, int k, uint32_t thr) {
   const int tid = threadIdx.x;
   unsigned long long *comp = reinterpret_cast<unsigned long long *>(st_scratch(sh, 0));
   // (key, ~index) composites: larger = earlier in rank order, all distinct
@@ -1015,16 +970,16 @@ __device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
   const int i1 = tid + kStThreads;
   const int f0 = (tid < n && sh.w.c.key[tid] >= thr) ? 1 : 0;
   const int f1 = (i1 < n && sh.w.c.key[i1] >= thr) ? 1 : 0;
-  const unsigned long long c0 = f0 ? compose(tid) : 0ull, c1 = f1 ? compose(i1) : 0ull;
-  int ex, n2;
-  st_bscan_i(sh, rf, f0 + f1, ex, n2);
-  if (f0) comp[ex] = c0;
-  if (f1) comp[ex + f0] = c1;
-  if (tid == 0) comp[n2] = 0ull;  // pad for the paired reads
+  if (f0 + f1) {
+    const int pos = atomicAdd(&sh.nhigh, f0 + f1);
+    if (f0) comp[pos] = compose(tid);
+    if (f1) comp[pos + f0] = compose(i1);
+  }
   __syncthreads();
+  const int n2 = sh.nhigh;
   const int m = min(n2, k);
   const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(comp);
-  const int npair = (n2 + 1) >> 1;
+  const int npair = n2 >> 1;
   for (int i = tid; i < n2; i += kStThreads) {
     const unsigned long long ci = comp[i];
     int rank = 0;
@@ -1032,6 +987,7 @@ __device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
       const ulonglong2 q = c2[j];
       rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
     }
+    if (n2 & 1) rank += comp[n2 - 1] > ci ? 1 : 0;
     if (rank < m) {
       sh.w.c.key[rank] = (uint32_t)(ci >> 32);
       sh.w.c.idx[rank] = (int)~(uint32_t)ci;
@@ -1042,34 +998,50 @@ __device__ int st_topk_rank(StShared &sh, int &rf, int n, int k, uint32_t thr) {
 }
 
 // Exact top-k finish: st_topk_rank, float64 weights exp(l/T - max/T)
-// (miniserve/sampler.py:35,45), top-p in rank order (sampler.py:49-58),
-// index-order draw (sampler.py:60-68).  All threads.
+// (miniserve/sampler.py:35,45; the maximum is the first ranked entry), top-p
+// in rank order (sampler.py:49-58), and the index-order draw
+// (sampler.py:60-68): each kept entry sums the kept weights at or before its
+// index, and the smallest index whose sum reaches U * (kept total) is the
+// token; U == 0 stops at index 0, a target past every sum gives V-1.  All
+// threads; n >= 1.
 __device__ void st_finish_small(StShared &sh, int &rf, const SampleArgs &a, int row, int n, int k, uint32_t thr,
-                                double T, double P, double U, float vmax) {
+                                double T, double P, double U) {
   const int tid = threadIdx.x;
-  const int m = st_topk_rank(sh, rf, n, k, thr);
-  // thread r holds rank r
-  const double xmax = (double)vmax / T;
+  const int m = st_topk_rank(sh, n, k, thr);
+  // thread r holds rank r (m <= kStTopK <= kStThreads)
+  const double xmax = (double)key_to_float(sh.w.c.key[0]) / T;
+  const int my = tid < m ? sh.w.c.idx[tid] : 0x7FFFFFFF;
   const double w = tid < m ? exp((double)key_to_float(sh.w.c.key[tid]) / T - xmax) : 0.0;
+  double *dw = reinterpret_cast<double *>(st_scratch(sh, 1));  // weight by rank
+  double *dinc = dw + kStTopK;                                 // running weight by rank
+  if (tid < m) dw[tid] = w;
   double wex, winc, total;
-  st_bscan(sh, rf, w, wex, winc, total);
+  st_bscan(sh, rf, w, wex, winc, total);  // its barrier publishes dw
+  if (tid < m) dinc[tid] = winc;
   int nkeep = m;
   if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept
-    const int first = st_bmin(sh, rf, (tid < m && winc >= P * total) ? tid : 0x7FFFFFFF);
+    const int first = st_bmin(sh, rf, (tid < m && winc >= P * total) ? tid : 0x7FFFFFFF);  // publishes dinc
     if (first != 0x7FFFFFFF) nkeep = first + 1;
+  } else {
+    __syncthreads();  // publishes dinc
   }
-  // kept entries in index order: position = kept entries of smaller index
-  double *dw = reinterpret_cast<double *>(st_scratch(sh, 1));
-  int *didx = sh.w.c.idx + kStTopK;
-  if (tid < nkeep) {
-    const int my = sh.w.c.idx[tid];
-    int pos = 0;
-    for (int j = 0; j < nkeep; ++j) pos += sh.w.c.idx[j] < my ? 1 : 0;
-    didx[pos] = my;
-    dw[pos] = w;
+  const double tot_keep = dinc[nkeep - 1];
+  const bool kept = tid < nkeep;
+  double cum = 0.0;
+  if (kept) {
+    for (int j = 0; j < nkeep; ++j) cum += sh.w.c.idx[j] <= my ? dw[j] : 0.0;
   }
-  const double tot_keep = st_bsum(sh, rf, tid < nkeep ? w : 0.0);
-  st_draw_sorted(sh, rf, a, row, didx, nkeep, tot_keep, U, [&](int i) { return dw[i]; });
+  const int special = U > 0.0 ? a.V - 1 : 0;  // the token when no kept entry reaches the target
+  int tok, holder;
+  st_bmin2(sh, rf, (kept && U > 0.0 && cum >= U * tot_keep) ? my : 0x7FFFFFFF,
+           (kept && my == special) ? tid : 0x7FFFFFFF, tok, holder);
+  if (tok != 0x7FFFFFFF) {
+    if (kept && my == tok) write_row(a, row, tok, (float)(w / tot_keep), 0);
+  } else if (holder != 0x7FFFFFFF) {
+    if (tid == holder) write_row(a, row, special, (float)(w / tot_keep), 0);
+  } else if (tid == 0) {
+    write_row(a, row, special, 0.0f, 0);
+  }
 }
 
 // Two fp32 values in one 64-bit register.  sm_100 executes add/sub/fma
@@ -1413,6 +1385,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     sh.ncand = 0;
+    sh.nhigh = 0;  // top-k rows: st_topk_rank's counter
   }
   __syncthreads();
   uint32_t ph = 0;
@@ -1642,8 +1615,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       if (sampled && !compacted && tau > -INFINITY && sh.ncand < k) continue;
       break;
     }
-    const float vmax = block_max_f<kStThreads>(rmax, sh.redf);
-    if (!(vmax > -INFINITY)) {  // every logit -inf (sampler.py:46-47)
+    // every finite logit is a candidate while tau is -inf, so an empty buffer
+    // means every logit is -inf (sampler.py:46-47)
+    if (sh.ncand == 0) {
       if (tid == 0) {
         if (shard) st_record_empty(a, row, 0u);  // no candidate in this slice
         else write_row(a, row, -1, 0.0f, MS_ROW_ALL_MASKED);
@@ -1691,10 +1665,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     }
     if (shard) {  // the slice's top-k, in rank order, with global ids
       // the slice's total relative to its maximum (rows without top-k)
+      const float vmax = shard_sum ? st_bmaxf(sh, rf, rmax, false, nullptr) : 0.0f;
       const double tot = shard_sum ? st_bsum(sh, rf, sm > -INFINITY ? (double)ss * exp2(((double)sm - (double)vmax) * cls)
                                                                      : 0.0)
                                    : 0.0;
-      const int m = st_topk_rank(sh, rf, n, k, thr);
+      const int m = st_topk_rank(sh, n, k, thr);
       uint32_t *rec = st_record(a, row);
       for (int i = tid; i < m; i += kStThreads) {
         rec[2 + i] = sh.w.c.key[i];
@@ -1707,7 +1682,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       return;
     }
-    st_finish_small(sh, rf, a, row, n, k, thr, T, P, U, vmax);
+    st_finish_small(sh, rf, a, row, n, k, thr, T, P, U);
     return;
   }
 
