@@ -38,6 +38,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "logits rows sampled/sec at 512x151936 top-k/top-p; % of B200 HBM roofline"
 WORKLOAD = "config3: 512x151936 fp32, heterogeneous per-row top_k/top_p/temperature"
+
+
+def config3_config(B: int, V: int, world: int) -> dict:
+    """The `config` of the metric's line, the same for both arms."""
+    return {"workload": WORKLOAD, "batch_rows": B, "vocab": V, "global_batch": B * world,
+            "parallelism": f"dp{world} (independent rows per rank)",
+            "l2": "inputs (311 MB) larger than L2 (126 MB); no flush"}
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -98,7 +105,14 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int, interval_ms: int = 20):
-        self.gpu = gpu_index
+        # nvidia-smi numbers the physical GPUs and ignores CUDA_VISIBLE_DEVICES:
+        # address this process's GPU by its UUID
+        self.gpu = str(gpu_index)
+        try:
+            import torch
+            self.gpu = f"GPU-{torch.cuda.get_device_properties(gpu_index).uuid}"
+        except Exception:
+            pass
         self.interval = interval_ms
         self.proc = None
         self.lines = []
@@ -113,7 +127,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", str(self.interval)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._reader, daemon=True).start()
@@ -262,6 +276,7 @@ def run_ours(args, rank, world, local_rank):
     clocks.__exit__(None, None, None)
     assert np.array_equal(otok.numpy(), tok.cpu().numpy())
 
+    shard = sharded_line(args, rank, world, dev, peak=hbm_peak()[0])
     if rank != 0:
         return None
     # roofline of the sampling kernel: algorithmic bytes per launch / launch time
@@ -282,9 +297,7 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Zipf-like logits, no dataset exists for this path)",
-        "config": {"workload": WORKLOAD, "batch_rows": B, "vocab": V, "global_batch": B * world,
-                   "parallelism": f"dp{world} (independent rows per rank)",
-                   "l2": "inputs (311 MB) larger than L2 (126 MB); no flush"},
+        "config": config3_config(B, V, world),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profiled_traffic(),
                      "traffic_unit": "DRAM bytes per launch (ncu, profiles/stream_kernel_config3_full.md)",
@@ -295,6 +308,60 @@ def run_ours(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "gpu_launches": args.steps * launches_per_call(),
         "clocks": clocks.summary(),
+        "sharded": shard,
+    }
+
+
+def sharded_line(args, rank, world, dev, peak):
+    """Config 5 (1024 x 256000 fp32, top_k 50, top_p 0.95, T 0.9) with the
+    vocabulary split into contiguous slices over the ranks, sampled through
+    ShardedSampler.sample (shard pass, NCCL all-gather of the candidate
+    records, merge).  Strong scaling: the same rows on every N.  Each phase
+    timed with CUDA events on the launching stream; the step time is the max
+    over ranks."""
+    import torch
+    import torch.distributed as dist
+    from miniserve_b200 import sharded, workloads
+    b = workloads.config5(5)
+    B, V = b.B, b.V
+    v0, v1 = sharded.shard_bounds(V, world, rank)
+    x = torch.from_numpy(b.logits[:, v0:v1].copy()).to(dev)
+    del b.logits
+    U = torch.from_numpy(b.uniforms).to(dev)
+    T, K, P = float(b.temperature[0]), int(b.top_k[0]), float(b.top_p[0])  # uniform over the rows
+    ss = sharded.ShardedSampler(V)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(3, min(args.steps, 20))
+    for _ in range(max(args.warmup, 3)):
+        ss.sample(x, v0, T, K, P, uniforms=U)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        tok, prob, st = ss.sample(x, v0, T, K, P, uniforms=U, events=evs[i])
+    torch.cuda.synchronize()
+    ph = torch.tensor([[e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), e[2].elapsed_time(e[3])]
+                       for e in evs], dtype=torch.float64, device=dev)
+    per_step = ph.sum(dim=1)
+    stats = torch.stack([per_step.mean(), ph[:, 0].mean(), ph[:, 1].mean(), ph[:, 2].mean()])
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    step_ms, shard_ms, gather_ms, merge_ms = (float(v) for v in stats.tolist())
+    flagged = int((st != 0).sum())
+    alg = B * ((v1 - v0) * 4 + 52)  # this rank's logits slice and per-row parameters
+    return {
+        "workload": "config5: 1024x256000 fp32, vocab sliced over the GPUs, top_k 50, top_p 0.95, T 0.9",
+        "api": "miniserve_b200.sharded.ShardedSampler.sample", "scaling": "strong", "nccl_ranks": world,
+        "value": round(B / (step_ms / 1e3), 1), "unit": "rows/s", "ms_per_step": round(step_ms, 5),
+        "phase_us": {"shard_pass": round(shard_ms * 1e3, 2), "all_gather": round(gather_ms * 1e3, 2),
+                     "merge": round(merge_ms * 1e3, 2)},
+        "gather_bytes_per_rank": B * sharded.record_words(50) * 4,
+        "per_gpu_hbm": {"achieved": round(alg / (shard_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(alg / (shard_ms / 1e3) / 1e9 / peak, 4), "kernel": "shard pass"},
+        "rows_flagged": flagged, "steps": steps,
+        "timing": "CUDA events per phase on the launching stream, max over ranks; device time",
     }
 
 
@@ -339,7 +406,30 @@ def run_workload(args, rank, world, local_rank):
            "vs_baseline": None, "data": "synthetic (seeded; BASELINE.json configuration)"}
     clocks = ClockSampler(local_rank).__enter__()
     clocks.wait_first()
-    if args.workload == "config2":
+    if args.workload == "config1":
+        lines = {}
+        for greedy in (False, True):
+            b = workloads.config1(1 + rank, greedy=greedy)
+            B, V = b.B, b.V
+            x = torch.from_numpy(b.logits).to(dev)
+            T, K, P, U = (torch.from_numpy(a).to(dev) for a in (b.temperature, b.top_k, b.top_p, b.uniforms))
+            tok = torch.empty(B, dtype=torch.int64, device=dev)
+            prob = torch.empty(B, dtype=torch.float32, device=dev)
+            st = torch.empty(B, dtype=torch.int32, device=dev)
+
+            def step():
+                _lib.check(L.ms_sample(x.data_ptr(), 0, B, V, V, T.data_ptr(), K.data_ptr(), P.data_ptr(),
+                                       U.data_ptr(), None, 0, tok.data_ptr(), prob.data_ptr(), st.data_ptr(),
+                                       sptr), "ms_sample")
+            lines["greedy" if greedy else "sampled"] = _time_ms(step, args.steps, args.warmup, stream, world)
+        ms = lines["sampled"]
+        out.update(metric="latency of one 8x151936 sampling call (config 1)", value=round(ms * 1e3, 2),
+                   unit="us/call", higher_is_better=False, ms_per_step=round(ms, 5), scaling="weak",
+                   dtype="f32", config={"workload": "config1: 8x151936 fp32, T 0.7, top_k 50, top_p 0.9",
+                                        "batch_rows": 8, "vocab": 151936},
+                   greedy_us_per_call=round(lines["greedy"] * 1e3, 2),
+                   note="latency-bound (8 rows on 148 SMs); the L2 holds the 4.9 MB batch between calls")
+    elif args.workload == "config2":
         b = workloads.config2(2 + rank)
         B, V = b.B, b.V
         esz = 2 if args.bf16 else 4
@@ -482,7 +572,7 @@ def run_reference(args, rank):
         "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded Zipf-like logits)",
-        "config": {"workload": WORKLOAD, "batch_rows": batch.B, "vocab": batch.V},
+        "config": config3_config(batch.B, batch.V, args.gpus),
         "cpu_baseline": {"value": round(value, 3), "unit": "rows/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "rows/s", "h2d_bytes_per_step": 0,
@@ -497,7 +587,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config3", "config2", "config4", "config5"], default="config3",
+    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5"], default="config3",
                     help="config3 (default) is the metric's configuration; the others print their own line")
     ap.add_argument("--bf16", action="store_true", help="config2: bf16 logits")
     args = ap.parse_args()

@@ -57,6 +57,17 @@ def choose_kmax(top_k: Sequence[int], temperature: Sequence[float],
     return need
 
 
+def _host_list(x, B: int):
+    """The per-row values of a host-side parameter (scalar or sequence) as a
+    list, or None for a tensor (whose values live on the device)."""
+    torch = _torch()
+    if isinstance(x, torch.Tensor):
+        return None
+    if isinstance(x, (int, float)):
+        return [x] * B
+    return list(x)
+
+
 def exchange_records(records, group=None):
     """All-gather [B, W] int32 records of every rank -> [world, B, W], rank-major."""
     torch = _torch()
@@ -99,14 +110,26 @@ class ShardedSampler:
 
     def sample(self, logits_slice, v0: int, temperature=1.0, top_k=0, top_p=1.0,
                uniforms=None, seeds: Optional[Sequence[Optional[int]]] = None,
-               mask=None):
+               mask=None, kmax: Optional[int] = None, events=None):
         """``logits_slice``: this rank's [B, Vloc] CUDA tensor (fp32/bf16) for
         tokens [v0, v0 + Vloc); ``mask``: optional [B, ceil(Vloc/32)] bitmask of
         the slice.  Per-row parameters must be the same on every rank.  Returns
-        (tokens i64, probs f32, status i32), identical on every rank."""
+        (tokens i64, probs f32, status i32), identical on every rank.
+
+        The record width ``kmax`` is chosen from the parameters (choose_kmax)
+        when they are host values; pass it when they are device tensors, or
+        their values are read back once.  After the merge one device->host read
+        of a count decides whether any row needs the full-row path.
+        ``events``: optional four CUDA events recorded around the shard pass,
+        the all-gather and the merge (for timing the phases)."""
         torch = _torch()
         if logits_slice.dim() != 2 or not logits_slice.is_cuda:
             raise ValueError("logits_slice must be a [B, Vloc] CUDA tensor")
+        if kmax is None:
+            B0 = logits_slice.shape[0]
+            hk, ht, hp = _host_list(top_k, B0), _host_list(temperature, B0), _host_list(top_p, B0)
+            if hk is not None and ht is not None and hp is not None:
+                kmax = choose_kmax(hk, ht, hp, self.V)
         if logits_slice.stride(1) != 1:
             logits_slice = logits_slice.contiguous()
         dtype = {torch.float32: _lib.MS_DTYPE_F32, torch.bfloat16: _lib.MS_DTYPE_BF16}.get(logits_slice.dtype)
@@ -121,7 +144,11 @@ class ShardedSampler:
             seeds = [None] * B if seeds is None else list(seeds)
             uniforms = [uniform_for_seed(s) for s in seeds]
         U = _param(uniforms, B, torch.float64, dev)
-        kmax = choose_kmax(K.tolist(), T.tolist(), P.tolist(), self.V)
+        if kmax is None:  # device-side parameters: one read of their values
+            kmax = choose_kmax(K.tolist(), T.tolist(), P.tolist(), self.V)
+        if not 1 <= int(kmax) <= KMAX_LIMIT:
+            raise ValueError(f"kmax must be in 1..{KMAX_LIMIT}")
+        kmax = int(kmax)
         W = record_words(kmax)
         L = _lib.lib()
         mask_ptr, mask_ld = None, 0
@@ -132,20 +159,29 @@ class ShardedSampler:
         probs = torch.empty(B, dtype=torch.float32, device=dev)
         status = torch.empty(B, dtype=torch.int32, device=dev)
         with torch.cuda.device(dev):
-            stream = torch.cuda.current_stream(dev).cuda_stream
+            cur = torch.cuda.current_stream(dev)
+            stream = cur.cuda_stream
+            if events is not None:
+                events[0].record(cur)
             rc = L.ms_shard_candidates(logits_slice.data_ptr(), dtype, B, Vloc, logits_slice.stride(0), int(v0),
                                        self.V, T.data_ptr(), K.data_ptr(), mask_ptr, mask_ld, kmax,
                                        records.data_ptr(), stream)
             _lib.check(rc, "ms_shard_candidates")
+            if events is not None:
+                events[1].record(cur)
             allrec = exchange_records(records, self.group)
+            if events is not None:
+                events[2].record(cur)
             nranks = allrec.shape[0]
             rc = L.ms_shard_merge(allrec.data_ptr(), nranks, B, kmax, self.V, T.data_ptr(), K.data_ptr(),
                                   P.data_ptr(), U.data_ptr(), tokens.data_ptr(), probs.data_ptr(),
                                   status.data_ptr(), stream)
             _lib.check(rc, "ms_shard_merge")
-        redo = ((status & (_lib.MS_ROW_UNSUPPORTED | _lib.MS_ROW_NONFINITE)) != 0).nonzero().flatten()
-        if redo.numel():
-            rows = redo.to(dev)
+            if events is not None:
+                events[3].record(cur)
+        flagged = (status & (_lib.MS_ROW_UNSUPPORTED | _lib.MS_ROW_NONFINITE)) != 0
+        if int(flagged.sum()):  # the statuses are identical on every rank: so is this branch
+            rows = flagged.nonzero().flatten()
             full = gather_rows(logits_slice, rows, self.V, self.group)
             fmask = None
             if mask is not None:
