@@ -429,6 +429,36 @@ def run_workload(args, rank, world, local_rank):
                                         "batch_rows": 8, "vocab": 151936},
                    greedy_us_per_call=round(lines["greedy"] * 1e3, 2),
                    note="latency-bound (8 rows on 148 SMs); the L2 holds the 4.9 MB batch between calls")
+    elif args.workload == "cliff":
+        # config 3 with one NaN row and one top_k 300 row: the cost of rows the
+        # streaming passes do not finish (the NaN row takes the generic kernel)
+        b = workloads.config3(3 + rank)
+        B, V = b.B, b.V
+        logits = b.logits.copy()
+        logits[5, 1234] = np.nan
+        K = b.top_k.copy()
+        K[6] = 300
+        x = torch.from_numpy(logits).to(dev)
+        x0 = torch.from_numpy(b.logits).to(dev)
+        T, Kt, K0, P, U = (torch.from_numpy(a).to(dev) for a in (b.temperature, K, b.top_k, b.top_p, b.uniforms))
+        tok = torch.empty(B, dtype=torch.int64, device=dev)
+        prob = torch.empty(B, dtype=torch.float32, device=dev)
+        st = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def call(xx, kk):
+            _lib.check(L.ms_sample(xx.data_ptr(), 0, B, V, V, T.data_ptr(), kk.data_ptr(), P.data_ptr(),
+                                   U.data_ptr(), None, 0, tok.data_ptr(), prob.data_ptr(), st.data_ptr(), sptr),
+                       "ms_sample")
+        ms_clean = _time_ms(lambda: call(x0, K0), args.steps, args.warmup, stream, world)
+        ms = _time_ms(lambda: call(x, Kt), args.steps, args.warmup, stream, world)
+        nonfinite = int((st.cpu() & _lib.MS_ROW_NONFINITE != 0).sum())
+        out.update(metric="config 3 with one NaN row and one top_k 300 row: us per 512-row call",
+                   value=round(ms * 1e3, 2), unit="us/call", higher_is_better=False, ms_per_step=round(ms, 5),
+                   scaling="weak", dtype="f32",
+                   config={"workload": "config3 + row 5 holding a NaN + row 6 with top_k 300", "batch_rows": B,
+                           "vocab": V},
+                   clean_us_per_call=round(ms_clean * 1e3, 2), ratio_to_clean=round(ms / ms_clean, 3),
+                   rows_nonfinite=nonfinite)
     elif args.workload == "config2":
         b = workloads.config2(2 + rank)
         B, V = b.B, b.V
@@ -587,7 +617,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5"], default="config3",
+    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5", "cliff"], default="config3",
                     help="config3 (default) is the metric's configuration; the others print their own line")
     ap.add_argument("--bf16", action="store_true", help="config2: bf16 logits")
     args = ap.parse_args()

@@ -208,6 +208,19 @@ int ms_build_json_mask_ordered(const uint32_t *states, int64_t B, const uint8_t 
                                const int32_t *order, int64_t V, uint32_t *mask, int64_t mask_ld,
                                int32_t *row_status, ms_stream_t stream);
 
+/*
+ * The allowed-token bitmask from a logits-processor hook's output.
+ * Replaces the hook convention of miniserve/model_runner.py:166-168,214-216
+ * (fn(logits[V], generated) -> logits[V], a disallowed token set to -inf,
+ * then argmax): `logits` [B, ld] (dtype as in ms_sample) holds what the hook
+ * returned, and mask[b, t >> 5] bit (t & 31) is set when logits[b, t] is not
+ * -inf (a NaN counts as allowed; the sampler then flags the row
+ * MS_ROW_NONFINITE).  The mask feeds ms_sample unchanged.  1 <= B <= 65535,
+ * mask_ld >= ceil(V/32); words past ceil(V/32) are not written.
+ */
+int ms_mask_from_logits(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld, uint32_t *mask,
+                        int64_t mask_ld, ms_stream_t stream);
+
 /* Human-readable text for an MS_E_* code. */
 const char *ms_error_string(int code);
 

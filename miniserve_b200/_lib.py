@@ -35,6 +35,7 @@ SIGNATURES = {
                                          _I64, _P, _P, _P, _P]),
     "ms_shard_candidates": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
                                            _I64, ctypes.c_int32, _P, _P]),
+    "ms_mask_from_logits": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P]),
     "ms_shard_record_words": (_I64, [ctypes.c_int32]),
     "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,
                                       _P, _P, _P, _P]),

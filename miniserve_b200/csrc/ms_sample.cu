@@ -18,6 +18,7 @@
 
 #include "ms_common.cuh"
 #include "ms_generic.cuh"
+#include "ms_hook.cuh"
 #include "ms_json.cuh"
 #include "ms_shard.cuh"
 #include "ms_stream.cuh"
@@ -155,6 +156,24 @@ int ms_sample_generic(const void *logits, int dtype, int64_t B, int64_t V, int64
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
   return sample_impl(logits, dtype, B, V, ld, temperature, top_k, top_p, uniforms, mask, mask_ld,
                      tokens, probs, row_status, stream, true);
+}
+
+int ms_mask_from_logits(const void *logits, int dtype, int64_t B, int64_t V, int64_t ld, uint32_t *mask,
+                        int64_t mask_ld, ms_stream_t stream) {
+  if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
+  if (B < 0 || B > 65535 || V < 1 || V > 0x7FFFFFFFll - 32 || ld < V || mask_ld < (V + 31) / 32) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!logits || !mask) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t words = (V + 31) / 32;
+  const dim3 grid((unsigned)((words + ms::kHookWordsPerCta - 1) / ms::kHookWordsPerCta), (unsigned)B);
+  if (dtype == MS_DTYPE_F32) {
+    ms::ms_mask_from_logits_kernel<MS_DTYPE_F32><<<grid, ms::kHookThreads, 0, s>>>(logits, ld, (int)V, mask, mask_ld);
+  } else {
+    ms::ms_mask_from_logits_kernel<MS_DTYPE_BF16><<<grid, ms::kHookThreads, 0, s>>>(logits, ld, (int)V, mask, mask_ld);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
 
 int64_t ms_shard_record_words(int32_t kmax) { return 4 + 2 * (int64_t)kmax; }

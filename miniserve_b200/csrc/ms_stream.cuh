@@ -78,7 +78,7 @@ __host__ __device__ constexpr int st_nstages() {
 constexpr int kCandCap = 6144;                  // top-k candidate buffer entries
 constexpr int kSortCap = 4096;                  // largest set st_sort handles
 constexpr int kRankCap = 1024;                  // largest set sorted by rank counting
-constexpr int kStTopK = 256;                    // largest top_k resolved by the streaming pass
+constexpr int kStTopK = 512;                    // largest top_k resolved by the streaming pass (a rank per thread)
 constexpr int kMaxUnits = 2048;                 // per-unit summaries kept per row
 constexpr int kStreamMaxV = kMaxUnits * kUnit;  // longest row this kernel takes
 constexpr int kNarrowUnits = 128;               // top-p: the unit maxima tried as a narrow nucleus's bound

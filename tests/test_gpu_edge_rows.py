@@ -58,6 +58,9 @@ def edge_batch(seed=11):
     add(_zipf(rng), 1e-31, 0, 0.9, 0.5, "temperature below the fp32 weight range")
     add(_zipf(rng), 1e4, 0, 0.5, 0.4761, "temperature 1e4 top-p")
     add(_zipf(rng), 0.9, 256, 1.0, 0.81, "top_k 256 (streaming limit)")
+    add(_zipf(rng), 0.9, 300, 0.95, 0.33, "top_k 300")
+    add(_zipf(rng), 1.1, 512, 0.9, 0.66, "top_k 512 (streaming limit)")
+    add(_zipf(rng), 1.1, 513, 0.9, 0.66, "top_k 513 (generic kernel)")
     add(_zipf(rng), 0.9, 257, 0.95, 0.19, "top_k 257 (generic kernel)")
     add(_zipf(rng), 0.9, V - 1, 0.9, 0.33, "top_k V-1")
     q = np.round(_zipf(rng) * 20.0) / 20.0
