@@ -78,7 +78,7 @@ def _ref_rows(args):
     from oracle import sampler_oracle as so
     out = []
     for b in range(len(T)):
-        out.append(so.sample_row(logits[b].tolist(), float(T[b]), int(K[b]), float(P[b]), float(U[b])).token)
+        out.append(so.sample_token(logits[b].tolist(), float(T[b]), int(K[b]), float(P[b]), float(U[b])))
     return out
 
 

@@ -142,6 +142,50 @@ def sample_row(logits: Sequence[float], temperature: float, top_k: int, top_p: f
                      sum(1 for q in probs if q > 0.0))
 
 
+def sample_token(logits: Sequence[float], temperature: float, top_k: int, top_p: float, u: float) -> int:
+    """The token alone, in the reference's own steps and calls
+    (miniserve/sampler.py:33-68): builtins ``sum`` (which ``py_sum``
+    restates and the tests pin), no margins.  Used to time the reference
+    algorithm on the host (bench.py), where sample_row's bookkeeping would
+    make the CPU baseline slower than the reference itself."""
+    n = len(logits)
+    if temperature == 0.0:
+        return max(range(n), key=lambda i: logits[i])
+    if not (temperature > 0.0) or math.isinf(temperature):
+        return -1
+    scaled = [l / temperature for l in logits]
+    if top_k > 0:
+        order = sorted(range(n), key=lambda i: scaled[i], reverse=True)[:top_k]
+        filtered = [-math.inf] * n
+        for i in order:
+            filtered[i] = scaled[i]
+        scaled = filtered
+    max_v = max(scaled)
+    exps = [math.exp(v - max_v) if v != -math.inf else 0.0 for v in scaled]
+    total = sum(exps)
+    if total == 0.0:
+        return -1
+    probs = [e / total for e in exps]
+    if top_p < 1.0:
+        sorted_idx = sorted(range(n), key=lambda i: probs[i], reverse=True)
+        cumsum = 0.0
+        keep = set()
+        for i in sorted_idx:
+            cumsum += probs[i]
+            keep.add(i)
+            if cumsum >= top_p:
+                break
+        probs = [p if i in keep else 0.0 for i, p in enumerate(probs)]
+        total = sum(probs)
+        probs = [p / total for p in probs]
+    cumulative = 0.0
+    for i, p in enumerate(probs):
+        cumulative += p
+        if u <= cumulative:
+            return i
+    return n - 1
+
+
 def sample_rows(rows, temperature, top_k, top_p, uniforms) -> List[RowResult]:
     """Row loop over a 2-D array-like (one reference call per row)."""
     out = []

@@ -73,3 +73,16 @@ def test_c_oracle_matches_reference_configs():
         want = [golden_util.expected_token(t) for t in entry["ref_tokens"]]
         assert tok.tolist() == want, entry["name"]
         assert np.all(prob[np.array(want) >= 0] > 0)
+
+
+def test_token_only_restatement_matches_reference():
+    """sample_token (the host-timed form) gives the reference's tokens."""
+    for c in cases.kat_cases():
+        assert so.sample_token(c["logits"], c["temperature"], c["top_k"], c["top_p"], c["u"]) == c["token"]
+    g = golden_util.load()
+    for entry in g["small"]:
+        x, T, k, p, u, _ = cases.group(entry["V"], entry["case_seed"])
+        for b in range(x.shape[0]):
+            want = golden_util.expected_token(entry["ref_tokens"][b])
+            got = so.sample_token(x[b].tolist(), T[b], k[b], p[b], u[b])
+            assert got == (want if want >= 0 else -1), (entry["V"], b)
