@@ -48,8 +48,9 @@ struct SampleArgs {
   int kmax = 0;
   int64_t v0 = 0;
   int64_t Vg = 0;
-  // pair mode: the streaming kernel runs as 2 * rows CTAs in clusters of two;
-  // a top-p row takes both CTAs of a cluster, the other rows one CTA each
+  // pair mode (pairs > 0): the streaming kernel runs as 2 * rows CTAs in
+  // clusters of two; when the batch holds at most `pairs` top-p rows each
+  // takes both CTAs of a cluster, the other rows one CTA each
   int pairs = 0;
   int rows = 0;
 };

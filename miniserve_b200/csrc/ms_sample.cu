@@ -33,7 +33,8 @@ int cuda_fail(cudaError_t e) {
 
 constexpr int kMaxDevices = 64;
 
-// The streaming kernel alone (one CTA per row).
+// The streaming kernel alone: one CTA per row, or in pair mode B clusters of
+// two CTAs.
 template <int DT>
 cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int dev) {
   static std::atomic<int> ready[kMaxDevices];
@@ -66,8 +67,8 @@ cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int de
   return cudaGetLastError();
 }
 
-// The streaming kernel (one CTA per row) for every row it can finish, then
-// the generic kernel for the rows it marked pending.
+// The streaming kernel for every row it can finish, then the generic kernel
+// for the rows it marked pending.
 template <int DT>
 cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, bool generic_only) {
   if (generic_only || a.V > ms::kStreamMaxV) {
@@ -77,7 +78,9 @@ cudaError_t launch_all(const ms::SampleArgs &a, int B, cudaStream_t s, int dev, 
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   ms::SampleArgs ap = a;
-  ap.pairs = B <= (1 << 29) ? 1 : 0;
+  // top-p rows are shared by CTA pairs while they fit one wave (one cluster
+  // per SM)
+  ap.pairs = B <= (1 << 29) ? sms : 0;
   ap.rows = B;
   cudaError_t e = launch_stream<DT>(ap, B, s, dev);
   if (e != cudaSuccess) return e;

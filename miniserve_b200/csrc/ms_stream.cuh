@@ -1212,7 +1212,9 @@ __device__ __forceinline__ int st_row_class(const SampleArgs &a, int r) {
 // parameters.  One CTA per row: CTA i takes position i.  Pair mode (clusters
 // of two CTAs, 2B CTAs launched): cluster i takes work item i -- the i-th
 // top-p row, shared by both CTAs (*joint set), or after those, the next two
-// positions, one per CTA; the clusters past the work take none.
+// positions, one per CTA; the clusters past the work take none.  A batch with
+// more than a.pairs top-p rows shares none (sharing shortens a top-p row but
+// costs CTA time, which pays only while the top-p rows fit one wave).
 __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   *joint = false;
@@ -1240,7 +1242,7 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
   __syncthreads();
   int want = blockIdx.x;
   if (a.pairs) {
-    const int item = blockIdx.x >> 1, np = sh.ptot[0];
+    const int item = blockIdx.x >> 1, np = sh.ptot[0] <= a.pairs ? sh.ptot[0] : 0;
     if (item < np) {
       want = item;
       *joint = true;
