@@ -526,6 +526,68 @@ def run_workload(args, rank, world, local_rank):
                    roofline={"bound": "hbm", "kernel": "masked sampling",
                              "achieved": round(alg / (ms_sample / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(alg / (ms_sample / 1e3) / 1e9 / peak, 4), "traffic": None})
+    elif args.workload == "graphed":
+        # a decode step shaped like Qwen2.5-0.5B's last layer (hidden 896, fp32
+        # LM head over 151936 tokens, the max bucket of 32 rows) captured as a
+        # CUDA graph: the reference flow (replay, clone of the static logits,
+        # sampling of the clone) against sampling captured into the graph,
+        # reading the static buffer in place
+        from miniserve_b200.graphed import GraphedSampler
+        B, V, d = 32, workloads.QWEN_VOCAB, 896
+        gen = torch.Generator(device="cpu").manual_seed(6 + rank)
+        head = (torch.randn(V, d, generator=gen) * 0.05).to(dev)
+        hidden = torch.randn(B, d, generator=gen).to(dev)
+        out_buf = torch.zeros(B, V, dtype=torch.float32, device=dev)
+        gs = GraphedSampler(out_buf)
+        seeds = [1000 + i for i in range(B)]
+        gs.set_params(B, temperature=0.7, top_k=50, top_p=0.9, seeds=seeds)
+
+        def lm_head():
+            out_buf[:B] = hidden @ head.T
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            lm_head()
+        stream.wait_stream(side)
+        g_ref, g_ours = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_ref):
+            lm_head()
+        with torch.cuda.graph(g_ours):
+            lm_head()
+            gs.enqueue(B)
+        torch.cuda.synchronize(dev)
+        T, K, P = gs.temperature[:B].clone(), gs.top_k[:B].clone(), gs.top_p[:B].clone()
+        U = gs.uniforms[:B].clone()
+        tok = torch.empty(B, dtype=torch.int64, device=dev)
+        prob = torch.empty(B, dtype=torch.float32, device=dev)
+        st = torch.empty(B, dtype=torch.int32, device=dev)
+
+        def sample_on(x):
+            _lib.check(L.ms_sample(x.data_ptr(), 0, B, V, V, T.data_ptr(), K.data_ptr(), P.data_ptr(),
+                                   U.data_ptr(), None, 0, tok.data_ptr(), prob.data_ptr(), st.data_ptr(),
+                                   sptr), "ms_sample")
+
+        def step_ref():  # model_runner.py:321, then the sampler on the copy
+            g_ref.replay()
+            sample_on(out_buf[:B].clone())
+
+        ms_head = _time_ms(g_ref.replay, args.steps, args.warmup, stream, world)
+        ms_ref = _time_ms(step_ref, args.steps, args.warmup, stream, world)
+        ms = _time_ms(g_ours.replay, args.steps, args.warmup, stream, world)
+        ms_sample = _time_ms(lambda: sample_on(out_buf), args.steps, args.warmup, stream, world)
+        same = torch.equal(tok, gs.result(B)[0])
+        out.update(metric="decode-step rows/s at B 32 (fp32 LM head 896 -> 151936 + sampling in one CUDA graph)",
+                   value=round(world * B / (ms / 1e3), 1), unit="rows/s", ms_per_step=round(ms, 5),
+                   scaling="weak", dtype="f32",
+                   config={"workload": "graphed: LM head [151936, 896] fp32, B 32, T 0.7, top_k 50, top_p 0.9",
+                           "batch_rows": B, "vocab": V, "hidden": d},
+                   in_graph_us=round(ms * 1e3, 2), clone_flow_us=round(ms_ref * 1e3, 2),
+                   lm_head_us=round(ms_head * 1e3, 2), sampling_us=round(ms_sample * 1e3, 2),
+                   clone_bytes_per_step=B * V * 4, tokens_equal=bool(same),
+                   note="the clone flow copies the static logits before sampling (model_runner.py:321); "
+                        "the in-graph flow samples them in place")
+        del g_ref, g_ours
     else:  # config5: vocab-sharded over the ranks
         b = workloads.config5(5)
         B, V = b.B, b.V
@@ -617,7 +679,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5", "cliff"], default="config3",
+    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5", "cliff", "graphed"],
+                    default="config3",
                     help="config3 (default) is the metric's configuration; the others print their own line")
     ap.add_argument("--bf16", action="store_true", help="config2: bf16 logits")
     args = ap.parse_args()
