@@ -588,6 +588,50 @@ def run_workload(args, rank, world, local_rank):
                    note="the clone flow copies the static logits before sampling (model_runner.py:321); "
                         "the in-graph flow samples them in place")
         del g_ref, g_ours
+    elif args.workload == "nucleus":
+        # config 5's logits with top_k off (top_p 0.95 and top_p 1 rows, T 0.9
+        # and 1.5), vocab-sharded over the ranks, through ShardedSampler: rows
+        # the records settle, rows the distributed nucleus finishes (no logits
+        # exchanged), against the full-row path for the same rows (all-gather
+        # of their logits and ms_sample on every rank)
+        B = 256
+        b = workloads.config5(5, B=B)
+        V = b.V
+        v0, v1 = sharded.shard_bounds(V, world, rank)
+        x = torch.from_numpy(np.ascontiguousarray(b.logits[:, v0:v1])).to(dev)
+        del b.logits
+        rng = np.random.default_rng(55)
+        Th = np.where(rng.random(B) < 0.5, 0.9, 1.5)
+        Ph = np.where(rng.random(B) < 0.25, 1.0, 0.95)
+        Kh = np.zeros(B, np.int32)
+        T, K, P, U = (torch.from_numpy(a).to(dev) for a in (Th, Kh, Ph, b.uniforms))
+        ss = sharded.ShardedSampler(V)
+        kmax = sharded.choose_kmax(Kh.tolist(), Th.tolist(), Ph.tolist(), V)
+
+        def step():
+            ss.sample(x, v0, T, K, P, uniforms=U, kmax=kmax)
+
+        ms = _time_ms(step, args.steps, args.warmup, stream, world)
+        tok, prob, st = ss.sample(x, v0, T, K, P, uniforms=U, kmax=kmax)
+        n_nuc, n_full = ss.last_nucleus_rows, ss.last_full_rows
+        rows = torch.arange(B, device=dev)
+        single = sharded.Sampler()
+
+        def full_rows():  # the alternative for every row: gather the logits, sample the full rows
+            full = sharded.gather_rows(x, rows, V)
+            single.sample_batch(full, T, K, P, uniforms=U)
+
+        ms_full = _time_ms(full_rows, args.steps, args.warmup, stream, world)
+        out.update(metric="rows/s of vocab-sharded rows without top-k (config-5 logits, 256 rows)",
+                   value=round(B / (ms / 1e3), 1), unit="rows/s", ms_per_step=round(ms, 5), scaling="strong",
+                   dtype="f32",
+                   config={"workload": "nucleus: config-5 logits 256x256000 fp32, top_k 0, top_p 0.95/1.0, "
+                                       "T 0.9/1.5, vocab sliced over the GPUs",
+                           "batch_rows": B, "vocab": V, "nccl_ranks": world, "kmax": kmax},
+                   rows_settled_by_records=B - n_nuc - n_full, rows_distributed_nucleus=n_nuc,
+                   rows_full_row_path=n_full, full_row_gather_us=round(ms_full * 1e3, 2),
+                   full_row_gather_bytes_per_rank=B * (v1 - v0) * 4,
+                   note="device time of the whole call (CUDA events), host reads of the flag counts included")
     else:  # config5: vocab-sharded over the ranks
         b = workloads.config5(5)
         B, V = b.B, b.V
@@ -679,7 +723,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5", "cliff", "graphed"],
+    ap.add_argument("--workload", choices=["config3", "config1", "config2", "config4", "config5", "cliff", "graphed",
+                                           "nucleus"],
                     default="config3",
                     help="config3 (default) is the metric's configuration; the others print their own line")
     ap.add_argument("--bf16", action="store_true", help="config2: bf16 logits")

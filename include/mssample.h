@@ -145,6 +145,63 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
                    ms_stream_t stream);
 
 /*
+ * The distributed nucleus: vocab-sharded rows without top-k that
+ * ms_shard_merge flags MS_ROW_UNSUPPORTED (a nucleus wider than the
+ * candidates, or top_p >= 1), sampled without gathering their logits
+ * (miniserve/sampler.py:35-68 with top_k off).  rows: [F] the batch rows to
+ * finish; records: the all-gathered candidate records of the merge
+ * ([nranks][B][rec_words], kmax >= 2), which give each row's maximum.  Every
+ * rank, in this order:
+ *
+ *   1. ms_nucleus_hist on its slice -> hist [F][hist_words] u32 (fixed-point
+ *      histogram of the row's weights over (max - logit) / T, scaled from V
+ *      so that the sum over all ranks stays below 2^31)
+ *   2. the caller all-reduces hist (sum, as int32)
+ *   3. ms_nucleus_bracket -> bracket [F][2] i32 (the bins holding the top-p
+ *      crossing; identical on every rank)
+ *   4. ms_nucleus_classify on its slice -> entries [F][record_words] u32 (the
+ *      slice's mass above the bracket and in all, the bracket's values) and
+ *      segments [F][ms_nucleus_segments()] f64 (the mass above the bracket
+ *      of each index-order segment of the slice; stays on the rank)
+ *   5. the caller all-gathers entries rank-major: [nranks][F][record_words]
+ *   6. ms_nucleus_cut -> cut [F][cut_words] u32 (the crossing entry, the
+ *      rank whose slice holds the draw's target; identical on every rank).
+ *      bounds: [nranks + 1] i64, the slices' first global ids and V.
+ *   7. ms_nucleus_draw on its slice (with the all-gathered entries and its
+ *      own segments) -> out [F][2] i64: (token, float bits of its
+ *      probability) on the owning rank, (-1, 0) elsewhere
+ *   8. the caller all-reduces out (max): every rank has each row's token.
+ *
+ * A row whose cut record's status word ([3]) is nonzero (its bracket held
+ * more than 2048 of a slice's values, or the histogram missed the crossing)
+ * comes back with token -1 from step 7 and is left to the full-row path.
+ * Vloc <= 2^20, V < 2^27, nranks <= 256.
+ */
+int64_t ms_nucleus_hist_words(void);
+int64_t ms_nucleus_record_words(void);
+int64_t ms_nucleus_cut_words(void);
+int64_t ms_nucleus_segments(void);
+int ms_nucleus_hist(const void *logits, int dtype, int64_t Vloc, int64_t ld, const uint32_t *mask, int64_t mask_ld,
+                    const int32_t *rows, int64_t F, int64_t B, int64_t V, const uint32_t *records, int32_t nranks,
+                    int32_t kmax, const double *temperature, const double *top_p, uint32_t *hist,
+                    ms_stream_t stream);
+int ms_nucleus_bracket(const uint32_t *hist, const int32_t *rows, int64_t F, int64_t V, const double *top_p,
+                       int32_t *bracket, ms_stream_t stream);
+int ms_nucleus_classify(const void *logits, int dtype, int64_t Vloc, int64_t ld, int64_t v0, const uint32_t *mask,
+                        int64_t mask_ld, const int32_t *rows, int64_t F, int64_t B, const uint32_t *records,
+                        int32_t nranks, int32_t kmax, const double *temperature, const int32_t *bracket,
+                        uint32_t *entries, double *segments, ms_stream_t stream);
+int ms_nucleus_cut(const uint32_t *entries, int32_t nranks, const int64_t *bounds, const int32_t *bracket,
+                   const int32_t *rows, int64_t F, int64_t B, const uint32_t *records, int32_t kmax,
+                   const double *temperature, const double *top_p, const double *uniforms, uint32_t *cut,
+                   ms_stream_t stream);
+int ms_nucleus_draw(const void *logits, int dtype, int64_t Vloc, int64_t ld, int64_t v0, const uint32_t *mask,
+                    int64_t mask_ld, const int32_t *rows, int64_t F, int64_t B, const uint32_t *records,
+                    int32_t nranks, int32_t kmax, const double *temperature, const uint32_t *cut,
+                    const uint32_t *entries, const double *segments, int32_t rank, int64_t *out,
+                    ms_stream_t stream);
+
+/*
  * JSON-grammar allowed-token mask: bit t of a row is
  * JSONLogitsProcessor.is_valid_prefix(prefix + vocab[t])
  * (miniserve/sampler.py:139-148; the allowed_token_ids(partial, vocab) the

@@ -35,6 +35,19 @@ SIGNATURES = {
                                          _I64, _P, _P, _P, _P]),
     "ms_shard_candidates": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
                                            _I64, ctypes.c_int32, _P, _P]),
+    "ms_nucleus_hist_words": (_I64, []),
+    "ms_nucleus_record_words": (_I64, []),
+    "ms_nucleus_cut_words": (_I64, []),
+    "ms_nucleus_segments": (_I64, []),
+    "ms_nucleus_hist": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P,
+                                       ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P]),
+    "ms_nucleus_bracket": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _P, _P]),
+    "ms_nucleus_classify": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _P,
+                                           ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P]),
+    "ms_nucleus_cut": (ctypes.c_int, [_P, ctypes.c_int32, _P, _P, _P, _I64, _I64, _P, ctypes.c_int32, _P, _P, _P,
+                                      _P, _P]),
+    "ms_nucleus_draw": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _P,
+                                       ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, ctypes.c_int32, _P, _P]),
     "ms_mask_from_logits": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P]),
     "ms_shard_record_words": (_I64, [ctypes.c_int32]),
     "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,

@@ -21,6 +21,7 @@
 #include "ms_hook.cuh"
 #include "ms_json.cuh"
 #include "ms_shard.cuh"
+#include "ms_nucleus.cuh"
 #include "ms_stream.cuh"
 
 namespace {
@@ -228,6 +229,144 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;
+}
+
+int64_t ms_nucleus_hist_words(void) { return ms::kNuBins; }
+int64_t ms_nucleus_record_words(void) { return ms::kNuRecWords; }
+int64_t ms_nucleus_cut_words(void) { return ms::kNuCutWords; }
+int64_t ms_nucleus_segments(void) { return ms::kNuSegs; }
+
+namespace {
+// the dynamic shared memory of the histogram and cut kernels (once per device)
+cudaError_t nucleus_attrs() {
+  static std::atomic<int> ready[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (ready[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  const int hbytes = ms::kNuBins * (int)sizeof(uint32_t);
+  e = cudaFuncSetAttribute(ms::ms_nu_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sizeof(ms::NuCutShared));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(ms::ms_nu_hist_kernel<MS_DTYPE_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, hbytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(ms::ms_nu_hist_kernel<MS_DTYPE_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             hbytes);
+  if (e == cudaSuccess) ready[dev].store(1, std::memory_order_release);
+  return e;
+}
+
+int nucleus_check(int dtype, int64_t Vloc, int64_t ld, const uint32_t *mask, int64_t mask_ld, int64_t F, int64_t B,
+                  int32_t nranks, int32_t kmax) {
+  if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
+  if (Vloc < 1 || ld < Vloc || F < 0 || F > 0x7FFFFFFFll || B < 1 || B > 0x7FFFFFFFll || nranks < 1 || kmax < 1 ||
+      kmax > ms::kMgTopK)
+    return MS_E_INVALID;
+  if (mask && mask_ld < (Vloc + 31) / 32) return MS_E_INVALID;
+  if (Vloc > ms::kNuMaxSlice || nranks > ms::kMaxNuRanks) return MS_E_UNSUPPORTED;
+  return MS_OK;
+}
+}  // namespace
+
+int ms_nucleus_hist(const void *logits, int dtype, int64_t Vloc, int64_t ld, const uint32_t *mask, int64_t mask_ld,
+                    const int32_t *rows, int64_t F, int64_t B, int64_t V, const uint32_t *records, int32_t nranks,
+                    int32_t kmax, const double *temperature, const double *top_p, uint32_t *hist,
+                    ms_stream_t stream) {
+  int rc = nucleus_check(dtype, Vloc, ld, mask, mask_ld, F, B, nranks, kmax);
+  if (rc != MS_OK) return rc;
+  if (V < Vloc) return MS_E_INVALID;
+  if (V > 0x7FFFFFFFll / 16) return MS_E_UNSUPPORTED;  // the histogram scale stays >= 16
+  if (F == 0) return MS_OK;
+  if (!logits || !rows || !records || !temperature || !top_p || !hist) return MS_E_INVALID;
+  cudaError_t e = nucleus_attrs();
+  if (e != cudaSuccess) return cuda_fail(e);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::NuSlice sl{logits, Vloc, ld, 0, mask, mask_ld};
+  const ms::NuRows q{rows, (int)F, (int)B, records, nranks, kmax, temperature, top_p, nullptr};
+  const size_t hb = (size_t)ms::kNuBins * sizeof(uint32_t);
+  if (dtype == MS_DTYPE_F32) ms::ms_nu_hist_kernel<MS_DTYPE_F32><<<(unsigned)F, ms::kNuThreads, hb, s>>>(sl, q, V, hist);
+  else ms::ms_nu_hist_kernel<MS_DTYPE_BF16><<<(unsigned)F, ms::kNuThreads, hb, s>>>(sl, q, V, hist);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_nucleus_bracket(const uint32_t *hist, const int32_t *rows, int64_t F, int64_t V, const double *top_p,
+                       int32_t *bracket, ms_stream_t stream) {
+  if (F < 0 || F > 0x7FFFFFFFll || V < 1) return MS_E_INVALID;
+  if (V > 0x7FFFFFFFll / 16) return MS_E_UNSUPPORTED;
+  if (F == 0) return MS_OK;
+  if (!hist || !rows || !top_p || !bracket) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::NuRows q{rows, (int)F, 0, nullptr, 0, 0, nullptr, top_p, nullptr};
+  ms::ms_nu_bracket_kernel<<<(unsigned)F, ms::kNuThreads, 0, s>>>(hist, q, V, bracket);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_nucleus_classify(const void *logits, int dtype, int64_t Vloc, int64_t ld, int64_t v0, const uint32_t *mask,
+                        int64_t mask_ld, const int32_t *rows, int64_t F, int64_t B, const uint32_t *records,
+                        int32_t nranks, int32_t kmax, const double *temperature, const int32_t *bracket,
+                        uint32_t *entries, double *segments, ms_stream_t stream) {
+  int rc = nucleus_check(dtype, Vloc, ld, mask, mask_ld, F, B, nranks, kmax);
+  if (rc != MS_OK) return rc;
+  if (v0 < 0 || v0 + Vloc > 0x7FFFFFFFll) return MS_E_INVALID;
+  if (F == 0) return MS_OK;
+  if (!logits || !rows || !records || !temperature || !bracket || !entries || !segments) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::NuSlice sl{logits, Vloc, ld, v0, mask, mask_ld};
+  const ms::NuRows q{rows, (int)F, (int)B, records, nranks, kmax, temperature, nullptr, nullptr};
+  if (dtype == MS_DTYPE_F32)
+    ms::ms_nu_classify_kernel<MS_DTYPE_F32><<<(unsigned)F, ms::kNuThreads, 0, s>>>(sl, q, bracket, entries,
+                                                                                  segments);
+  else
+    ms::ms_nu_classify_kernel<MS_DTYPE_BF16><<<(unsigned)F, ms::kNuThreads, 0, s>>>(sl, q, bracket, entries,
+                                                                                   segments);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_nucleus_cut(const uint32_t *entries, int32_t nranks, const int64_t *bounds, const int32_t *bracket,
+                   const int32_t *rows, int64_t F, int64_t B, const uint32_t *records, int32_t kmax,
+                   const double *temperature, const double *top_p, const double *uniforms, uint32_t *cut,
+                   ms_stream_t stream) {
+  if (F < 0 || F > 0x7FFFFFFFll || B < 1 || B > 0x7FFFFFFFll || nranks < 1 || kmax < 1 || kmax > ms::kMgTopK)
+    return MS_E_INVALID;
+  if (nranks > ms::kMaxNuRanks) return MS_E_UNSUPPORTED;
+  if (F == 0) return MS_OK;
+  if (!entries || !bounds || !bracket || !rows || !records || !temperature || !top_p || !uniforms || !cut)
+    return MS_E_INVALID;
+  cudaError_t e = nucleus_attrs();
+  if (e != cudaSuccess) return cuda_fail(e);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::NuRows q{rows, (int)F, (int)B, records, nranks, kmax, temperature, top_p, uniforms};
+  ms::ms_nu_cut_kernel<<<(unsigned)F, ms::kNuThreads, sizeof(ms::NuCutShared), s>>>(entries, bounds, bracket, q,
+                                                                                    cut);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_nucleus_draw(const void *logits, int dtype, int64_t Vloc, int64_t ld, int64_t v0, const uint32_t *mask,
+                    int64_t mask_ld, const int32_t *rows, int64_t F, int64_t B, const uint32_t *records,
+                    int32_t nranks, int32_t kmax, const double *temperature, const uint32_t *cut,
+                    const uint32_t *entries, const double *segments, int32_t rank, int64_t *out,
+                    ms_stream_t stream) {
+  int rc = nucleus_check(dtype, Vloc, ld, mask, mask_ld, F, B, nranks, kmax);
+  if (rc != MS_OK) return rc;
+  if (v0 < 0 || v0 + Vloc > 0x7FFFFFFFll || rank < 0 || rank >= nranks) return MS_E_INVALID;
+  if (F == 0) return MS_OK;
+  if (!logits || !rows || !records || !temperature || !cut || !entries || !segments || !out) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::NuSlice sl{logits, Vloc, ld, v0, mask, mask_ld};
+  const ms::NuRows q{rows, (int)F, (int)B, records, nranks, kmax, temperature, nullptr, nullptr};
+  if (dtype == MS_DTYPE_F32)
+    ms::ms_nu_draw_kernel<MS_DTYPE_F32><<<(unsigned)F, ms::kNuThreads, 0, s>>>(sl, q, cut, entries, segments, rank,
+                                                                              out);
+  else
+    ms::ms_nu_draw_kernel<MS_DTYPE_BF16><<<(unsigned)F, ms::kNuThreads, 0, s>>>(sl, q, cut, entries, segments, rank,
+                                                                               out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
 
 int64_t ms_json_state_words(void) { return ms::kJsonStateWords; }

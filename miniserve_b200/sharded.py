@@ -52,8 +52,10 @@ def choose_kmax(top_k: Sequence[int], temperature: Sequence[float],
             continue
         if 2 <= k <= KMAX_LIMIT and (V is None or k < V):
             need = max(need, int(k))
-        elif p < 1.0 and (k == 0 or (V is not None and k >= V)):
-            need = max(need, KMAX_NUCLEUS)
+        elif k == 0 or (V is not None and k >= V):
+            # no top-k: the record carries the slice's maximum and total (and,
+            # for top-p rows, the top KMAX_NUCLEUS candidates)
+            need = max(need, KMAX_NUCLEUS if p < 1.0 else 2)
     return need
 
 
@@ -79,6 +81,24 @@ def exchange_records(records, group=None):
                       device=records.device)
     dist.all_gather_into_tensor(out, records.contiguous(), group=group)
     return out.view((world,) + tuple(records.shape))
+
+
+def _world(group=None) -> Tuple[int, int]:
+    """(world size, rank) of the group, (1, 0) without a process group."""
+    import torch.distributed as dist
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _all_reduce(t, op: str, group=None):
+    """In-place all-reduce ('sum' or 'max') over the group; the identity
+    without a process group."""
+    import torch.distributed as dist
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return t
+    dist.all_reduce(t, op=dist.ReduceOp.SUM if op == "sum" else dist.ReduceOp.MAX, group=group)
+    return t
 
 
 def gather_rows(logits_slice, rows, V: int, group=None):
@@ -107,6 +127,10 @@ class ShardedSampler:
         self.V = int(V)
         self.group = group
         self._single = Sampler()
+        # rows of the last call finished by the distributed nucleus, and rows
+        # that took the full-row path (gathered logits)
+        self.last_nucleus_rows = 0
+        self.last_full_rows = 0
 
     def sample(self, logits_slice, v0: int, temperature=1.0, top_k=0, top_p=1.0,
                uniforms=None, seeds: Optional[Sequence[Optional[int]]] = None,
@@ -180,7 +204,22 @@ class ShardedSampler:
             if events is not None:
                 events[3].record(cur)
         flagged = (status & (_lib.MS_ROW_UNSUPPORTED | _lib.MS_ROW_NONFINITE)) != 0
-        if int(flagged.sum()):  # the statuses are identical on every rank: so is this branch
+        # rows without top-k the records could not settle: the distributed
+        # nucleus (no logits exchanged); the statuses are identical on every
+        # rank, so are these counts and branches
+        nuc = flagged & ((status & _lib.MS_ROW_NONFINITE) == 0) & ((K <= 0) | (K >= self.V))
+        n_flagged, n_nuc = (int(v) for v in torch.stack([flagged.sum(), nuc.sum()]).tolist())
+        self.last_nucleus_rows = 0
+        if (n_nuc and kmax >= 2 and Vloc <= NUCLEUS_MAX_SLICE and self.V <= NUCLEUS_MAX_V
+                and allrec.shape[0] <= NUCLEUS_MAX_RANKS):
+            rows = nuc.nonzero().flatten()
+            done = self._nucleus(logits_slice, dtype, v0, rows, allrec, kmax, T, P, U, mask_ptr, mask_ld,
+                                 tokens, probs, status)
+            flagged[rows] = ~done
+            n_flagged, n_done = (int(v) for v in torch.stack([flagged.sum(), done.sum()]).tolist())
+            self.last_nucleus_rows = n_done
+        self.last_full_rows = n_flagged
+        if n_flagged:
             rows = flagged.nonzero().flatten()
             full = gather_rows(logits_slice, rows, self.V, self.group)
             fmask = None
@@ -189,6 +228,64 @@ class ShardedSampler:
             t2, p2, s2 = self._single.sample_batch(full, T[rows], K[rows], P[rows], uniforms=U[rows], mask=fmask)
             tokens[rows], probs[rows], status[rows] = t2, p2, s2
         return tokens, probs, status
+
+
+    def _nucleus(self, logits_slice, dtype, v0, rows, allrec, kmax, T, P, U, mask_ptr, mask_ld, tokens, probs,
+                 status):
+        """Rows without top-k that the candidate records could not settle:
+        histogram all-reduce, bracket, classifying pass, all-gather of the
+        bracket's values, exact cut, draw on the rank holding the target, max
+        all-reduce of the tokens (ms_nucleus_* in include/mssample.h).  Writes
+        the finished rows; returns which of ``rows`` it finished."""
+        torch = _torch()
+        L = _lib.lib()
+        dev = logits_slice.device
+        B, Vloc = logits_slice.shape
+        F = int(rows.numel())
+        world, rank = _world(self.group)
+        nranks = int(allrec.shape[0])
+        rows32 = rows.to(torch.int32).contiguous()
+        hist = torch.empty((F, int(L.ms_nucleus_hist_words())), dtype=torch.int32, device=dev)
+        bracket = torch.empty((F, 2), dtype=torch.int32, device=dev)
+        ent = torch.empty((F, int(L.ms_nucleus_record_words())), dtype=torch.int32, device=dev)
+        cut = torch.empty((F, int(L.ms_nucleus_cut_words())), dtype=torch.int32, device=dev)
+        segs = torch.empty((F, int(L.ms_nucleus_segments())), dtype=torch.float64, device=dev)
+        out = torch.empty((F, 2), dtype=torch.int64, device=dev)
+        bounds = torch.tensor([shard_bounds(self.V, world, r)[0] for r in range(world)] + [self.V],
+                              dtype=torch.int64, device=dev)
+        ld = logits_slice.stride(0)
+        x = logits_slice.data_ptr()
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _lib.check(L.ms_nucleus_hist(x, dtype, Vloc, ld, mask_ptr, mask_ld, rows32.data_ptr(), F, B, self.V,
+                                         allrec.data_ptr(), nranks, kmax, T.data_ptr(), P.data_ptr(),
+                                         hist.data_ptr(), stream), "ms_nucleus_hist")
+            _all_reduce(hist, "sum", self.group)
+            _lib.check(L.ms_nucleus_bracket(hist.data_ptr(), rows32.data_ptr(), F, self.V, P.data_ptr(),
+                                            bracket.data_ptr(), stream), "ms_nucleus_bracket")
+            _lib.check(L.ms_nucleus_classify(x, dtype, Vloc, ld, int(v0), mask_ptr, mask_ld, rows32.data_ptr(), F,
+                                             B, allrec.data_ptr(), nranks, kmax, T.data_ptr(), bracket.data_ptr(),
+                                             ent.data_ptr(), segs.data_ptr(), stream), "ms_nucleus_classify")
+            allent = exchange_records(ent, self.group)
+            _lib.check(L.ms_nucleus_cut(allent.data_ptr(), nranks, bounds.data_ptr(), bracket.data_ptr(),
+                                        rows32.data_ptr(), F, B, allrec.data_ptr(), kmax, T.data_ptr(),
+                                        P.data_ptr(), U.data_ptr(), cut.data_ptr(), stream), "ms_nucleus_cut")
+            _lib.check(L.ms_nucleus_draw(x, dtype, Vloc, ld, int(v0), mask_ptr, mask_ld, rows32.data_ptr(), F, B,
+                                         allrec.data_ptr(), nranks, kmax, T.data_ptr(), cut.data_ptr(),
+                                         allent.data_ptr(), segs.data_ptr(), rank, out.data_ptr(), stream),
+                       "ms_nucleus_draw")
+            _all_reduce(out, "max", self.group)
+        # written on the device, without reading `done` back
+        done = (cut[:, 3] == 0) & (out[:, 0] >= 0)
+        tokens[rows] = torch.where(done, out[:, 0], tokens[rows])
+        probs[rows] = torch.where(done, out[:, 1].to(torch.int32).view(torch.float32), probs[rows])
+        status[rows] = torch.where(done, torch.zeros_like(status[rows]), status[rows])
+        return done
+
+
+NUCLEUS_MAX_SLICE = 1 << 20  # longest slice the distributed nucleus takes
+NUCLEUS_MAX_V = (2**31 - 1) // 16  # largest vocabulary (histogram scale >= 16)
+NUCLEUS_MAX_RANKS = 256
 
 
 def _full_mask(mask, rows, Vloc: int, V: int, group):

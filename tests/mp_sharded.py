@@ -29,13 +29,20 @@ def main():
         B, V = b.logits.shape
         K = b.top_k.copy()
         T = b.temperature.copy()
-        K[:3] = [0, 1, 300]          # a fallback row, a greedy row, a fallback row
+        P = b.top_p.copy()
+        K[:3] = [0, 1, 300]          # a distributed-nucleus row, a greedy row, a full-row-path row
         T[3] = 0.0
+        K[4:12] = 0                  # rows without top-k: top_p 1 (the whole-vocabulary draw) and
+        P[4:8] = 1.0                 # high-temperature nuclei wider than the candidates
+        T[8:12] = 1.5
         v0, v1 = sharded.shard_bounds(V, world, rank)
         part = torch.from_numpy(np.ascontiguousarray(b.logits[:, v0:v1])).cuda()
         s = sharded.ShardedSampler(V)
-        tok, prob, st = s.sample(part, v0, T, K, b.top_p, uniforms=b.uniforms)
+        tok, prob, st = s.sample(part, v0, T, K, P, uniforms=b.uniforms)
         torch.cuda.synchronize()
+        # rows 0 and 4-11 (no top-k) finish without logits crossing ranks;
+        # row 2 (top_k 300, above the record width) takes the full-row path
+        assert s.last_full_rows <= 1 and s.last_nucleus_rows >= 4, (s.last_full_rows, s.last_nucleus_rows)
         tok = tok.cpu().numpy()
         # every rank must hold the same tokens
         t_all = [torch.empty(B, dtype=torch.int64, device="cuda") for _ in range(world)]
@@ -43,7 +50,7 @@ def main():
         same = all(np.array_equal(t.cpu().numpy(), tok) for t in t_all)
         if rank == 0:
             from parity import compare
-            compare(tok, prob.cpu().numpy().astype(np.float64), st.cpu().numpy(), b.logits, T, K, b.top_p,
+            compare(tok, prob.cpu().numpy().astype(np.float64), st.cpu().numpy(), b.logits, T, K, P,
                     b.uniforms, label=f"nccl x{world}")
             assert same, "ranks disagree"
             print("sharded ok", world, flush=True)

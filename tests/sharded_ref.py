@@ -104,3 +104,93 @@ def sparse_rows(allrec, B, V, kmax):
             ids = allrec[r, b, 2 + kmax:2 + kmax + m].astype(np.int64)
             rows[b, ids] = key_to_f32(allrec[r, b, 2:2 + m])
     return rows, st
+
+
+NU_BINS, NU_RANGE = 16384, 20.0
+
+
+def np_distributed_nucleus(slices, bounds, t, p, u, V):
+    """Restatement of the distributed nucleus (ms_nucleus_* in
+    include/mssample.h) for one row without top-k, in float64: the ranks'
+    fixed-point histograms over (M - v) / T summed, the bracket of bins that
+    must hold the top-p crossing, each slice's mass above the bracket and the
+    bracket's values, the exact cut on the ranked bracket values, each rank's
+    kept mass, the owner of the index-order target and its draw.  `slices`:
+    each rank's fp32 values of the row.  Returns the token, or None when the
+    bracket cannot place the crossing (the full-row path)."""
+    M = max(float(s[s > -np.inf].max()) for s in slices if np.any(s > -np.inf))
+    xs = NU_BINS / (NU_RANGE * t)
+
+    def weights_bins(s):
+        v = s.astype(np.float64)
+        fin = v > -np.inf
+        w = np.where(fin, np.exp((np.where(fin, v, M) - M) / t), 0.0)
+        z = (M - np.where(fin, v, -1e300)) * xs
+        b = np.where(z < NU_BINS, np.floor(np.minimum(z, NU_BINS)), NU_BINS).astype(np.int64)
+        return fin, w, b
+
+    if p < 1.0:
+        # each value adds round(scale * its weight relative to its bin's upper
+        # edge); bin b then carries e^-(b dz) * hist[b] / scale
+        scale = float(min(65535, (2**31 - 1) // V))
+        dz = NU_RANGE / NU_BINS
+        hist = np.zeros(NU_BINS, np.float64)
+        for s in slices:
+            fin, w, b = weights_bins(s)
+            sel = fin & (b < NU_BINS)
+            z = (M - s.astype(np.float64)[sel]) / t
+            q = np.rint(scale * np.exp(-(z / dz - b[sel]) * dz))
+            np.add.at(hist, b[sel], q)
+        c = np.cumsum(hist * np.exp(-np.arange(NU_BINS) * dz))
+        Z = c[-1]
+        tol = 2.0 * (0.51 / scale + 1e-5) * Z
+        lo = np.nonzero(c > p * Z - tol)[0]
+        hi = np.nonzero(c >= p * Z + tol)[0]
+        b_lo = int(lo[0]) if lo.size else NU_BINS
+        b_hi = int(hi[0]) if hi.size else NU_BINS
+    else:
+        b_lo = b_hi = NU_BINS + 1
+    above, total, ents = [], [], []
+    for r, s in enumerate(slices):
+        fin, w, b = weights_bins(s)
+        above.append(w[fin & (b < b_lo)].sum())
+        total.append(w[fin].sum())
+        sel = np.nonzero(fin & (b >= b_lo) & (b <= b_hi))[0]
+        ents += [(float(s[i]), bounds[r] + int(i), w[i]) for i in sel]
+    A, Z = sum(above), sum(total)
+    ents.sort(key=lambda e: (-e[0], e[1]))
+    kept_ids = None  # None: every value kept
+    if p < 1.0:
+        need = p * Z
+        run = A + np.cumsum([e[2] for e in ents]) if ents else np.zeros(0)
+        j = np.nonzero(run >= need)[0]
+        if A >= need or (not j.size and b_hi < NU_BINS):
+            return None
+        if j.size:
+            kept_ids = {e[1]: e[2] for e in ents[: int(j[0]) + 1]}
+    kr = []
+    for r in range(len(slices)):
+        if kept_ids is None:
+            kr.append(total[r])
+        else:
+            kr.append(above[r] + sum(w for i, w in kept_ids.items() if bounds[r] <= i < bounds[r + 1]))
+    K = sum(kr)
+    target = u * K
+    pre, owner = 0.0, None
+    for r, k in enumerate(kr):
+        if pre + k >= target and (k > 0 or not u > 0.0):
+            owner = r
+            break
+        pre += k
+    if owner is None:
+        return V - 1
+    s = slices[owner]
+    fin, w, b = weights_bins(s)
+    if kept_ids is not None:
+        ids = bounds[owner] + np.arange(len(s))
+        cutv, cuti = min(((e[0], e[1]) for e in ents if e[1] in kept_ids), key=lambda e: (e[0], -e[1]))
+        keep = fin & ((s.astype(np.float64) > cutv) | ((s.astype(np.float64) == cutv) & (ids <= cuti)))
+        w = np.where(keep, w, 0.0)
+    c = np.cumsum(w)
+    hit = np.nonzero(c >= target - pre)[0]
+    return int(bounds[owner] + hit[0]) if hit.size else int(bounds[owner] + len(s) - 1)

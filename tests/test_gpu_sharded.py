@@ -153,6 +153,133 @@ def test_nucleus_rows_from_records(torch, world):
                 label="sharded sampler, nucleus rows")
 
 
+def emulate_nucleus(torch, x, T, K, P, U, world):
+    """The merge, then the distributed nucleus for the rows it flags, with
+    `world` ranks emulated on one GPU: the histogram all-reduce is a sum over
+    the ranks' histograms, the entries all-gather a stack, the token all-reduce
+    a maximum.  Returns (tokens, probs, status, rows the nucleus finished)."""
+    from miniserve_b200 import _lib, sharded
+    L = _lib.lib()
+    B, V = x.shape
+    kmax = sharded.choose_kmax(list(K), list(T), list(P), V)
+    W = sharded.record_words(kmax)
+    xt = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    dev = xt.device
+    Tt = torch.tensor(T, dtype=torch.float64, device=dev)
+    Kt = torch.tensor(K, dtype=torch.int32, device=dev)
+    Pt = torch.tensor(P, dtype=torch.float64, device=dev)
+    Ut = torch.tensor(U, dtype=torch.float64, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    recs = torch.empty((world, B, W), dtype=torch.int32, device=dev)
+    bnd = [sharded.shard_bounds(V, world, r) for r in range(world)]
+    for r, (v0, v1) in enumerate(bnd):
+        part = xt[:, v0:v1]
+        assert L.ms_shard_candidates(part.data_ptr(), 0, B, v1 - v0, part.stride(0), v0, V, Tt.data_ptr(),
+                                     Kt.data_ptr(), None, 0, kmax, recs[r].data_ptr(), s) == 0
+    tok = torch.empty(B, dtype=torch.int64, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+    assert L.ms_shard_merge(recs.data_ptr(), world, B, kmax, V, Tt.data_ptr(), Kt.data_ptr(), Pt.data_ptr(),
+                            Ut.data_ptr(), tok.data_ptr(), prob.data_ptr(), st.data_ptr(), s) == 0
+    nuc = ((st & 8) != 0) & ((Kt <= 0) | (Kt >= V))
+    rows = nuc.nonzero().flatten().to(torch.int32).contiguous()
+    F = int(rows.numel())
+    if F:
+        NB, RW, CW = (int(L.ms_nucleus_hist_words()), int(L.ms_nucleus_record_words()),
+                      int(L.ms_nucleus_cut_words()))
+        hist = torch.zeros((F, NB), dtype=torch.int32, device=dev)
+        for r, (v0, v1) in enumerate(bnd):
+            h = torch.empty((F, NB), dtype=torch.int32, device=dev)
+            part = xt[:, v0:v1]
+            assert L.ms_nucleus_hist(part.data_ptr(), 0, v1 - v0, part.stride(0), None, 0, rows.data_ptr(), F, B, V,
+                                     recs.data_ptr(), world, kmax, Tt.data_ptr(), Pt.data_ptr(), h.data_ptr(),
+                                     s) == 0
+            hist += h
+        bracket = torch.empty((F, 2), dtype=torch.int32, device=dev)
+        assert L.ms_nucleus_bracket(hist.data_ptr(), rows.data_ptr(), F, V, Pt.data_ptr(), bracket.data_ptr(),
+                                    s) == 0
+        ent = torch.empty((world, F, RW), dtype=torch.int32, device=dev)
+        segs = torch.empty((world, F, int(L.ms_nucleus_segments())), dtype=torch.float64, device=dev)
+        for r, (v0, v1) in enumerate(bnd):
+            part = xt[:, v0:v1]
+            assert L.ms_nucleus_classify(part.data_ptr(), 0, v1 - v0, part.stride(0), v0, None, 0, rows.data_ptr(),
+                                         F, B, recs.data_ptr(), world, kmax, Tt.data_ptr(), bracket.data_ptr(),
+                                         ent[r].data_ptr(), segs[r].data_ptr(), s) == 0
+        bounds = torch.tensor([a for a, _ in bnd] + [V], dtype=torch.int64, device=dev)
+        cut = torch.empty((F, CW), dtype=torch.int32, device=dev)
+        assert L.ms_nucleus_cut(ent.data_ptr(), world, bounds.data_ptr(), bracket.data_ptr(), rows.data_ptr(), F, B,
+                                recs.data_ptr(), kmax, Tt.data_ptr(), Pt.data_ptr(), Ut.data_ptr(), cut.data_ptr(),
+                                s) == 0
+        out = torch.full((F, 2), -1, dtype=torch.int64, device=dev)
+        for r, (v0, v1) in enumerate(bnd):
+            o = torch.empty((F, 2), dtype=torch.int64, device=dev)
+            part = xt[:, v0:v1]
+            assert L.ms_nucleus_draw(part.data_ptr(), 0, v1 - v0, part.stride(0), v0, None, 0, rows.data_ptr(), F,
+                                     B, recs.data_ptr(), world, kmax, Tt.data_ptr(), cut.data_ptr(), ent.data_ptr(),
+                                     segs[r].data_ptr(), r, o.data_ptr(), s) == 0
+            out = torch.maximum(out, o)
+        done = (cut[:, 3] == 0) & (out[:, 0] >= 0)
+        r = rows.long()[done]
+        tok[r] = out[done, 0]
+        prob[r] = out[done, 1].to(torch.int32).view(torch.float32)
+        st[r] = 0
+        finished = r.cpu().numpy()
+    else:
+        finished = np.zeros(0, np.int64)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy(), prob.cpu().numpy().astype(np.float64), st.cpu().numpy(), finished
+
+
+def _wide_rows(seed, B, V):
+    rng = np.random.default_rng(seed)
+    base = -1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))
+    x = np.stack([(base[rng.permutation(V)] + rng.normal(0, 0.5, V)).astype(np.float32) for _ in range(B)])
+    x[B // 2:] = rng.normal(0.0, 2.0, (B - B // 2, V)).astype(np.float32)  # Gaussian rows: wide nuclei
+    T = rng.choice([0.4, 0.7, 1.0, 1.4], B)
+    K = np.zeros(B, np.int32)
+    K[::7] = V + 3
+    P = 0.5 + 0.49 * rng.random(B)
+    P[1::5] = 1.0   # top_p 1 without top-k: the draw over the whole vocabulary
+    U = rng.random(B)
+    U[2] = 0.0
+    U[4] = 1.0 - 1e-12
+    return x, T, K, P, U
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_distributed_nucleus_emulated(torch, world):
+    """Rows without top-k that the records cannot settle (nuclei wider than
+    the candidates, top_p 1) finish through the histogram all-reduce, the
+    bracket exchange and the owner's draw, with no logits exchanged: every
+    row matches the oracle on the full row."""
+    B, V = 48, 65536
+    x, T, K, P, U = _wide_rows(31, B, V)
+    tok, prob, st, finished = emulate_nucleus(torch, x, T, K, P, U, world)
+    flagged_by_merge = len(finished)
+    assert flagged_by_merge >= B // 3, flagged_by_merge
+    assert np.all(st == 0), st
+    compare(tok, prob, st, x, T, K, P, U, label=f"distributed nucleus x{world}")
+
+
+def test_distributed_nucleus_through_sharded_sampler(torch):
+    """ShardedSampler on one process (world 1): the k=0 rows go through the
+    distributed nucleus, not the full-row path; bf16 logits and a mask too."""
+    from miniserve_b200.sharded import ShardedSampler
+    B, V = 24, 40000
+    x, T, K, P, U = _wide_rows(32, B, V)
+    xb = ((x.view(np.uint32) >> 16).astype(np.uint32) << 16).view(np.float32)
+    rng = np.random.default_rng(4)
+    mask = rng.integers(0, 2**32, (B, V // 32), dtype=np.uint64).astype(np.uint32)  # V % 32 == 0
+    s = ShardedSampler(V)
+    xt = torch.from_numpy(xb).cuda().to(torch.bfloat16)
+    mt = torch.from_numpy(mask.view(np.int32)).cuda()
+    t2, p2, s2 = s.sample(xt, 0, T, K, P, uniforms=U, mask=mt)
+    torch.cuda.synchronize()
+    assert s.last_full_rows == 0 and s.last_nucleus_rows > 0, (s.last_full_rows, s.last_nucleus_rows)
+    compare(t2.cpu().numpy(), p2.cpu().numpy().astype(np.float64), s2.cpu().numpy(), xb, T, K, P, U,
+            bf16=False, mask=mask, label="sharded sampler bf16 + mask, nucleus rows")
+
+
 def test_nccl_two_ranks(torch):
     n = torch.cuda.device_count()
     if n < 2:

@@ -24,7 +24,9 @@ def test_shard_bounds_partition():
 
 def test_choose_kmax():
     assert sharded.choose_kmax([0, 1, 50, 20], [1.0, 1.0, 0.9, 0.0]) == 50
-    assert sharded.choose_kmax([0, 300], [1.0, 1.0]) == 1
+    # a row without top-k at top_p 1 needs the slice's maximum and total in its record
+    assert sharded.choose_kmax([0, 300], [1.0, 1.0]) == 2
+    assert sharded.choose_kmax([300, 1], [1.0, 1.0]) == 1
     assert sharded.record_words(50) == 104
     assert sharded.choose_kmax([0, 20], [1.0, 1.0], [0.9, 1.0], 1000) == sharded.KMAX_NUCLEUS
     assert sharded.choose_kmax([0, 20], [1.0, 1.0], [1.0, 1.0], 1000) == 20
@@ -119,3 +121,32 @@ def test_nucleus_decomposition(world):
         if mp[b] >= 1e-6 and mu[b] >= 1e-6:
             assert t == o_tok[b], (b, t, o_tok[b])
     assert settled >= B // 3
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_distributed_nucleus_rule(world):
+    """The distributed nucleus's rule (histogram bracket, exact cut on the
+    bracket's values, owner of the index-order target), restated in numpy:
+    its token is the oracle's token on the full row for every row outside the
+    1e-6 boundary band, with nuclei far wider than any candidate record, top_p
+    1 rows, r == 0 and r near 1."""
+    rng = np.random.default_rng(41)
+    B, V = 24, 8192
+    base = -1.1 * np.log(np.arange(1, V + 1, dtype=np.float64))
+    x = np.stack([(base[rng.permutation(V)] + rng.normal(0, 0.5, V)).astype(np.float32) for _ in range(B)])
+    x[B // 2:] = rng.normal(0.0, 2.0, (B - B // 2, V)).astype(np.float32)
+    x[5, 1000:1100] = -np.inf
+    T = rng.choice([0.4, 1.0, 1.5], B)
+    K = np.zeros(B, np.int32)
+    P = 0.5 + 0.49 * rng.random(B)
+    P[1::4] = 1.0
+    U = rng.random(B)
+    U[2], U[3] = 0.0, 1.0 - 1e-12
+    bounds = [sharded.shard_bounds(V, world, r)[0] for r in range(world)] + [V]
+    o_tok, _, _, mp, mu = oracle.c_sample(x, T, K, P, U)
+    for b in range(B):
+        slices = [x[b, bounds[r]:bounds[r + 1]] for r in range(world)]
+        t = sharded_ref.np_distributed_nucleus(slices, bounds, T[b], P[b], U[b], V)
+        assert t is not None, b
+        if mp[b] >= 1e-6 and mu[b] >= 1e-6:
+            assert t == o_tok[b], (b, t, o_tok[b])
