@@ -1459,10 +1459,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     //
     // First pass: tau is the m-th largest value of chunk 0 (to 16 bits).
     // Chunk 0 holds lam = k * n0 / V of the row's top-k set on average; with
-    // m = lam + 4 sqrt(lam) + 4 the row's k-th largest value lies below tau
-    // only when chunk 0 holds m members of that set (a Poisson tail below
-    // 1e-4 for a row in random order).  Every value >= tau is a candidate, so
-    // at least k candidates prove that tau is low enough; with fewer, a
+    // m = lam + 3 sqrt(lam) + 2 the row's k-th largest value lies below tau
+    // only when chunk 0 holds m members of that set (a Poisson tail near 1e-3
+    // for a row in random order; such a row takes a second pass).  Every
+    // value >= tau is a candidate, so at least k candidates prove that tau is
+    // low enough; with fewer, a
     // second pass starts over with tau rising to lower bounds of the k-th
     // largest from the lanes' running maxima (st_topk_bound) and the buffer's
     // k-th largest (chunks 3 and 11).  A buffer that could overflow is cut to
@@ -1488,7 +1489,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     int msamp = k;
     if (r.nchunks > 1) {
       const double lam = (double)k * (double)n0 / (double)V;
-      msamp = (int)ceil(lam + 4.0 * sqrt(lam) + 4.0);
+      msamp = (int)ceil(lam + 3.0 * sqrt(lam) + 2.0);
     }
     msamp = min(msamp, n0);
     for (int attempt = 0;; ++attempt) {
