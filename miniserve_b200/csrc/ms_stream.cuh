@@ -1252,12 +1252,10 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
     }
   }
   if (sh.ptot[0] == B || sh.ptot[1] == B || sh.ptot[2] == B || sh.ptot[3] == B) return want;
-  int base[4];
-  base[0] = 0;
-  base[1] = sh.ptot[0];
-  base[2] = base[1] + sh.ptot[1];
-  base[3] = base[2] + sh.ptot[2];
-  int carry[4] = {0, 0, 0, 0};
+  // positions in (class, index) order: the class's first position, the rows
+  // of that class in earlier rounds (carry), in earlier warps of this round
+  // (a per-class prefix over the warps, four threads) and in earlier lanes
+  int b0 = 0, b1 = sh.ptot[0], b2 = b1 + sh.ptot[1], b3 = b2 + sh.ptot[2];  // bases plus carries
   int found = -1;
   const unsigned lt = (1u << lane) - 1u;
   for (int r0 = 0; r0 < B; r0 += kStThreads) {
@@ -1271,21 +1269,25 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
       if (cls == c) pre = __popc(m & lt);
     }
     __syncthreads();
-    int tot[4] = {0, 0, 0, 0};
+    if (tid < 4) {  // exclusive prefix over the warps of class tid, and its round total
+      int run = 0;
 #pragma unroll
-    for (int w = 0; w < kStWarps; ++w) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int v = sh.pick[w][c];
-        if (w < warp && c == cls) pre += v;
-        tot[c] += v;
+      for (int w = 0; w < kStWarps; ++w) {
+        const int v = sh.pick[w][tid];
+        sh.pick[w][tid] = run;
+        run += v;
       }
+      sh.bcast_i[4 + tid] = run;
     }
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      if (c == cls && base[c] + carry[c] + pre == want) found = r;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) carry[c] += tot[c];
+    __syncthreads();
+    if (cls >= 0) {
+      const int bc = cls == 0 ? b0 : cls == 1 ? b1 : cls == 2 ? b2 : b3;
+      if (bc + sh.pick[warp][cls] + pre == want) found = r;
+    }
+    b0 += sh.bcast_i[4];
+    b1 += sh.bcast_i[5];
+    b2 += sh.bcast_i[6];
+    b3 += sh.bcast_i[7];
     __syncthreads();
   }
   if (found >= 0) sh.bcast_i[0] = found;
