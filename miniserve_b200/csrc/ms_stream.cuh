@@ -115,8 +115,7 @@ struct StShared {
     } n;
   } w;
   uint32_t wbound[kStWarps];
-  int pick[kStWarps][4];  // row ordering: per-warp class counts
-  int ptot[4];
+  int pick[kStWarps][4];  // row ordering: per-warp class counts, then their prefix over the warps
   alignas(16) uint32_t sel[4][256];  // st_select_kth: one digit histogram per round
   unsigned long long full[kMaxStages];
   double r1d[2][64];  // one-barrier reductions (st_bsum and friends): two halves
@@ -1219,49 +1218,15 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   *joint = false;
   if (!a.pairs && (int)blockIdx.x >= B) return -1;
-  if (tid < 4) sh.ptot[tid] = 0;
-  __syncthreads();
-  int n0 = 0, n1 = 0, n2 = 0, n3 = 0;
-  for (int r = tid; r < B; r += kStThreads) {
-    const int c = st_row_class(a, r);
-    n0 += c == 0;
-    n1 += c == 1;
-    n2 += c == 2;
-    n3 += c == 3;
-  }
-  n0 = __reduce_add_sync(0xFFFFFFFFu, n0);
-  n1 = __reduce_add_sync(0xFFFFFFFFu, n1);
-  n2 = __reduce_add_sync(0xFFFFFFFFu, n2);
-  n3 = __reduce_add_sync(0xFFFFFFFFu, n3);
-  if (lane == 0) {
-    atomicAdd(&sh.ptot[0], n0);
-    atomicAdd(&sh.ptot[1], n1);
-    atomicAdd(&sh.ptot[2], n2);
-    atomicAdd(&sh.ptot[3], n3);
-  }
-  __syncthreads();
-  int want = blockIdx.x;
-  if (a.pairs) {
-    const int item = blockIdx.x >> 1, np = sh.ptot[0] <= a.pairs ? sh.ptot[0] : 0;
-    if (item < np) {
-      want = item;
-      *joint = true;
-    } else {
-      want = np + 2 * (item - np) + (int)st_crank();
-      if (want >= B) return -1;
-    }
-  }
-  if (sh.ptot[0] == B || sh.ptot[1] == B || sh.ptot[2] == B || sh.ptot[3] == B) return want;
-  // positions in (class, index) order: the class's first position, the rows
-  // of that class in earlier rounds (carry), in earlier warps of this round
-  // (a per-class prefix over the warps, four threads) and in earlier lanes
-  int b0 = 0, b1 = sh.ptot[0], b2 = b1 + sh.ptot[1], b3 = b2 + sh.ptot[2];  // bases plus carries
-  int found = -1;
   const unsigned lt = (1u << lane) - 1u;
-  for (int r0 = 0; r0 < B; r0 += kStThreads) {
+  // One round of up to kStThreads rows: the rows of each class in this warp
+  // and in earlier lanes (ballots), the per-class prefix over the warps and
+  // the round's class totals (four threads).  `pre` and `cls` describe this
+  // thread's row r0 + tid.
+  auto round = [&](int r0, int &cls, int &pre) {
     const int r = r0 + tid;
-    const int cls = r < B ? st_row_class(a, r) : -1;
-    int pre = 0;
+    cls = r < B ? st_row_class(a, r) : -1;
+    pre = 0;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const unsigned m = __ballot_sync(0xFFFFFFFFu, cls == c);
@@ -1269,7 +1234,7 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
       if (cls == c) pre = __popc(m & lt);
     }
     __syncthreads();
-    if (tid < 4) {  // exclusive prefix over the warps of class tid, and its round total
+    if (tid < 4) {  // exclusive prefix over the warps of class tid, and the round's total
       int run = 0;
 #pragma unroll
       for (int w = 0; w < kStWarps; ++w) {
@@ -1280,16 +1245,50 @@ __device__ int st_pick_row(StShared &sh, const SampleArgs &a, int B, bool *joint
       sh.bcast_i[4 + tid] = run;
     }
     __syncthreads();
+  };
+  // class totals (the first round already holds them when B <= kStThreads)
+  int cls = -1, pre = 0;
+  int t0 = 0, t1 = 0, t2 = 0, t3 = 0;
+  for (int r0 = 0; r0 < B; r0 += kStThreads) {
+    if (r0 > 0) __syncthreads();  // the previous round's totals are read
+    round(r0, cls, pre);
+    t0 += sh.bcast_i[4];
+    t1 += sh.bcast_i[5];
+    t2 += sh.bcast_i[6];
+    t3 += sh.bcast_i[7];
+  }
+  int want = blockIdx.x;
+  if (a.pairs) {
+    const int item = blockIdx.x >> 1, np = t0 <= a.pairs ? t0 : 0;
+    if (item < np) {
+      want = item;
+      *joint = true;
+    } else {
+      want = np + 2 * (item - np) + (int)st_crank();
+      if (want >= B) return -1;
+    }
+  }
+  if (t0 == B || t1 == B || t2 == B || t3 == B) return want;
+  // positions in (class, index) order: the class's first position, the rows
+  // of that class in earlier rounds, in earlier warps of this round and in
+  // earlier lanes
+  int b0 = 0, b1 = t0, b2 = t0 + t1, b3 = t0 + t1 + t2;
+  int found = -1;
+  for (int r0 = 0; r0 < B; r0 += kStThreads) {
+    if (B > kStThreads) {  // one round holds every row otherwise: its ballots are still in place
+      __syncthreads();
+      round(r0, cls, pre);
+    }
     if (cls >= 0) {
       const int bc = cls == 0 ? b0 : cls == 1 ? b1 : cls == 2 ? b2 : b3;
-      if (bc + sh.pick[warp][cls] + pre == want) found = r;
+      if (bc + sh.pick[warp][cls] + pre == want) found = r0 + tid;
     }
     b0 += sh.bcast_i[4];
     b1 += sh.bcast_i[5];
     b2 += sh.bcast_i[6];
     b3 += sh.bcast_i[7];
-    __syncthreads();
   }
+  __syncthreads();
   if (found >= 0) sh.bcast_i[0] = found;
   __syncthreads();
   return sh.bcast_i[0];
