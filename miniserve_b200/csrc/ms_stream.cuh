@@ -535,14 +535,15 @@ __device__ __forceinline__ bool st_stream(StShared &sh, const StRow &r, int c0, 
   return __syncthreads_and(ok) != 0;
 }
 
-// Start a pass over chunks [c0, c1) (their first copies) and read chunk c0
-// into x[8] without consuming it: st_stream(..., issued = true) then takes the
-// same copies.  Returns false when the copy timed out.  All threads.
+// Start a pass over chunks [c0, c1) (their first copies, unless `issued`) and
+// read chunk c0 into x[8] without consuming it: st_stream(..., issued = true)
+// then takes the same copies.  Returns false when the copy timed out.  All
+// threads.
 template <int DT>
 __device__ __forceinline__ bool st_peek(StShared &sh, const StRow &r, int c0, int c1, uint64_t pol, uint32_t ph,
-                                        float x[8]) {
+                                        float x[8], bool issued = false) {
   constexpr int S = st_nstages<DT>();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && !issued) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     for (int c = c0; c < c0 + S && c < c1; ++c) st_issue<DT>(sh, r, c, c - c0, pol);
   }
@@ -1313,19 +1314,64 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // every CTA of this grid has started: a programmatic dependent launch (the
   // pending-row pass) may begin launching
   asm volatile("griddepcontrol.launch_dependents;");
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  // the stage barriers first: the row ordering's barriers publish them
+  if (tid < st_nstages<DT>()) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
+  }
+  if (tid == 0) {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   bool joint;
   const int row = st_pick_row(sh, a, a.pairs ? a.rows : (int)gridDim.x, &joint);
   if (row < 0) return;
   const int crank = joint ? (int)st_crank() : 0;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
+  const int V = a.V;
+  StRow r;
+  r.g = reinterpret_cast<const char *>(a.logits) + (int64_t)row * a.ld * st_esz<DT>();
+  r.mask = a.mask ? a.mask + (int64_t)row * a.mask_ld : nullptr;
+  r.V = V;
+  r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
+  r.mtma = r.mask && r.tma && (reinterpret_cast<uintptr_t>(r.mask) & 15u) == 0;
+  r.nchunks = (V + kChunk - 1) / kChunk;
+  r.nfull = r.tma ? V / kChunk : 0;
+  const uint64_t pol_stream = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+  // The first copies of the row's first pass go out before its parameters
+  // are read: a shared row (a top-p row) its half, kept in L2 for the second
+  // pass; any other row from chunk 0.  pre_c0 / pre_n: the chunks under way,
+  // which every exit before the pass waits for (pre_drain).
+  int pre_c0 = 0, pre_n = 0;
+  uint64_t pre_pol = pol_stream;
+  {
+    int c1 = r.nchunks;
+    if (joint) {
+      pre_pol = pol_keep;
+      if (r.nchunks >= 2) {
+        pre_c0 = crank == 0 ? 0 : r.nchunks / 2;
+        c1 = crank == 0 ? r.nchunks / 2 : r.nchunks;
+      } else if (crank == 1) {
+        c1 = 0;  // too short to share: the first CTA takes it alone
+      }
+    }
+    pre_n = max(0, min(c1 - pre_c0, st_nstages<DT>()));
+    if (tid == 0)
+      for (int c = pre_c0; c < pre_c0 + pre_n; ++c) st_issue<DT>(sh, r, c, c - pre_c0, pre_pol);
+  }
+  uint32_t ph = 0;
+  auto pre_drain = [&]() {  // all threads, before leaving with the first copies under way
+    if (pre_n) st_drain<DT>(sh, pre_c0, pre_c0, pre_c0 + pre_n, ph);
+    pre_n = 0;
+  };
   const double T = a.temperature[row];
   int k = a.top_k[row];
   const double P = a.top_p[row];
   const double U = a.uniforms[row];
-  const int V = a.V;
   const bool shard = a.records != nullptr;
   if (!(T >= 0.0) || isinf(T)) {  // negative, NaN or infinite temperature
+    pre_drain();
     if (tid == 0 && crank == 0) {
       if (shard) st_record_empty(a, row, MS_ROW_BAD_TEMPERATURE);
       else write_row(a, row, -1, 0.0f, MS_ROW_BAD_TEMPERATURE);
@@ -1335,6 +1381,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   // a row this kernel does not finish: the generic kernel takes it, or in
   // sharded mode its record says why (nonfinite: a NaN / +inf logit)
   auto leave = [&](bool nonfinite) {
+    pre_drain();
     if (tid == 0 && crank == 0) {
       if (shard) st_record_empty(a, row, nonfinite ? MS_ROW_NONFINITE : MS_ROW_UNSUPPORTED);
       else a.status[row] = kRowPending;
@@ -1372,28 +1419,12 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     leave(false);
     return;
   }
-  StRow r;
-  r.g = reinterpret_cast<const char *>(a.logits) + (int64_t)row * a.ld * st_esz<DT>();
-  r.mask = a.mask ? a.mask + (int64_t)row * a.mask_ld : nullptr;
-  r.V = V;
-  r.tma = (reinterpret_cast<uintptr_t>(r.g) & 15u) == 0;
-  r.mtma = r.mask && r.tma && (reinterpret_cast<uintptr_t>(r.mask) & 15u) == 0;
-  r.nchunks = (V + kChunk - 1) / kChunk;
-  r.nfull = r.tma ? V / kChunk : 0;
-  if (tid < st_nstages<DT>()) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(st_smem(&sh.full[tid])) : "memory");
-  }
   if (tid < kStWarps) sh.wbound[tid] = 0u;
   if (tid == 0) {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     sh.ncand = 0;
     sh.nhigh = 0;  // top-k rows: st_topk_rank's counter
   }
   __syncthreads();
-  uint32_t ph = 0;
-  const uint64_t pol_stream = policy_evict_first();
-  const uint64_t pol_keep = policy_evict_last();
   bool ok = true;
   int rf = 0;  // scratch half of the next one-barrier reduction
 
@@ -1403,6 +1434,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // larger chunk maximum moves the thread's best to its first occurrence
     float tm = -INFINITY, tnan = -INFINITY;
     int ti = 0x7FFFFFFF;
+    const bool pre = pre_n > 0;
+    pre_n = 0;
     ok = st_stream<DT, false>(
         sh, r, 0, r.nchunks, pol_stream, ph,
         [&](const float *x, int g0, int, int) {
@@ -1416,7 +1449,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
             ti = st_gidx(g0, e);
           }
         },
-        StNoAfter());
+        StNoAfter(), pre);
     const bool bad = st_bad(tnan);
     uint32_t bk = tm > -INFINITY ? fkey(tm) : 0u;
     int bi = tm > -INFINITY ? ti : 0x7FFFFFFF;
@@ -1489,8 +1522,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     const int n0 = min(kChunk, V);
     int msamp = k;
     if (r.nchunks > 1) {
-      const double lam = (double)k * (double)n0 / (double)V;
-      msamp = (int)ceil(lam + 3.0 * sqrt(lam) + 2.0);
+      const float lam = (float)k * (float)n0 / (float)V;
+      msamp = (int)ceilf(lam + 3.0f * sqrtf(lam) + 2.0f);
     }
     msamp = min(msamp, n0);
     for (int attempt = 0;; ++attempt) {
@@ -1508,6 +1541,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         if (tid == 0) sh.ncand = 0;
         __syncthreads();
       }
+      const bool pre = pre_n > 0;
+      pre_n = 0;
       ok = st_stream<DT, true>(
           sh, r, 0, r.nchunks, pol_stream, ph,
           [&](const float *x, int g0, int, int c) -> int {
@@ -1608,7 +1643,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
               }
             }
             return over;
-          });
+          },
+          pre);
       const bool bad = st_bad(rmax);
       if (__syncthreads_or(bad || !ok || over)) {
         leave(__syncthreads_or(bad) != 0);
@@ -1810,7 +1846,9 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     // the first chunk first: the anchor, and for top-p rows the prediction
     {
       float x[8];
-      if (!st_peek<DT>(sh, r, c0, c1, pol1, ph, x)) ok = false;
+      const bool pre = pre_n > 0;  // the first copies went out at the start
+      pre_n = 0;
+      if (!st_peek<DT>(sh, r, c0, c1, pol1, ph, x, pre)) ok = false;
       const float cm = st_max8n(x);
       float g = G;
       if (!(G > -INFINITY)) {
