@@ -627,6 +627,72 @@ __device__ uint32_t st_sample_kth(StShared &sh, const float *x, int m) {
   return prefix << 16;
 }
 
+// The m-th largest (1 <= m <= kStThreads) of one key per thread, to its
+// leading 16 bits (a lower bound on it): two rounds of 8-bit digits.  Used
+// with each thread's maximum of its 8 values: the m largest of those are m
+// distinct values, so the result is also a lower bound on the m-th largest
+// of all the values.  All threads.
+__device__ uint32_t st_sample_kth1(StShared &sh, uint32_t key, int m) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  __syncthreads();  // no warp still scans the histograms of an earlier selection
+  (&sh.sel[0][0])[tid] = 0u;
+  __syncthreads();
+  uint32_t prefix = 0;
+  int rem = m;
+#pragma unroll
+  for (int d = 0; d < 2; ++d) {
+    const int shift = 24 - 8 * d;
+    uint32_t *h = sh.sel[d];
+    const bool in = d == 0 || (key >> 24) == prefix;
+    const uint32_t digit = (key >> shift) & 255u;
+    const unsigned act = __ballot_sync(0xFFFFFFFFu, in);
+    if (act) {  // the first active lane's digit takes one atomic for every lane that holds it
+      const int first = __ffs(act) - 1;
+      const uint32_t lead = __shfl_sync(0xFFFFFFFFu, digit, first);
+      const unsigned same = __ballot_sync(0xFFFFFFFFu, in && digit == lead);
+      if (lane == first) {
+        atomicAdd(&h[lead], (uint32_t)__popc(same));
+      } else if (in && digit != lead) {
+        atomicAdd(&h[digit], 1u);
+      }
+    }
+    __syncthreads();
+    const uint4 *h4 = reinterpret_cast<const uint4 *>(h);
+    const uint4 lo = h4[(248 - 8 * lane) >> 2], hi = h4[((248 - 8 * lane) >> 2) + 1];
+    const uint32_t c8[8] = {hi.w, hi.z, hi.y, hi.x, lo.w, lo.z, lo.y, lo.x};
+    uint32_t s8 = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s8 += c8[q];
+    uint32_t incl = s8;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - s8;
+    const unsigned hit = __ballot_sync(0xFFFFFFFFu, incl >= (uint32_t)rem && excl < (uint32_t)rem);
+    uint32_t dig = 0, before = 0;
+    if (hit && lane == __ffs(hit) - 1) {
+      uint32_t acc = excl;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (acc + c8[q] >= (uint32_t)rem) {
+          dig = 255u - (uint32_t)(8 * lane + q);
+          before = acc;
+          break;
+        }
+        acc += c8[q];
+      }
+    }
+    const int src = hit ? __ffs(hit) - 1 : 0;
+    dig = __shfl_sync(0xFFFFFFFFu, dig, src);
+    before = __shfl_sync(0xFFFFFFFFu, before, src);
+    rem -= (int)before;
+    prefix = (prefix << 8) | dig;
+  }
+  return prefix << 16;
+}
+
 __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
@@ -1567,7 +1633,10 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
             }
             if (sampled) {
               if (c == 0) {  // block-uniform: the threshold from chunk 0's values
-                const uint32_t tk = st_sample_kth(sh, x, msamp);
+                // (from the threads' maxima when the sample rank allows)
+                const uint32_t tk = msamp <= kStThreads / 8 && r.nchunks > 1
+                                        ? st_sample_kth1(sh, cm > -INFINITY ? fkey(cm) : kNegInfKey, msamp)
+                                        : st_sample_kth(sh, x, msamp);
                 if (tk > kNegInfKey) set_tau(key_to_float(tk), false);
               }
             } else if (!exact_tau && st_refresh_chunk(c)) {
