@@ -1901,8 +1901,11 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   float vmax = -INFINITY;
   double zsum = 0.0;  // the row's total of W
   // top-p: a wide nucleus predicted at the first chunk(s), whose histogram
-  // pass 1 builds too (when the chunk's unit maxima carry under 0.8 top_p of
-  // its mass, the row's largest values rarely reach top_p of the total)
+  // pass 1 builds too (when the chunk's unit maxima carry under top_p of its
+  // mass, the row's largest values rarely reach top_p of the total).  A wide
+  // row predicted narrow costs a histogram pass, a narrow row predicted wide
+  // the classifying pass instead of the narrow capture; the threshold keeps
+  // the first, dearer mistake rare.
   bool wide = false;
   for (int attempt = 0;; ++attempt) {
     if (attempt > 0) set_anchor(vmax);  // no weight above 1
@@ -1968,7 +1971,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
       }
       if (!(G > -INFINITY) && g > -INFINITY) set_anchor(g);
       if (topp && G > -INFINITY) {
-        wide = t0 < 0.8 * P * z0;
+        wide = t0 < P * z0;
         if (wide) set_hist_anchor(G);
       }
     }
