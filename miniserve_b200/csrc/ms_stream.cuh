@@ -69,10 +69,7 @@ __host__ __device__ constexpr int st_esz() {
   return DT == MS_DTYPE_F32 ? 4 : 2;
 }
 template <int DT>
-__host__ __device__ constexpr int st_nstages() {
-#ifdef MS_BF16_STAGES
-  if (DT != MS_DTYPE_F32) return MS_BF16_STAGES;
-#endif
+__host__ __device__ constexpr int st_nstages() {  // single-chunk stages in the ring
   return kRingBytes / (kChunk * st_esz<DT>());
 }
 constexpr int kCandCap = 6144;                  // top-k candidate buffer entries
@@ -229,26 +226,57 @@ __device__ __forceinline__ int tma_elems(const StRow &r, int c) {
   return ne & -(16 / st_esz<DT>());
 }
 
-// thread 0: start the copy of chunk c into stage s (and, for a whole chunk of
-// a row with an aligned mask row, of its kChunk / 32 mask words)
-template <int DT>
-__device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, int s, uint64_t pol) {
-  const uint32_t bytes = (uint32_t)(tma_elems<DT>(r, c) * st_esz<DT>());
-  const uint32_t mbytes = r.mtma && c < r.nfull ? (uint32_t)(kChunk / 8) : 0u;
+// Chunks per stage: bf16 passes without per-chunk counts carry two chunks
+// (16 KB) per stage, so a stage moves as many bytes as an fp32 one and the
+// chunk barrier and copy issue are paid once per 8192 values.  Sub-chunk k of
+// stage s occupies the memory (and mask words) of single-chunk stage
+// s * SUB + k.
+template <int DT, bool COUNT>
+__host__ __device__ constexpr int st_sub() {
+  return DT != MS_DTYPE_F32 && !COUNT ? 2 : 1;
+}
+
+// thread 0: start the copies of chunks [c, min(c + SUB, c1)) into stage s
+// (and, for whole chunks of a row with an aligned mask row, of their kChunk /
+// 32 mask words each), all completing on stage s's barrier
+template <int DT, int SUB = 1>
+__device__ __forceinline__ void st_issue(StShared &sh, const StRow &r, int c, int s, uint64_t pol,
+                                         int c1 = 0x7FFFFFFF) {
+  const int n = min(SUB, c1 - c);
+  const int sb = s * SUB;  // single-chunk stage of the first chunk
+  uint32_t b[SUB], m[SUB], bytes = 0, mbytes = 0;
+#pragma unroll
+  for (int k = 0; k < SUB; ++k) {
+    b[k] = k < n ? (uint32_t)(tma_elems<DT>(r, c + k) * st_esz<DT>()) : 0u;
+    m[k] = k < n && r.mtma && c + k < r.nfull ? (uint32_t)(kChunk / 8) : 0u;
+    bytes += b[k];
+    mbytes += m[k];
+  }
   const uint32_t mb = st_smem(&sh.full[s]);
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(bytes + mbytes) : "memory");
-  if (bytes) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-            st_smem(st_stage<DT>(sh, s))),
-        "l"(r.g + (int64_t)c * kChunk * st_esz<DT>()), "r"(bytes), "r"(mb), "l"(pol)
-        : "memory");
+  // a whole first chunk is followed by the next one in both memories: one copy
+  const bool one = SUB == 1 || b[0] == (uint32_t)(kChunk * st_esz<DT>());
+#pragma unroll
+  for (int k = 0; k < SUB; ++k) {
+    const uint32_t bk = one ? (k == 0 ? bytes : 0u) : b[k];
+    if (bk) {
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+              st_smem(st_stage<DT>(sh, sb + k))),
+          "l"(r.g + (int64_t)(c + k) * kChunk * st_esz<DT>()), "r"(bk), "r"(mb), "l"(pol)
+          : "memory");
+    }
   }
-  if (mbytes) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     st_smem(sh.mstage[s])),
-                 "l"(r.mask + (int64_t)c * (kChunk / 32)), "r"(mbytes), "r"(mb)
-                 : "memory");
+  const bool mone = SUB == 1 || m[0] != 0u;  // whole chunks have their words contiguous too
+#pragma unroll
+  for (int k = 0; k < SUB; ++k) {
+    const uint32_t mk = mone ? (k == 0 ? mbytes : 0u) : m[k];
+    if (mk) {
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       st_smem(sh.mstage[sb + k])),
+                   "l"(r.mask + (int64_t)(c + k) * (kChunk / 32)), "r"(mk), "r"(mb)
+                   : "memory");
+    }
   }
 }
 
@@ -462,13 +490,14 @@ __device__ __forceinline__ float st_pick8(const float *x, int e) {
 __device__ __forceinline__ int st_gidx(int g0, int e) { return e < 4 ? g0 + e : g0 + 124 + e; }
 
 // Wait for the copies of chunks [c, ce) still in flight after an early exit
-// from st_stream (chunk c sits in stage (c - c0) % stages).
-template <int DT>
+// from a pass over chunks from c0 with SUB chunks per stage (c - c0 a
+// multiple of SUB; chunk c sits in stage ((c - c0) / SUB) % stages).
+template <int DT, int SUB = 1>
 __device__ bool st_drain(StShared &sh, int c0, int c, int ce, uint32_t &ph) {
-  constexpr int S = st_nstages<DT>();
+  constexpr int S = st_nstages<DT>() / SUB;
   bool ok = true;
-  for (int c2 = c; c2 < ce; ++c2) {
-    const int s2 = (c2 - c0) % S;
+  for (int c2 = c; c2 < ce; c2 += SUB) {
+    const int s2 = ((c2 - c0) / SUB) % S;
     if (!st_wait(sh, s2, (ph >> s2) & 1u)) ok = false;
     ph ^= 1u << s2;
   }
@@ -486,43 +515,42 @@ struct StNoAfter {
 // whose flag was set) runs in every thread and may end the pass early by
 // returning true.  Returns false when a copy timed out.  `ph` carries the
 // stages' phase parities across passes.  With `issued`, the copies of the
-// first chunks are already under way (st_peek).
+// first stages are already under way (st_peek, or the kernel's prologue).
+// bf16 passes without COUNT take two chunks per stage (st_sub).
 template <int DT, bool COUNT, class Body, class After>
 __device__ __forceinline__ bool st_stream(StShared &sh, const StRow &r, int c0, int c1, uint64_t pol, uint32_t &ph,
                                           Body body, After after, bool issued = false) {
-  constexpr int S = st_nstages<DT>();
+  constexpr int SUB = st_sub<DT, COUNT>();
+  constexpr int S = st_nstages<DT>() / SUB;
   const int tid = threadIdx.x;
   if (tid == 0 && !issued) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int c = c0; c < c0 + S && c < c1; ++c) st_issue<DT>(sh, r, c, c - c0, pol);
+    for (int k = 0; k < S && c0 + k * SUB < c1; ++k) st_issue<DT, SUB>(sh, r, c0 + k * SUB, k, pol, c1);
   }
   bool ok = true;
-#ifdef MS_STREAM_UNROLL
-  for (int cb = c0; cb < c1; cb += S) {
-#pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int c = cb + s;
-      if (c >= c1) break;
-#else
   {
 #pragma unroll 1
-    for (int c = c0, s = 0; c < c1; ++c, s = s == S - 1 ? 0 : s + 1) {
-#endif
+    for (int c = c0, s = 0; c < c1; c += SUB, s = s == S - 1 ? 0 : s + 1) {
       if (!st_wait(sh, s, (ph >> s) & 1u)) ok = false;
       ph ^= 1u << s;
-      float x[8];
-      const int g0 = st_get8<DT>(sh, r, c, s, x);
-      const int u = c * kStWarps + (tid >> 5);
       int n = 0;
-      if constexpr (COUNT) {
-        n = __syncthreads_count(body(x, g0, u, c));
-      } else {
-        body(x, g0, u, c);
-        __syncthreads();  // every thread is done with stage s
+#pragma unroll 1
+      for (int k = 0; k < SUB; ++k) {
+        const int ck = c + k;
+        if (SUB > 1 && ck >= c1) break;  // block-uniform
+        float x[8];
+        const int g0 = st_get8<DT>(sh, r, ck, s * SUB + k, x);
+        const int u = ck * kStWarps + (tid >> 5);
+        if constexpr (COUNT) {
+          n = __syncthreads_count(body(x, g0, u, ck));
+        } else {
+          body(x, g0, u, ck);
+        }
       }
-      if (tid == 0 && c + S < c1) {
+      if constexpr (!COUNT) __syncthreads();  // every thread is done with stage s
+      if (tid == 0 && c + S * SUB < c1) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        st_issue<DT>(sh, r, c + S, s, pol);
+        st_issue<DT, SUB>(sh, r, c + S * SUB, s, pol, c1);
       }
       if constexpr (COUNT) {
         if (after(c, n)) {  // block-uniform
@@ -542,10 +570,11 @@ __device__ __forceinline__ bool st_stream(StShared &sh, const StRow &r, int c0, 
 template <int DT>
 __device__ __forceinline__ bool st_peek(StShared &sh, const StRow &r, int c0, int c1, uint64_t pol, uint32_t ph,
                                         float x[8], bool issued = false) {
-  constexpr int S = st_nstages<DT>();
+  constexpr int SUB = st_sub<DT, false>();
+  constexpr int S = st_nstages<DT>() / SUB;
   if (threadIdx.x == 0 && !issued) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int c = c0; c < c0 + S && c < c1; ++c) st_issue<DT>(sh, r, c, c - c0, pol);
+    for (int k = 0; k < S && c0 + k * SUB < c1; ++k) st_issue<DT, SUB>(sh, r, c0 + k * SUB, k, pol, c1);
   }
   const bool ok = st_wait(sh, 0, ph & 1u);
   st_get8<DT>(sh, r, c0, 0, x);
@@ -1422,7 +1451,8 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         c1 = 0;  // too short to share: the first CTA takes it alone
       }
     }
-    pre_n = max(0, min(c1 - pre_c0, st_nstages<DT>()));
+    // (fp32 rows: a bf16 row's stage layout depends on its mode)
+    pre_n = DT == MS_DTYPE_F32 ? max(0, min(c1 - pre_c0, st_nstages<DT>())) : 0;
     if (tid == 0)
       for (int c = pre_c0; c < pre_c0 + pre_n; ++c) st_issue<DT>(sh, r, c, c - pre_c0, pre_pol);
   }
@@ -1960,7 +1990,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
         if (!(g > -INFINITY)) {
           // neither half starts with a finite value: the first CTA takes the
           // row alone, from a fresh start (the copies under way land first)
-          if (!st_drain<DT>(sh, c0, c0, min(c1, c0 + st_nstages<DT>()), ph)) ok = false;
+          if (!st_drain<DT, st_sub<DT, false>()>(sh, c0, c0, min(c1, c0 + st_nstages<DT>()), ph)) ok = false;
           if (crank == 1) return;
           joint = false;
           c0 = 0;
