@@ -385,10 +385,14 @@ struct JsonVocab {
 };
 
 constexpr uint8_t kJsonLongToken = 255;
+constexpr uint8_t kJsonPlain = 0x40;  // lens flag: no '"', '\\' or control byte (a short token)
+constexpr uint8_t kJsonLenMask = 0x1F;
 
 // One thread per position p: token t = order[p] (t = p without an order) --
-// its bytes zero-padded to 16 in packed[p], its length in lens[p].  An order
-// entry outside [0, V) packs an empty token.
+// its bytes zero-padded to 16 in packed[p], its length in lens[p] (with
+// kJsonPlain when none of its bytes is '"', '\\' or below 0x20: such a token
+// leaves a string body a string body).  An order entry outside [0, V) packs
+// an empty token.
 __global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, int64_t V, const int32_t *order,
                                     uint4 *packed, uint8_t *lens) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -399,11 +403,17 @@ __global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, in
   const int64_t n = e - b;
   uint32_t w[4] = {0u, 0u, 0u, 0u};
   const int m = n < 16 ? (int)n : 16;
+  bool plain = true;
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    if (i < m) w[i >> 2] |= (uint32_t)bytes[b + i] << (8 * (i & 3));
+  for (int i = 0; i < 16; ++i) {
+    if (i < m) {
+      const uint8_t c = bytes[b + i];
+      w[i >> 2] |= (uint32_t)c << (8 * (i & 3));
+      plain = plain && c >= 0x20 && c != '"' && c != '\\';
+    }
+  }
   packed[p] = make_uint4(w[0], w[1], w[2], w[3]);
-  lens[p] = n <= 16 ? (uint8_t)n : kJsonLongToken;
+  lens[p] = n <= 16 ? (uint8_t)(n | (plain && n > 0 ? kJsonPlain : 0)) : kJsonLongToken;
 }
 
 __device__ __forceinline__ void j_load_state(const uint32_t *g, uint32_t *sbits, JState &st) {
@@ -540,6 +550,10 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     if (st0.decided == J_RAISE && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(row_status + row, 1);
     return;
   }
+  // a row inside a string body keeps it through a plain token (no '"', '\\'
+  // or control byte), and a string body at the end of the text is "Unterminated
+  // string": allowed (j_finish)
+  const bool in_str = st0.mode == JM_STR;
   // a token whose first byte already decides takes that answer: once decided
   // the automaton ignores the rest of the text (j_step, j_finish)
   static_assert(kJsonThreads == 256, "one thread per first byte");
@@ -558,29 +572,34 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     // the token at position t (ordered vocabulary), or t itself; < 0: none
     int64_t tok = t < voc.V ? (voc.order ? (int64_t)voc.order[t] : t) : -1;
     if (tok >= voc.V) tok = -1;
-    const int nb = tok >= 0 && voc.lens ? voc.lens[t] : kJsonLongToken;
-    const uint4 q = tok >= 0 && voc.lens ? voc.packed[t] : make_uint4(0u, 0u, 0u, 0u);
+    const int lb = tok >= 0 && voc.lens ? voc.lens[t] : kJsonLongToken;
+    const int nb = lb == kJsonLongToken ? kJsonLongToken : (lb & kJsonLenMask);
     uint8_t r = J_FALSE;
-    const uint8_t d = tok >= 0 && voc.lens && nb >= 1 ? first_dec[q.x & 0xFFu] : (uint8_t)J_UNDECIDED;
-    if (d != J_UNDECIDED) {
-      r = d;
-      my_flags |= d == J_RAISE ? 1 : 0;
-    } else if (tok >= 0) {
-      JState st = st0;
-      JStackTok stk(sbits, st0.depth);
-      if (nb != kJsonLongToken) {  // the bytes from registers, low byte first
-        uint64_t lo = (uint64_t)q.x | ((uint64_t)q.y << 32), hi = (uint64_t)q.z | ((uint64_t)q.w << 32);
-        for (int i = 0; i < nb && !st.decided && !stk.over; ++i) {
-          j_step(st, stk, (uint8_t)lo);
-          lo = (lo >> 8) | (hi << 56);
-          hi >>= 8;
+    if (in_str && lb != kJsonLongToken && (lb & kJsonPlain)) {
+      r = J_TRUE;  // the packed bytes are not needed
+    } else {
+      const uint4 q = tok >= 0 && voc.lens ? voc.packed[t] : make_uint4(0u, 0u, 0u, 0u);
+      const uint8_t d = tok >= 0 && voc.lens && nb >= 1 ? first_dec[q.x & 0xFFu] : (uint8_t)J_UNDECIDED;
+      if (d != J_UNDECIDED) {
+        r = d;
+        my_flags |= d == J_RAISE ? 1 : 0;
+      } else if (tok >= 0) {
+        JState st = st0;
+        JStackTok stk(sbits, st0.depth);
+        if (nb != kJsonLongToken) {  // the bytes from registers, low byte first
+          uint64_t lo = (uint64_t)q.x | ((uint64_t)q.y << 32), hi = (uint64_t)q.z | ((uint64_t)q.w << 32);
+          for (int i = 0; i < nb && !st.decided && !stk.over; ++i) {
+            j_step(st, stk, (uint8_t)lo);
+            lo = (lo >> 8) | (hi << 56);
+            hi >>= 8;
+          }
+        } else {
+          const int64_t b = voc.off[tok], e = voc.off[tok + 1];
+          for (int64_t i = b; i < e && !st.decided && !stk.over; ++i) j_step(st, stk, voc.bytes[i]);
         }
-      } else {
-        const int64_t b = voc.off[tok], e = voc.off[tok + 1];
-        for (int64_t i = b; i < e && !st.decided && !stk.over; ++i) j_step(st, stk, voc.bytes[i]);
+        r = stk.over ? (uint8_t)J_UNDECIDED : j_finish(st, stk);
+        my_flags |= r == J_RAISE ? 1 : (stk.over ? 2 : 0);
       }
-      r = stk.over ? (uint8_t)J_UNDECIDED : j_finish(st, stk);
-      my_flags |= r == J_RAISE ? 1 : (stk.over ? 2 : 0);
     }
     if (voc.order) {
       if (r == J_TRUE) atomicOr(mask + (int64_t)row * mask_ld + (tok >> 5), 1u << (tok & 31));

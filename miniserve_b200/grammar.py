@@ -30,12 +30,19 @@ def _pack_texts(texts: Sequence[str], device):
     return by, torch.tensor(off, dtype=torch.int64, device=device)
 
 
+def _plain(b: bytes) -> bool:
+    """A short token with no '"', '\\' or control byte: it leaves a JSON string
+    body a string body (the mask kernel settles it without the automaton)."""
+    return 0 < len(b) <= 16 and all(c >= 0x20 and c not in (0x22, 0x5C) for c in b)
+
+
 def length_order(vocab: Sequence[str]) -> List[int]:
-    """Token ids sorted by (UTF-8 length, bytes): a warp of the mask kernel
-    then holds tokens of one length that share their first bytes, so its lanes
-    take the same automaton steps and finish together."""
+    """Token ids sorted by (plain first, UTF-8 length, bytes): a warp of the
+    mask kernel then holds tokens of one length that share their first bytes,
+    so its lanes take the same automaton steps and finish together, and rows
+    inside a string settle whole warps of plain tokens at once."""
     enc = [t.encode("utf-8") for t in vocab]
-    return sorted(range(len(enc)), key=lambda t: (len(enc[t]), enc[t]))
+    return sorted(range(len(enc)), key=lambda t: (not _plain(enc[t]), len(enc[t]), enc[t]))
 
 
 class JsonMaskBuilder:

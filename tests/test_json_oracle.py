@@ -78,16 +78,22 @@ def test_fuzz_against_live_reference():
 
 
 def test_length_order():
-    """The mask builder's evaluation order: token ids sorted by (UTF-8 byte
-    length, bytes), a permutation of the vocabulary; unknown orders are
+    """The mask builder's evaluation order: token ids sorted by (plain first,
+    UTF-8 byte length, bytes) -- plain: 1-16 bytes, none of them '"', '\\' or
+    a control byte -- a permutation of the vocabulary; unknown orders are
     refused before anything touches a device."""
     from miniserve_b200.grammar import JsonMaskBuilder, length_order
-    vocab = ["bb", "a", "ab", "", "é", "{", "aa"]
+    vocab = ["bb", "a", "ab", "", "é", "{", "aa", 'a"', "\\n", "x\n", "z" * 17]
     order = length_order(vocab)
     assert sorted(order) == list(range(len(vocab)))
-    keys = [(len(vocab[t].encode()), vocab[t].encode()) for t in order]
+
+    def plain(b):
+        return 0 < len(b) <= 16 and all(c >= 0x20 and c not in (0x22, 0x5C) for c in b)
+    keys = [(not plain(vocab[t].encode()), len(vocab[t].encode()), vocab[t].encode()) for t in order]
     assert keys == sorted(keys)
-    assert order[0] == 3  # the empty token first
+    # the six plain tokens first, by (length, bytes); then the rest, the empty token first
+    assert [vocab[t] for t in order[:6]] == ["a", "{", "aa", "ab", "bb", "é"]
+    assert vocab[order[6]] == ""
     with pytest.raises(ValueError):
         JsonMaskBuilder(vocab, device="cpu", order="alphabetical")
 
