@@ -385,14 +385,16 @@ struct JsonVocab {
 };
 
 constexpr uint8_t kJsonLongToken = 255;
-constexpr uint8_t kJsonPlain = 0x40;  // lens flag: no '"', '\\' or control byte (a short token)
+constexpr uint8_t kJsonPlain = 0x40;      // lens flag: no '"', '\\' or control byte (a short token)
+constexpr uint8_t kJsonPlainTail = 0x20;  // lens flag: the same for every byte after the first
 constexpr uint8_t kJsonLenMask = 0x1F;
+constexpr uint8_t kJsonFirstStr = 4;      // first_dec: undecided, inside a string after the byte
 
 // One thread per position p: token t = order[p] (t = p without an order) --
 // its bytes zero-padded to 16 in packed[p], its length in lens[p] (with
 // kJsonPlain when none of its bytes is '"', '\\' or below 0x20: such a token
-// leaves a string body a string body).  An order entry outside [0, V) packs
-// an empty token.
+// leaves a string body a string body; kJsonPlainTail when that holds for its
+// bytes after the first).  An order entry outside [0, V) packs an empty token.
 __global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, int64_t V, const int32_t *order,
                                     uint4 *packed, uint8_t *lens) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -403,17 +405,20 @@ __global__ void ms_json_pack_kernel(const uint8_t *bytes, const int64_t *off, in
   const int64_t n = e - b;
   uint32_t w[4] = {0u, 0u, 0u, 0u};
   const int m = n < 16 ? (int)n : 16;
-  bool plain = true;
+  bool plain = true, tail = true;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     if (i < m) {
       const uint8_t c = bytes[b + i];
       w[i >> 2] |= (uint32_t)c << (8 * (i & 3));
-      plain = plain && c >= 0x20 && c != '"' && c != '\\';
+      const bool pc = c >= 0x20 && c != '"' && c != '\\';
+      plain = plain && pc;
+      if (i > 0) tail = tail && pc;
     }
   }
   packed[p] = make_uint4(w[0], w[1], w[2], w[3]);
-  lens[p] = n <= 16 ? (uint8_t)(n | (plain && n > 0 ? kJsonPlain : 0)) : kJsonLongToken;
+  lens[p] = n <= 16 ? (uint8_t)(n | (plain && n > 0 ? kJsonPlain : 0) | (tail && n > 0 ? kJsonPlainTail : 0))
+                    : kJsonLongToken;
 }
 
 __device__ __forceinline__ void j_load_state(const uint32_t *g, uint32_t *sbits, JState &st) {
@@ -561,7 +566,9 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     JState st = st0;
     JStackTok stk(sbits, st0.depth);
     j_step(st, stk, (uint8_t)threadIdx.x);
-    first_dec[threadIdx.x] = st.decided;  // one byte never leaves the register window
+    // one byte never leaves the register window; a byte that opens (or keeps)
+    // a string body is marked: a plain rest of the token keeps it open
+    first_dec[threadIdx.x] = st.decided ? st.decided : (st.mode == JM_STR ? kJsonFirstStr : (uint8_t)J_UNDECIDED);
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -580,7 +587,9 @@ __global__ void __launch_bounds__(kJsonThreads) ms_json_mask_kernel(const uint32
     } else {
       const uint4 q = tok >= 0 && voc.lens ? voc.packed[t] : make_uint4(0u, 0u, 0u, 0u);
       const uint8_t d = tok >= 0 && voc.lens && nb >= 1 ? first_dec[q.x & 0xFFu] : (uint8_t)J_UNDECIDED;
-      if (d != J_UNDECIDED) {
+      if (d == kJsonFirstStr && lb != kJsonLongToken && (lb & kJsonPlainTail)) {
+        r = J_TRUE;  // the first byte leaves a string body, the rest keeps it: "Unterminated string"
+      } else if (d != J_UNDECIDED && d != kJsonFirstStr) {
         r = d;
         my_flags |= d == J_RAISE ? 1 : 0;
       } else if (tok >= 0) {
