@@ -315,10 +315,13 @@ def run_ours(args, rank, world, local_rank):
 def sharded_line(args, rank, world, dev, peak):
     """Config 5 (1024 x 256000 fp32, top_k 50, top_p 0.95, T 0.9) with the
     vocabulary split into contiguous slices over the ranks, sampled through
-    ShardedSampler.sample (shard pass, NCCL all-gather of the candidate
-    records, merge).  Strong scaling: the same rows on every N.  Each phase
-    timed with CUDA events on the launching stream; the step time is the max
-    over ranks."""
+    ShardedSampler.sample: the default path (shard pass, NCCL all-gather of
+    the candidate records, merge kernel), and beside it the fused peer
+    exchange (one streaming kernel that stores each row's record into every
+    rank's buffer over NVLink and merges the rows it completes, then a finish
+    kernel that waits for every row's result).  Strong scaling: the same rows
+    on every N.  Each phase timed with CUDA events on the launching stream;
+    the step time is the max over ranks."""
     import torch
     import torch.distributed as dist
     from miniserve_b200 import sharded, workloads
@@ -329,29 +332,34 @@ def sharded_line(args, rank, world, dev, peak):
     del b.logits
     U = torch.from_numpy(b.uniforms).to(dev)
     T, K, P = float(b.temperature[0]), int(b.top_k[0]), float(b.top_p[0])  # uniform over the rows
-    ss = sharded.ShardedSampler(V)
-    stream = torch.cuda.current_stream(dev)
     steps = max(3, min(args.steps, 20))
-    for _ in range(max(args.warmup, 3)):
-        ss.sample(x, v0, T, K, P, uniforms=U)
-    torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    for i in range(steps):
-        tok, prob, st = ss.sample(x, v0, T, K, P, uniforms=U, events=evs[i])
-    torch.cuda.synchronize()
-    ph = torch.tensor([[e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), e[2].elapsed_time(e[3])]
-                       for e in evs], dtype=torch.float64, device=dev)
-    per_step = ph.sum(dim=1)
-    stats = torch.stack([per_step.mean(), ph[:, 0].mean(), ph[:, 1].mean(), ph[:, 2].mean()])
-    if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    step_ms, shard_ms, gather_ms, merge_ms = (float(v) for v in stats.tolist())
-    flagged = int((st != 0).sum())
+
+    def run(mode):
+        ss = sharded.ShardedSampler(V, exchange=mode)
+        for _ in range(max(args.warmup, 3)):
+            ss.sample(x, v0, T, K, P, uniforms=U)
+        torch.cuda.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(steps):
+            tok, prob, st = ss.sample(x, v0, T, K, P, uniforms=U, events=evs[i])
+        torch.cuda.synchronize()
+        used = ss.last_exchange
+        ss.close()
+        ph = torch.tensor([[e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), e[2].elapsed_time(e[3])]
+                           for e in evs], dtype=torch.float64, device=dev)
+        per_step = ph.sum(dim=1)
+        stats = torch.stack([per_step.mean(), ph[:, 0].mean(), ph[:, 1].mean(), ph[:, 2].mean()])
+        if world > 1:
+            dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        return used, [float(v) for v in stats.tolist()], int((st != 0).sum())
+
+    _, (step_ms, shard_ms, gather_ms, merge_ms), flagged = run("nccl")
+    used, (p_step, p_kernel, p_finish, _), p_flagged = run("auto")
     alg = B * ((v1 - v0) * 4 + 52)  # this rank's logits slice and per-row parameters
-    return {
+    line = {
         "workload": "config5: 1024x256000 fp32, vocab sliced over the GPUs, top_k 50, top_p 0.95, T 0.9",
         "api": "miniserve_b200.sharded.ShardedSampler.sample", "scaling": "strong", "nccl_ranks": world,
         "value": round(B / (step_ms / 1e3), 1), "unit": "rows/s", "ms_per_step": round(step_ms, 5),
@@ -363,6 +371,14 @@ def sharded_line(args, rank, world, dev, peak):
         "rows_flagged": flagged, "steps": steps,
         "timing": "CUDA events per phase on the launching stream, max over ranks; device time",
     }
+    if used == "peer":
+        line["peer_exchange"] = {
+            "value": round(B / (p_step / 1e3), 1), "unit": "rows/s", "ms_per_step": round(p_step, 5),
+            "phase_us": {"fused_shard_exchange_merge": round(p_kernel * 1e3, 2), "finish": round(p_finish * 1e3, 2)},
+            "peer_bytes_per_rank": B * sharded.record_words(50) * 4 * max(world - 1, 0), "rows_flagged": p_flagged}
+    else:
+        line["peer_exchange"] = {"unavailable": "CUDA IPC mapping of the exchange buffers failed"}
+    return line
 
 
 # ------------------------------------------------------- other BASELINE configs

@@ -20,6 +20,7 @@ MS_ROW_ALL_MASKED = 1
 MS_ROW_BAD_TEMPERATURE = 2
 MS_ROW_NONFINITE = 4
 MS_ROW_UNSUPPORTED = 8
+MS_ROW_PEER_TIMEOUT = 16
 
 _lock = threading.Lock()
 _lib = None
@@ -52,6 +53,18 @@ SIGNATURES = {
     "ms_shard_record_words": (_I64, [ctypes.c_int32]),
     "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,
                                       _P, _P, _P, _P]),
+    "ms_exchange_words": (_I64, [_I64, ctypes.c_int32, ctypes.c_int32]),
+    "ms_exchange_records_offset": (_I64, [_I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32]),
+    "ms_shard_exchange": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P,
+                                         _I64, ctypes.c_int32, _P, _P, ctypes.c_int32, ctypes.c_int32, _I64,
+                                         ctypes.c_int32, ctypes.c_uint32, _P]),
+    "ms_exchange_finish": (ctypes.c_int, [_P, _I64, _I64, ctypes.c_uint64, ctypes.c_uint32, _I64, _P, _P, _P,
+                                          _P]),
+    "ms_device_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "ms_device_free": (ctypes.c_int, [_P]),
+    "ms_ipc_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),
+    "ms_ipc_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "ms_ipc_close": (ctypes.c_int, [_P]),
     "ms_json_state_words": (_I64, []),
     "ms_json_init": (ctypes.c_int, [_P, _P, _I64, _P, _P]),
     "ms_json_advance": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _P]),

@@ -15,11 +15,13 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstring>
 
 #include "ms_common.cuh"
 #include "ms_generic.cuh"
 #include "ms_hook.cuh"
 #include "ms_json.cuh"
+#include "ms_exchange.cuh"
 #include "ms_shard.cuh"
 #include "ms_nucleus.cuh"
 #include "ms_stream.cuh"
@@ -37,14 +39,22 @@ constexpr int kMaxDevices = 64;
 // The streaming kernel alone: one CTA per row, or in pair mode B clusters of
 // two CTAs.
 template <int DT>
-cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int dev) {
+cudaError_t launch_stream(const ms::SampleArgs &a, int B, cudaStream_t s, int dev,
+                          const ms::XArgs *x = nullptr) {
   static std::atomic<int> ready[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!ready[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(ms::ms_stream_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sizeof(ms::StShared));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ms::ms_stream_xkernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)sizeof(ms::StShared));
     if (e != cudaSuccess) return e;
     ready[dev].store(1, std::memory_order_release);
+  }
+  if (x) {  // the fused peer exchange: one CTA per row
+    ms::ms_stream_xkernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a, *x);
+    return cudaGetLastError();
   }
   if (!a.pairs) {
     ms::ms_stream_kernel<DT><<<dim3((unsigned)B), dim3(ms::kStThreads), sizeof(ms::StShared), s>>>(a);
@@ -229,6 +239,121 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;
+}
+
+int64_t ms_exchange_words(int64_t Bcap, int32_t nranks, int32_t kmax_cap) {
+  if (Bcap < 1 || Bcap > (1 << 20) || nranks < 1 || nranks > ms::kMgRanks || kmax_cap < 1 ||
+      kmax_cap > ms::kMgTopK)
+    return -1;
+  return ms::x_layout(Bcap, nranks, kmax_cap).total;
+}
+
+int64_t ms_exchange_records_offset(int64_t Bcap, int32_t nranks, int32_t kmax_cap, uint32_t epoch) {
+  if (ms_exchange_words(Bcap, nranks, kmax_cap) < 0) return -1;
+  const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
+  return L.rec0 + (int64_t)(epoch & 1u) * L.half;
+}
+
+int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, int64_t ld, int64_t v0, int64_t V,
+                      const double *temperature, const int32_t *top_k, const double *top_p, const double *uniforms,
+                      const uint32_t *mask, int64_t mask_ld, int32_t kmax, uint32_t *xbuf, uint32_t *const *peers,
+                      int32_t rank, int32_t nranks, int64_t Bcap, int32_t kmax_cap, uint32_t epoch,
+                      ms_stream_t stream) {
+  if (dtype != MS_DTYPE_F32 && dtype != MS_DTYPE_BF16) return MS_E_DTYPE;
+  if (ms_exchange_words(Bcap, nranks, kmax_cap) < 0 || B < 0 || B > Bcap || Vloc < 1 || ld < Vloc || v0 < 0 ||
+      V < v0 + Vloc || V > 0x7FFFFFFFll - 4096 || kmax < 1 || kmax > kmax_cap || rank < 0 || rank >= nranks ||
+      epoch == 0u)
+    return MS_E_INVALID;
+  if ((int64_t)nranks * kmax > ms::kMgCap) return MS_E_UNSUPPORTED;
+  if (B == 0) return MS_OK;
+  if (!logits || !temperature || !top_k || !top_p || !uniforms || !xbuf || !peers) return MS_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
+  if (mask && mask_ld < (Vloc + 31) / 32) return MS_E_INVALID;
+  if (Vloc > ms::kStreamMaxV) return MS_E_UNSUPPORTED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
+  const int64_t rec = L.rec0 + (int64_t)(epoch & 1u) * L.half;
+  ms::SampleArgs a{logits, ld, (int)Vloc, temperature, top_k, top_p, uniforms,
+                   mask, mask_ld, nullptr, nullptr, nullptr};
+  a.records = xbuf + rec + (int64_t)rank * B * (4 + 2 * (int64_t)kmax);
+  a.kmax = kmax;
+  a.v0 = v0;
+  a.Vg = V;
+  a.rows = (int)B;
+  const ms::XArgs x{peers, rank, nranks, epoch, L.cnt, L.out, rec};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = dtype == MS_DTYPE_F32 ? launch_stream<MS_DTYPE_F32>(a, (int)B, s, dev, &x)
+                            : launch_stream<MS_DTYPE_BF16>(a, (int)B, s, dev, &x);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
+}
+
+int ms_exchange_finish(const uint32_t *xbuf, int64_t B, int64_t Bcap, uint64_t done_target, uint32_t epoch,
+                       int64_t timeout_ns, int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
+  if (B < 0 || B > Bcap || Bcap > (1 << 20) || timeout_ns < 0 || epoch == 0u) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!xbuf || !tokens || !probs || !row_status) return MS_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::XLayout L = ms::x_layout(Bcap, 1, 1);  // the counter and entry offsets depend on Bcap only
+  const int grid = (int)((B + ms::kXThreads - 1) / ms::kXThreads);
+  ms::ms_xfinish_kernel<<<dim3((unsigned)(grid < 64 ? grid : 64)), dim3(ms::kXThreads), 0, s>>>(
+      xbuf, L.out, (int)B, (unsigned long long)done_target, epoch, timeout_ns, tokens, probs, row_status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
+}
+
+int ms_device_alloc(int64_t bytes, void **ptr) {
+  if (!ptr || bytes < 1) return MS_E_INVALID;
+  *ptr = nullptr;
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaMemset(p, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e);
+  }
+  *ptr = p;
+  return MS_OK;
+}
+
+int ms_device_free(void *ptr) {
+  if (!ptr) return MS_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
+}
+
+int ms_ipc_handle(void *ptr, unsigned char *handle) {
+  if (!ptr || !handle) return MS_E_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
+  memcpy(handle, &h, sizeof(h));
+  return MS_OK;
+}
+
+int ms_ipc_open(const unsigned char *handle, void **ptr) {
+  if (!handle || !ptr) return MS_E_INVALID;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e);
+  *ptr = p;
+  return MS_OK;
+}
+
+int ms_ipc_close(void *ptr) {
+  if (!ptr) return MS_E_INVALID;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? MS_OK : cuda_fail(e);
 }
 
 int64_t ms_nucleus_hist_words(void) { return ms::kNuBins; }

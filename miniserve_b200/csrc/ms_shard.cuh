@@ -9,6 +9,10 @@
 // softmax total, and a crossing value above every full slice's kmax-th
 // largest value has every larger value of the row among the candidates;
 // otherwise the row is flagged MS_ROW_UNSUPPORTED.
+//
+// The row merge (mg_row) runs as its own kernel after an all-gather, or
+// inside the streaming kernel for the fused peer exchange (ms_exchange.cuh),
+// where the results go to every rank's exchange buffer.
 #pragma once
 
 #include "ms_common.cuh"
@@ -34,6 +38,12 @@ struct MergeArgs {
   int64_t *tokens;
   float *probs;
   int32_t *status;
+  // fused peer exchange: the result of row r goes, as one 16-byte entry
+  // {token, prob bits, status, epoch} at word xout + 4 r, to every rank's
+  // exchange buffer instead of tokens / probs / status
+  uint32_t *const *xpeers = nullptr;
+  int64_t xout = 0;
+  uint32_t xepoch = 0;
 };
 
 struct MgShared {
@@ -53,10 +63,22 @@ struct MgShared {
 };
 
 __device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok, float prob, int32_t st) {
+  if (a.xpeers) {
+    const uint4 e = make_uint4((uint32_t)(int32_t)tok, __float_as_uint(prob), (uint32_t)st, a.xepoch);
+    for (int q = 0; q < a.nranks; ++q) *reinterpret_cast<uint4 *>(a.xpeers[q] + a.xout + 4 * (size_t)r) = e;
+    return;
+  }
   a.tokens[r] = tok;
   a.probs[r] = prob;
   a.status[r] = st;
 }
+
+// Rank r's record of `row`; read through L2 (records written by other GPUs
+// into the fused exchange buffer are never served from a stale L1 line).
+__device__ __forceinline__ const uint32_t *mg_rec(const MergeArgs &a, int r, int row, size_t rw) {
+  return a.records + ((size_t)r * a.B + row) * rw;
+}
+__device__ __forceinline__ uint32_t mg_ld(const uint32_t *p) { return __ldcg(p); }
 
 // A row without top-k (miniserve/sampler.py:35-68 with top_k off): every
 // candidate ranked; float64 weights exp(l/T - max/T); the row's total from the
@@ -64,6 +86,7 @@ __device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok,
 // kept), settled only when the crossing value lies above every full slice's
 // kmax-th largest value; the index-order draw over the kept prefix.  The
 // composites of the n candidates are in sh.u.comp.  All threads.
+template <int NT>
 __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, size_t rw, double T, double P,
                            double U) {
   const int tid = threadIdx.x;
@@ -74,7 +97,7 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
   // rank every candidate (all distinct composites)
   const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
   const int npair = (n + 1) >> 1;
-  for (int i = tid; i < n; i += kMgThreads) {
+  for (int i = tid; i < n; i += NT) {
     const unsigned long long ci = sh.u.comp[i];
     int rank = 0;
     for (int j = 0; j < npair; ++j) {
@@ -90,33 +113,33 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
   const float vmax = key_to_float(sh.key[0]);
   double zr = 0.0;
   if (tid < a.nranks) {
-    const uint32_t *rec = a.records + ((size_t)tid * a.B + row) * rw;
-    const int mr = (int)min(rec[0], (uint32_t)a.kmax);
+    const uint32_t *rec = mg_rec(a, tid, row, rw);
+    const int mr = (int)min(mg_ld(rec), (uint32_t)a.kmax);
     if (mr > 0) {
-      const unsigned long long b = (unsigned long long)rec[2 + 2 * a.kmax] |
-                                   ((unsigned long long)rec[3 + 2 * a.kmax] << 32);
-      zr = __longlong_as_double((long long)b) * exp(((double)key_to_float(rec[2]) - (double)vmax) / T);
+      const unsigned long long b = (unsigned long long)mg_ld(rec + 2 + 2 * a.kmax) |
+                                   ((unsigned long long)mg_ld(rec + 3 + 2 * a.kmax) << 32);
+      zr = __longlong_as_double((long long)b) * exp(((double)key_to_float(mg_ld(rec + 2)) - (double)vmax) / T);
     }
   }
   __syncthreads();
   if (tid == 0) {  // the largest last value among full slices (at most kMgRanks reads)
     float cut = -INFINITY;
     for (int r = 0; r < a.nranks; ++r) {
-      const uint32_t *rec = a.records + ((size_t)r * a.B + row) * rw;
-      if ((int)min(rec[0], (uint32_t)a.kmax) == a.kmax) cut = fmaxf(cut, key_to_float(rec[2 + a.kmax - 1]));
+      const uint32_t *rec = mg_rec(a, r, row, rw);
+      if ((int)min(mg_ld(rec), (uint32_t)a.kmax) == a.kmax) cut = fmaxf(cut, key_to_float(mg_ld(rec + 2 + a.kmax - 1)));
     }
     sh.cut = cut;
   }
-  const double Z = block_sum<kMgThreads>(zr, sh.redd);  // ends with a barrier
+  const double Z = block_sum<NT>(zr, sh.redd);  // ends with a barrier
   const float cut = sh.cut;
   // weights in rank order, a contiguous block of ranks per thread
-  const int per = (n + kMgThreads - 1) / kMgThreads;
+  const int per = (n + NT - 1) / NT;
   const int p0 = tid * per, p1 = min(n, p0 + per);
   const double xmax = (double)vmax / T;
   double sw = 0.0;
   for (int i = p0; i < p1; ++i) sw += exp((double)key_to_float(sh.key[i]) / T - xmax);
   double ex, inc, tt;
-  block_scan<kMgThreads, double>(sw, ex, inc, tt, sh.redd);
+  block_scan<NT, double>(sw, ex, inc, tt, sh.redd);
   const double need = P * Z;
   int cand = 0x7FFFFFFF;
   if (p0 < p1 && inc >= need) {  // sampler.py:54-57: cumsum >= top_p, crossing entry kept
@@ -130,14 +153,14 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
     }
     if (cand == 0x7FFFFFFF) cand = p1 - 1;
   }
-  const int j = block_min_i<kMgThreads>(cand, sh.redi);
+  const int j = block_min_i<NT>(cand, sh.redi);
   if (j == 0x7FFFFFFF || !(key_to_float(sh.key[j]) > cut)) {  // the nucleus may reach past the candidates
     if (tid == 0) mg_write(a, row, -1, 0.0f, MS_ROW_UNSUPPORTED);
     return;
   }
   const int nkeep = j + 1;
   // kept entries in index order (position = kept entries of smaller id)
-  for (int i = tid; i < nkeep; i += kMgThreads) {
+  for (int i = tid; i < nkeep; i += NT) {
     const int my = sh.id[i];
     int pos = 0;
     for (int q = 0; q < nkeep; ++q) pos += sh.id[q] < my ? 1 : 0;
@@ -147,11 +170,11 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
   __syncthreads();
   // index-order inverse CDF over the kept entries (sampler.py:58-68)
   double s2 = 0.0;
-  const int q0 = tid * ((nkeep + kMgThreads - 1) / kMgThreads);
-  const int q1 = min(nkeep, q0 + (nkeep + kMgThreads - 1) / kMgThreads);
+  const int q0 = tid * ((nkeep + NT - 1) / NT);
+  const int q1 = min(nkeep, q0 + (nkeep + NT - 1) / NT);
   for (int i = q0; i < q1; ++i) s2 += sh.u.kw[i];
   double cx, ci2, tot;
-  block_scan<kMgThreads, double>(s2, cx, ci2, tot, sh.redd);
+  block_scan<NT, double>(s2, cx, ci2, tot, sh.redd);
   if (!(U > 0.0)) {  // r == 0 stops at index 0
     if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / tot), 0);
     return;
@@ -169,7 +192,7 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
     }
     if (who == 0x7FFFFFFF) who = q1 - 1;
   }
-  const int w = block_min_i<kMgThreads>(who, sh.redi);
+  const int w = block_min_i<NT>(who, sh.redi);
   if (tid == 0) {
     if (w == 0x7FFFFFFF) {  // ran past the end (sampler.py:68)
       mg_write(a, row, a.V - 1, (float)((sh.kid[nkeep - 1] == a.V - 1 ? sh.u.kw[nkeep - 1] : 0.0) / tot), 0);
@@ -179,9 +202,9 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, siz
   }
 }
 
-__global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
-  __shared__ MgShared sh;
-  const int row = blockIdx.x;
+// One row's merge: all NT threads of the CTA.
+template <int NT>
+__device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row) {
   const int tid = threadIdx.x;
   const size_t rw = (size_t)(4 + 2 * a.kmax);
   const double T = a.temperature[row];
@@ -192,15 +215,15 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   int m_r = 0;
   uint32_t st_r = 0u;
   if (tid < a.nranks) {
-    const uint32_t *rec = a.records + ((size_t)tid * a.B + row) * rw;
-    m_r = (int)min(rec[0], (uint32_t)a.kmax);
-    st_r = rec[1];
+    const uint32_t *rec = mg_rec(a, tid, row, rw);
+    m_r = (int)min(mg_ld(rec), (uint32_t)a.kmax);
+    st_r = mg_ld(rec + 1);
   }
   if (tid == 0) sh.st = 0u;
   __syncthreads();
   if (st_r) atomicOr(&sh.st, st_r);
   int ex, inc, n;
-  block_scan<kMgThreads, int>(m_r, ex, inc, n, sh.redi);  // ends with a barrier
+  block_scan<NT, int>(m_r, ex, inc, n, sh.redi);  // ends with a barrier
   if (tid < a.nranks) sh.off[tid] = ex;
   const uint32_t st = sh.st;
   if (st != 0u) {  // bad temperature, or a slice that needs the full row
@@ -209,10 +232,11 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   }
   __syncthreads();
   for (int r = 0; r < a.nranks; ++r) {
-    const uint32_t *rec = a.records + ((size_t)r * a.B + row) * rw;
-    const int mr = (int)min(rec[0], (uint32_t)a.kmax);
-    for (int i = tid; i < mr; i += kMgThreads)
-      sh.u.comp[sh.off[r] + i] = ((unsigned long long)rec[2 + i] << 32) | (unsigned long long)(~rec[2 + a.kmax + i]);
+    const uint32_t *rec = mg_rec(a, r, row, rw);
+    const int mr = (int)min(mg_ld(rec), (uint32_t)a.kmax);
+    for (int i = tid; i < mr; i += NT)
+      sh.u.comp[sh.off[r] + i] =
+          ((unsigned long long)mg_ld(rec + 2 + i) << 32) | (unsigned long long)(~mg_ld(rec + 2 + a.kmax + i));
   }
   if (tid == 0) {
     sh.u.comp[n] = 0ull;
@@ -228,13 +252,13 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   }
   if (T == 0.0 || k == 1) {  // the first maximum (sampler.py:33-34, or top-k 1)
     unsigned long long best = 0ull;
-    for (int i = tid; i < n; i += kMgThreads) best = max(best, sh.u.comp[i]);
+    for (int i = tid; i < n; i += NT) best = max(best, sh.u.comp[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
     if ((tid & 31) == 0) sh.redq[tid >> 5] = best;
     __syncthreads();
     if (tid == 0) {
-      for (int w = 1; w < kMgThreads / 32; ++w) best = max(best, sh.redq[w]);
+      for (int w = 1; w < NT / 32; ++w) best = max(best, sh.redq[w]);
       const int64_t id = (int64_t)(~(uint32_t)best);
       if (T == 0.0 || U > 0.0) mg_write(a, row, id, 1.0f, 0);
       else mg_write(a, row, 0, id == 0 ? 1.0f : 0.0f, 0);  // r == 0 stops at index 0
@@ -242,14 +266,14 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
     return;
   }
   if (!(k >= 2 && (int64_t)k < a.V)) {  // no top-k: the nucleus from the candidates
-    mg_nucleus(a, sh, row, n, rw, T, P, U);
+    mg_nucleus<NT>(a, sh, row, n, rw, T, P, U);
     return;
   }
   // top-k: rank every candidate; the best min(n, k) are the row's top-k set
   const int m = min(n, k);
   const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
   const int npair = (n + 1) >> 1;
-  for (int i = tid; i < n; i += kMgThreads) {
+  for (int i = tid; i < n; i += NT) {
     const unsigned long long ci = sh.u.comp[i];
     int rank = 0;
     for (int j = 0; j < npair; ++j) {
@@ -266,10 +290,10 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   const double xmax = (double)key_to_float(sh.key[0]) / T;
   const double w = tid < m ? exp((double)key_to_float(sh.key[tid]) / T - xmax) : 0.0;
   double wex, winc, total;
-  block_scan<kMgThreads, double>(w, wex, winc, total, sh.redd);
+  block_scan<NT, double>(w, wex, winc, total, sh.redd);
   int nkeep = m;
   if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept (sampler.py:49-58)
-    const int first = block_min_i<kMgThreads>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
+    const int first = block_min_i<NT>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
     if (first != 0x7FFFFFFF) nkeep = first + 1;
   }
   // kept entries in index order
@@ -280,7 +304,7 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
     sh.kid[pos] = my;
     sh.u.kw[pos] = w;
   }
-  const double tot = block_sum<kMgThreads>(tid < nkeep ? w : 0.0, sh.redd);  // ends with a barrier
+  const double tot = block_sum<NT>(tid < nkeep ? w : 0.0, sh.redd);  // ends with a barrier
   // index-order inverse CDF (sampler.py:60-68)
   if (!(U > 0.0)) {  // r == 0 stops at index 0
     if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / tot), 0);
@@ -289,13 +313,18 @@ __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
   const double target = U * tot;
   const double kwv = tid < nkeep ? sh.u.kw[tid] : 0.0;
   double cex, cinc, ctot;
-  block_scan<kMgThreads, double>(kwv, cex, cinc, ctot, sh.redd);
-  const int who = block_min_i<kMgThreads>((tid < nkeep && kwv > 0.0 && cinc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  block_scan<NT, double>(kwv, cex, cinc, ctot, sh.redd);
+  const int who = block_min_i<NT>((tid < nkeep && kwv > 0.0 && cinc >= target) ? tid : 0x7FFFFFFF, sh.redi);
   if (tid == 0 && who == 0x7FFFFFFF) {  // ran past the end
     const int last = nkeep - 1;
     mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.u.kw[last] : 0.0) / tot), 0);
   }
   if (tid == who) mg_write(a, row, sh.kid[tid], (float)(kwv / tot), 0);
+}
+
+__global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {
+  __shared__ MgShared sh;
+  mg_row<kMgThreads>(a, sh, blockIdx.x);
 }
 
 }  // namespace ms

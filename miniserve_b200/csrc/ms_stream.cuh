@@ -53,7 +53,9 @@
 #include <cfloat>
 
 #include "ms_common.cuh"
+#include "ms_exchange.cuh"
 #include "ms_generic.cuh"
+#include "ms_shard.cuh"
 
 namespace ms {
 
@@ -1402,10 +1404,12 @@ __device__ __forceinline__ f2_t st_w2(f2_t v, f2_t C, f2_t NA) {
   return f2_pack(st_ex2(z0), st_ex2(z1));
 }
 
-template <int DT>
-__global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) {
-  extern __shared__ __align__(128) unsigned char st_raw[];
-  StShared &sh = *reinterpret_cast<StShared *>(st_raw);
+// One row of the streaming kernel (the CTA's row from st_pick_row).  XCH
+// (the fused peer exchange): prow is set to the row, whose record is
+// published after the body returns (every return past that point is
+// block-uniform).
+template <int DT, bool XCH>
+__device__ __forceinline__ void st_row_body(const SampleArgs &a, StShared &sh, int &prow) {
   // every CTA of this grid has started: a programmatic dependent launch (the
   // pending-row pass) may begin launching
   asm volatile("griddepcontrol.launch_dependents;");
@@ -1422,6 +1426,7 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
   bool joint;
   const int row = st_pick_row(sh, a, a.pairs ? a.rows : (int)gridDim.x, &joint);
   if (row < 0) return;
+  if constexpr (XCH) prow = row;  // shard mode: no pairs, every path writes the record
   const int crank = joint ? (int)st_crank() : 0;
   const int V = a.V;
   StRow r;
@@ -2600,5 +2605,78 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) 
     if (!(v > -INFINITY) || !(v > vc || (v == vc && g <= ic))) return 0.0;
     return rw(v);
   });
+}
+
+// The merge of a published row, on the CTA's candidate area (noinline: its
+// registers stay out of the streaming loops).
+__device__ __noinline__ void st_merge_published(MergeArgs m, int row) {
+  extern __shared__ __align__(128) unsigned char st_raw_m[];
+  StShared &sh = *reinterpret_cast<StShared *>(st_raw_m);
+  static_assert(sizeof(MgShared) <= sizeof(sh.w), "merge scratch fits the candidate area");
+  mg_row<kStThreads>(m, *reinterpret_cast<MgShared *>(&sh.w), row);
+}
+
+// Fused peer exchange of vocab-sharded sampling (ms_shard_exchange): after
+// the CTA wrote its record of `row` into this rank's slot of its own buffer,
+// the record is copied into the same slot of every other rank's buffer and
+// counted in the row's arrival counter on the row's home rank (row mod
+// nranks).  The CTA whose arrival completes the count (every rank's record
+// of the row is then in every buffer) merges the row from its own buffer
+// (mg_row) and writes the result entry into every rank's buffer, then counts
+// the row in every rank's done counter (ms_xfinish_kernel waits for it).
+// No wait: every step either stores or reads what has arrived.
+__device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, StShared &sh, int row) {
+  const int tid = threadIdx.x;
+  const int N = x.n, me = x.rank;
+  const int W = 4 + 2 * a.kmax;  // even
+  const int64_t roff = x.rec + ((int64_t)me * a.rows + row) * W;
+  __syncthreads();  // the record is written
+  if (N > 1) {
+    const uint2 *src = reinterpret_cast<const uint2 *>(x.peers[me] + roff);
+    for (int q = 1; q < N; ++q) {
+      uint2 *dst = reinterpret_cast<uint2 *>(x.peers[(me + q) % N] + roff);
+      for (int i = tid; i < W / 2; i += kStThreads) dst[i] = src[i];
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    __threadfence_system();  // the record's stores, every thread's, before the arrival
+    unsigned long long *cnt = reinterpret_cast<unsigned long long *>(x.peers[row % N] + x.cnt) + row;
+    const unsigned long long old = x_atom_add_acq_rel_sys(cnt, 1ull);
+    sh.bcast_i[0] = (old + 1ull) % (unsigned long long)N == 0ull ? 1 : 0;
+  }
+  __syncthreads();
+  if (!sh.bcast_i[0]) return;
+  // every rank's record of the row is in this buffer
+  MergeArgs m{x.peers[me] + x.rec, N, a.rows, a.kmax, a.Vg, a.temperature, a.top_k, a.top_p, a.uniforms,
+              nullptr, nullptr, nullptr};
+  m.xpeers = x.peers;
+  m.xout = x.out;
+  m.xepoch = x.epoch;
+  st_merge_published(m, row);
+  __syncthreads();  // the result entries are stored
+  if (tid == 0) {
+    __threadfence_system();
+    for (int q = 0; q < N; ++q) x_red_add_release_sys(reinterpret_cast<unsigned long long *>(x.peers[q]), 1ull);
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kStThreads, 2) ms_stream_kernel(SampleArgs a) {
+  extern __shared__ __align__(128) unsigned char st_raw[];
+  StShared &sh = *reinterpret_cast<StShared *>(st_raw);
+  int prow = -1;
+  st_row_body<DT, false>(a, sh, prow);
+}
+
+// The streaming kernel in vocab-sharded mode with the fused peer exchange
+// (one CTA per row): the row's record, then st_publish.
+template <int DT>
+__global__ void __launch_bounds__(kStThreads, 2) ms_stream_xkernel(SampleArgs a, XArgs x) {
+  extern __shared__ __align__(128) unsigned char st_raw[];
+  StShared &sh = *reinterpret_cast<StShared *>(st_raw);
+  int prow = -1;
+  st_row_body<DT, true>(a, sh, prow);
+  if (prow >= 0) st_publish(a, x, sh, prow);
 }
 }  // namespace ms

@@ -10,6 +10,13 @@ every rank, which finishes each row exactly as miniserve's
 ``Sampler.sample`` (miniserve/sampler.py:23-68) does on the whole vocabulary:
 the row's top-k set is contained in the union of the slices' top-k sets.
 
+With a peer exchange (``PeerExchange``, ``exchange="peer"``) steps 1-3 are
+fused: ``ms_shard_exchange`` stores each row's record into every rank's
+exchange buffer over NVLink as the row finishes, and the CTA whose record
+completes the row merges it in the same kernel and stores the result into
+every rank's buffer; ``ms_exchange_finish`` waits (bounded) for all rows'
+results.  No collective call is made on that path.
+
 A top-p row without top-k is settled from the records too when its nucleus
 lies among the candidates (the records carry each slice's softmax total);
 rows the records cannot carry exactly (top_k above kmax, top_p >= 1 without
@@ -83,6 +90,118 @@ def exchange_records(records, group=None):
     return out.view((world,) + tuple(records.shape))
 
 
+class _RawInt32:
+    """A CUDA array interface over raw device memory, for a tensor view."""
+
+    def __init__(self, ptr: int, shape: Tuple[int, ...]) -> None:
+        self.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": "<i4",
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+class PeerExchangeError(RuntimeError):
+    pass
+
+
+class PeerExchange:
+    """Exchange buffers of the fused peer exchange (``ms_shard_exchange``):
+    one zeroed device block per rank, mapped into every other rank's process
+    by CUDA IPC (no multicast object).  Collective: every rank of ``group``
+    constructs it with the same capacities; all ranks agree on success (the
+    constructor raises PeerExchangeError on every rank when any rank fails).
+    ``timeout_s`` bounds each call's wait for the other ranks' results."""
+
+    def __init__(self, Bcap: int, kmax_cap: int, group=None, device=None, timeout_s: float = 10.0) -> None:
+        import ctypes
+        torch = _torch()
+        self.group = group
+        self.world, self.rank = _world(group)
+        self.Bcap, self.kmax_cap = int(Bcap), int(kmax_cap)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        L = _lib.lib()
+        words = L.ms_exchange_words(self.Bcap, self.world, self.kmax_cap)
+        if words < 0:
+            raise ValueError("exchange capacity out of range")
+        self.words = int(words)
+        self.local = None
+        self._opened = []
+        self.epoch = 0
+        self.done = 0
+        self.broken = False
+        err = None
+        handle = b""
+        with torch.cuda.device(self.device):
+            ptr = ctypes.c_void_p()
+            rc = L.ms_device_alloc(self.words * 4, ctypes.byref(ptr))
+            if rc == _lib.MS_OK:
+                self.local = ptr.value
+                if self.world > 1:
+                    h = ctypes.create_string_buffer(64)
+                    rc = L.ms_ipc_handle(self.local, h)
+                    handle = h.raw if rc == _lib.MS_OK else b""
+            if rc != _lib.MS_OK:
+                err = f"exchange buffer: {L.ms_error_string(rc).decode()}"
+            peers = [0] * self.world
+            peers[self.rank] = self.local or 0
+            if self.world > 1:
+                import torch.distributed as dist
+                handles = [None] * self.world
+                dist.all_gather_object(handles, handle, group=group)
+                for q in range(self.world):
+                    if q == self.rank or err is not None:
+                        continue
+                    if len(handles[q]) != 64:
+                        err = f"rank {q} has no exchange buffer"
+                        continue
+                    p = ctypes.c_void_p()
+                    rc = L.ms_ipc_open(handles[q], ctypes.byref(p))
+                    if rc != _lib.MS_OK:
+                        err = f"CUDA IPC open of rank {q}: {L.ms_error_string(rc).decode()}"
+                        continue
+                    self._opened.append(p.value)
+                    peers[q] = p.value
+                errs = [None] * self.world
+                dist.all_gather_object(errs, err, group=group)
+                err = next((e for e in errs if e is not None), None)
+            if err is not None:
+                self._release()
+                raise PeerExchangeError(err)
+            self.peers = torch.tensor(peers, dtype=torch.int64, device=self.device)
+
+    def fits(self, B: int, kmax: int) -> bool:
+        return B <= self.Bcap and kmax <= self.kmax_cap and not self.broken
+
+    def records(self, B: int, kmax: int, epoch: int):
+        """[world, B, 4 + 2 kmax] int32 view of call ``epoch``'s records in
+        this rank's buffer (the all-gather layout)."""
+        torch = _torch()
+        off = _lib.lib().ms_exchange_records_offset(self.Bcap, self.world, self.kmax_cap, epoch)
+        shape = (self.world, B, record_words(kmax))
+        return torch.as_tensor(_RawInt32(self.local + 4 * off, shape), device=self.device)
+
+    def _release(self) -> None:
+        L = _lib.lib()
+        for p in self._opened:
+            L.ms_ipc_close(p)
+        self._opened = []
+        if self.local:
+            L.ms_device_free(self.local)
+            self.local = None
+
+    def close(self) -> None:
+        """Unmap and free the buffers once no call is in flight on any rank
+        (device synchronize and a barrier first).  Collective."""
+        torch = _torch()
+        if self.local is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            if self.world > 1:
+                import torch.distributed as dist
+                dist.barrier(group=self.group)
+            self._release()
+
+
 def _world(group=None) -> Tuple[int, int]:
     """(world size, rank) of the group, (1, 0) without a process group."""
     import torch.distributed as dist
@@ -123,14 +242,51 @@ def gather_rows(logits_slice, rows, V: int, group=None):
 class ShardedSampler:
     """Sample [B, V] rows whose vocabulary is split across the ranks of `group`."""
 
-    def __init__(self, V: int, group=None) -> None:
+    def __init__(self, V: int, group=None, exchange: str = "nccl", peer_timeout_s: float = 10.0) -> None:
+        """``exchange``: "nccl" (all-gather of the records and a merge
+        kernel), "peer" (the fused peer exchange; PeerExchangeError if CUDA
+        IPC is unavailable) or "auto" (peer when available, else nccl; the
+        choice is the same on every rank)."""
+        if exchange not in ("auto", "peer", "nccl"):
+            raise ValueError("exchange must be 'auto', 'peer' or 'nccl'")
         self.V = int(V)
         self.group = group
+        self.exchange = exchange
+        self.peer_timeout_s = float(peer_timeout_s)
+        self._x = None
+        self.last_exchange = None  # "peer" or "nccl": the path the last call took
         self._single = Sampler()
         # rows of the last call finished by the distributed nucleus, and rows
         # that took the full-row path (gathered logits)
         self.last_nucleus_rows = 0
         self.last_full_rows = 0
+
+    def _peer(self, B: int, kmax: int, dev):
+        """The peer exchange for a call of B rows and record width kmax, (re)made
+        when it does not fit; None on the nccl path."""
+        if self.exchange == "nccl":
+            return None
+        if self._x is not None and self._x.fits(B, kmax):
+            return self._x
+        if self._x is not None:
+            if self._x.broken:
+                raise PeerExchangeError("the peer exchange timed out in an earlier call")
+            self._x.close()
+            self._x = None
+        try:
+            self._x = PeerExchange(max(B, 256), max(kmax, KMAX_NUCLEUS), self.group, dev, self.peer_timeout_s)
+        except PeerExchangeError:
+            if self.exchange == "peer":
+                raise
+            self.exchange = "nccl"
+            return None
+        return self._x
+
+    def close(self) -> None:
+        """Release the peer exchange buffers (collective)."""
+        if self._x is not None:
+            self._x.close()
+            self._x = None
 
     def sample(self, logits_slice, v0: int, temperature=1.0, top_k=0, top_p=1.0,
                uniforms=None, seeds: Optional[Sequence[Optional[int]]] = None,
@@ -145,7 +301,9 @@ class ShardedSampler:
         their values are read back once.  After the merge one device->host read
         of a count decides whether any row needs the full-row path.
         ``events``: optional four CUDA events recorded around the shard pass,
-        the all-gather and the merge (for timing the phases)."""
+        the all-gather and the merge (for timing the phases); with the peer
+        exchange: before and after the fused kernel and after the finish
+        (the last two events together)."""
         torch = _torch()
         if logits_slice.dim() != 2 or not logits_slice.is_cuda:
             raise ValueError("logits_slice must be a [B, Vloc] CUDA tensor")
@@ -178,10 +336,37 @@ class ShardedSampler:
         mask_ptr, mask_ld = None, 0
         if mask is not None:
             mask_ptr, mask_ld = check_mask(mask, B, Vloc, dev)
-        records = torch.empty((B, W), dtype=torch.int32, device=dev)
         tokens = torch.empty(B, dtype=torch.int64, device=dev)
         probs = torch.empty(B, dtype=torch.float32, device=dev)
         status = torch.empty(B, dtype=torch.int32, device=dev)
+        x = self._peer(B, kmax, dev) if B > 0 else None
+        self.last_exchange = "peer" if x is not None else "nccl"
+        if x is not None:
+            with torch.cuda.device(dev):
+                cur = torch.cuda.current_stream(dev)
+                stream = cur.cuda_stream
+                x.epoch += 1
+                x.done += B
+                epoch = (x.epoch - 1) % (2 ** 32 - 2) + 1  # parity alternates across the wrap
+                if events is not None:
+                    events[0].record(cur)
+                rc = L.ms_shard_exchange(logits_slice.data_ptr(), dtype, B, Vloc, logits_slice.stride(0), int(v0),
+                                         self.V, T.data_ptr(), K.data_ptr(), P.data_ptr(), U.data_ptr(), mask_ptr,
+                                         mask_ld, kmax, x.local, x.peers.data_ptr(), x.rank, x.world, x.Bcap,
+                                         x.kmax_cap, epoch, stream)
+                _lib.check(rc, "ms_shard_exchange")
+                if events is not None:
+                    events[1].record(cur)
+                rc = L.ms_exchange_finish(x.local, B, x.Bcap, x.done % 2 ** 64, epoch, x.timeout_ns,
+                                          tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
+                _lib.check(rc, "ms_exchange_finish")
+                if events is not None:
+                    events[2].record(cur)
+                    events[3].record(cur)
+            allrec = x.records(B, kmax, epoch)
+            return self._finish(logits_slice, dtype, v0, allrec, kmax, T, K, P, U, mask, mask_ptr, mask_ld,
+                                tokens, probs, status, x)
+        records = torch.empty((B, W), dtype=torch.int32, device=dev)
         with torch.cuda.device(dev):
             cur = torch.cuda.current_stream(dev)
             stream = cur.cuda_stream
@@ -203,12 +388,26 @@ class ShardedSampler:
             _lib.check(rc, "ms_shard_merge")
             if events is not None:
                 events[3].record(cur)
+        return self._finish(logits_slice, dtype, v0, allrec, kmax, T, K, P, U, mask, mask_ptr, mask_ld,
+                            tokens, probs, status, None)
+
+    def _finish(self, logits_slice, dtype, v0, allrec, kmax, T, K, P, U, mask, mask_ptr, mask_ld, tokens, probs,
+                status, x):
+        """The flagged rows of a merged call: the distributed nucleus, then
+        the full-row path for what is left."""
+        torch = _torch()
+        Vloc = logits_slice.shape[1]
         flagged = (status & (_lib.MS_ROW_UNSUPPORTED | _lib.MS_ROW_NONFINITE)) != 0
         # rows without top-k the records could not settle: the distributed
         # nucleus (no logits exchanged); the statuses are identical on every
         # rank, so are these counts and branches
         nuc = flagged & ((status & _lib.MS_ROW_NONFINITE) == 0) & ((K <= 0) | (K >= self.V))
-        n_flagged, n_nuc = (int(v) for v in torch.stack([flagged.sum(), nuc.sum()]).tolist())
+        late = (status & _lib.MS_ROW_PEER_TIMEOUT) != 0
+        n_flagged, n_nuc, n_late = (int(v) for v in torch.stack([flagged.sum(), nuc.sum(), late.sum()]).tolist())
+        if n_late:
+            x.broken = True
+            raise PeerExchangeError(f"{n_late} rows had no result from the other ranks within "
+                                    f"{self.peer_timeout_s} s")
         self.last_nucleus_rows = 0
         if (n_nuc and kmax >= 2 and Vloc <= NUCLEUS_MAX_SLICE and self.V <= NUCLEUS_MAX_V
                 and allrec.shape[0] <= NUCLEUS_MAX_RANKS):

@@ -1,8 +1,10 @@
-"""torchrun worker: vocab-sharded sampling over NCCL, one process per GPU.
+"""torchrun worker: vocab-sharded sampling, one process per GPU.
 
 Each rank holds its contiguous slice of the config-5 rows (B=128 here,
-V=256000), samples through ShardedSampler, and rank 0 checks the tokens
-against the oracle on the full rows.  Run by tests/test_gpu_sharded.py."""
+V=256000), samples through ShardedSampler with the fused peer exchange (CUDA
+IPC buffers, NVLink peer stores) and with the NCCL all-gather path, and rank
+0 checks the tokens against the oracle on the full rows and the two paths
+against each other.  Run by tests/test_gpu_sharded.py."""
 import datetime
 import os
 import sys
@@ -37,22 +39,33 @@ def main():
         T[8:12] = 1.5
         v0, v1 = sharded.shard_bounds(V, world, rank)
         part = torch.from_numpy(np.ascontiguousarray(b.logits[:, v0:v1])).cuda()
-        s = sharded.ShardedSampler(V)
-        tok, prob, st = s.sample(part, v0, T, K, P, uniforms=b.uniforms)
-        torch.cuda.synchronize()
-        # rows 0 and 4-11 (no top-k) finish without logits crossing ranks;
-        # row 2 (top_k 300, above the record width) takes the full-row path
-        assert s.last_full_rows <= 1 and s.last_nucleus_rows >= 4, (s.last_full_rows, s.last_nucleus_rows)
-        tok = tok.cpu().numpy()
-        # every rank must hold the same tokens
-        t_all = [torch.empty(B, dtype=torch.int64, device="cuda") for _ in range(world)]
-        dist.all_gather(t_all, torch.from_numpy(tok).cuda())
-        same = all(np.array_equal(t.cpu().numpy(), tok) for t in t_all)
+        results = {}
+        # the fused peer exchange (three calls: both record areas) and the
+        # all-gather path must give the same tokens
+        for mode in ("peer", "nccl"):
+            s = sharded.ShardedSampler(V, exchange=mode)
+            for call in range(3 if mode == "peer" else 1):
+                tok, prob, st = s.sample(part, v0, T, K, P, uniforms=b.uniforms)
+                torch.cuda.synchronize()
+            # rows 0 and 4-11 (no top-k) finish without logits crossing ranks;
+            # row 2 (top_k 300, above the record width) takes the full-row path
+            assert s.last_full_rows <= 1 and s.last_nucleus_rows >= 4, (s.last_full_rows, s.last_nucleus_rows)
+            assert s.last_exchange == mode
+            s.close()
+            tok = tok.cpu().numpy()
+            # every rank must hold the same tokens
+            t_all = [torch.empty(B, dtype=torch.int64, device="cuda") for _ in range(world)]
+            dist.all_gather(t_all, torch.from_numpy(tok).cuda())
+            same = all(np.array_equal(t.cpu().numpy(), tok) for t in t_all)
+            results[mode] = (tok, prob.cpu().numpy(), st.cpu().numpy())
+            if rank == 0:
+                from parity import compare
+                compare(tok, results[mode][1].astype(np.float64), results[mode][2], b.logits, T, K, P,
+                        b.uniforms, label=f"{mode} x{world}")
+                assert same, f"ranks disagree ({mode})"
+        for a, c in zip(results["peer"], results["nccl"]):
+            assert np.array_equal(a, c), "peer exchange and all-gather paths disagree"
         if rank == 0:
-            from parity import compare
-            compare(tok, prob.cpu().numpy().astype(np.float64), st.cpu().numpy(), b.logits, T, K, P,
-                    b.uniforms, label=f"nccl x{world}")
-            assert same, "ranks disagree"
             print("sharded ok", world, flush=True)
     finally:
         dist.destroy_process_group()
