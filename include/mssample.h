@@ -43,7 +43,9 @@ enum {
   MS_E_INVALID = -1,     /* null pointer, B < 0, V < 1, ld < V, V >= 2^31 ... */
   MS_E_DTYPE = -2,       /* dtype not MS_DTYPE_F32 / MS_DTYPE_BF16 */
   MS_E_CUDA = -3,        /* a CUDA call failed (see ms_last_cuda_error) */
-  MS_E_UNSUPPORTED = -4  /* valid request outside what this build handles */
+  MS_E_UNSUPPORTED = -4, /* valid request outside what this build handles */
+  MS_E_TOO_LARGE = -5    /* a size beyond the fixed device array of
+                            ms_build_json_mask_noalloc (V > 262144) */
 };
 
 enum { MS_DTYPE_F32 = 0, MS_DTYPE_BF16 = 1 };
@@ -319,6 +321,28 @@ int ms_json_pack_vocab_ordered(const uint8_t *vocab_bytes, const int64_t *vocab_
 int ms_build_json_mask_ordered(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
                                const int64_t *vocab_off, const uint32_t *packed, const uint8_t *lens,
                                const int32_t *order, int64_t V, uint32_t *mask, int64_t mask_ld,
+                               int32_t *row_status, ms_stream_t stream);
+
+/*
+ * ms_build_json_mask without any device allocation by anyone: the
+ * fixed-width vocabulary copy that ms_build_json_mask_packed reads from
+ * caller memory lives here in a device array inside the library (4.25 MB,
+ * allocated when the library is loaded and held by every GPU that loads it
+ * until the process exits), repacked from vocab_bytes / vocab_off on every
+ * call.  For callers that cannot allocate device memory themselves: a
+ * runtime that owns the whole device through its own memory pool, or a
+ * plugin that has no device allocator it may call.  The caller passes the
+ * same inputs and outputs as ms_build_json_mask and gets the same mask and
+ * row_status.  V <= 262144 (MS_E_TOO_LARGE beyond).  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.
+ * Every call uses the one array: calls that can overlap on the GPU (other
+ * streams, other host threads) race and must be serialized by the caller.
+ * No counterpart in the reference (miniserve has no device code); an
+ * addition to this library's interface.
+ */
+int ms_build_json_mask_noalloc(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                               const int64_t *vocab_off, int64_t V, uint32_t *mask, int64_t mask_ld,
                                int32_t *row_status, ms_stream_t stream);
 
 /*

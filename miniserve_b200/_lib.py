@@ -13,6 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libmssample.so")
 
 MS_OK = 0
+MS_E_TOO_LARGE = -5
 MS_DTYPE_F32 = 0
 MS_DTYPE_BF16 = 1
 MS_ROW_OK = 0
@@ -49,6 +50,7 @@ SIGNATURES = {
                                       _P, _P]),
     "ms_nucleus_draw": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _P,
                                        ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, ctypes.c_int32, _P, _P]),
+    "ms_build_json_mask_noalloc": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _P]),
     "ms_mask_from_logits": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _P, _I64, _P]),
     "ms_shard_record_words": (_I64, [ctypes.c_int32]),
     "ms_shard_merge": (ctypes.c_int, [_P, ctypes.c_int32, _I64, ctypes.c_int32, _I64, _P, _P, _P, _P,

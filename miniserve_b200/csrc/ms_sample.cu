@@ -128,6 +128,7 @@ const char *ms_error_string(int code) {
     case MS_E_DTYPE: return "unsupported dtype (expected MS_DTYPE_F32 or MS_DTYPE_BF16)";
     case MS_E_CUDA: return "CUDA error (see ms_last_cuda_error)";
     case MS_E_UNSUPPORTED: return "request outside what this build supports";
+    case MS_E_TOO_LARGE: return "size beyond the fixed device array of the no-alloc entry point (V > 262144)";
     default: return "unknown error";
   }
 }
@@ -598,6 +599,56 @@ int ms_build_json_mask_ordered(const uint32_t *states, int64_t B, const uint8_t 
                                int32_t *row_status, ms_stream_t stream) {
   if (!packed || !lens || !order) return MS_E_INVALID;
   return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, order, V, mask, mask_ld, row_status,
+                         stream);
+}
+
+// ------------------------------------------------ no-alloc JSON mask build
+namespace {
+// The fixed-width vocabulary tables of ms_build_json_mask_noalloc: up to
+// kNoAllocMaxV tokens of 16 bytes, then their lengths.  File-scope device
+// memory: created with the module on every GPU that loads the library and
+// held until the process exits.  Nothing in it needs to start at zero: each
+// call rewrites the entries of its V tokens before the mask kernel reads them.
+constexpr int64_t kNoAllocMaxV = 262144;
+constexpr size_t kNoAllocPackedBytes = (size_t)kNoAllocMaxV * 16;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPackedBytes + kNoAllocMaxV];
+
+std::atomic<unsigned char *> g_noalloc_ptr[kMaxDevices];
+
+// The array's device address on the current device.  In host code its name
+// only stands in for it, so the address is looked up (once per device, with
+// that device current) and passed to the kernels.
+int noalloc_scratch(unsigned char **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return MS_E_UNSUPPORTED;
+  unsigned char *p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    e = cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return MS_OK;
+}
+}  // namespace
+
+int ms_build_json_mask_noalloc(const uint32_t *states, int64_t B, const uint8_t *vocab_bytes,
+                               const int64_t *vocab_off, int64_t V, uint32_t *mask, int64_t mask_ld,
+                               int32_t *row_status, ms_stream_t stream) {
+  if (V > kNoAllocMaxV) return MS_E_TOO_LARGE;
+  if (B < 0 || B > 65535 || V < 1 || mask_ld < (V + 31) / 32) return MS_E_INVALID;
+  if (B == 0) return MS_OK;
+  if (!states || !vocab_bytes || !vocab_off || !mask || !row_status) return MS_E_INVALID;
+  unsigned char *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != MS_OK) return rc;
+  uint32_t *packed = reinterpret_cast<uint32_t *>(scratch);
+  uint8_t *lens = scratch + kNoAllocPackedBytes;
+  rc = pack_vocab(vocab_bytes, vocab_off, V, nullptr, packed, lens, stream);
+  if (rc != MS_OK) return rc;
+  return build_json_mask(states, B, vocab_bytes, vocab_off, packed, lens, nullptr, V, mask, mask_ld, row_status,
                          stream);
 }
 
