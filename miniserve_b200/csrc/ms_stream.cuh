@@ -2640,7 +2640,7 @@ __device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, 
     __syncthreads();
   }
   if (tid == 0) {
-    __threadfence_system();  // the record's stores, every thread's, before the arrival
+    // release (cumulative over the CTA's stores before the barrier) and acquire
     unsigned long long *cnt = reinterpret_cast<unsigned long long *>(x.peers[row % N] + x.cnt) + row;
     const unsigned long long old = x_atom_add_acq_rel_sys(cnt, 1ull);
     sh.bcast_i[0] = (old + 1ull) % (unsigned long long)N == 0ull ? 1 : 0;
@@ -2655,8 +2655,7 @@ __device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, 
   m.xepoch = x.epoch;
   st_merge_published(m, row);
   __syncthreads();  // the result entries are stored
-  if (tid == 0) {
-    __threadfence_system();
+  if (tid == 0) {  // each a release, cumulative over the entries stored before the barrier
     for (int q = 0; q < N; ++q) x_red_add_release_sys(reinterpret_cast<unsigned long long *>(x.peers[q]), 1ull);
   }
 }
