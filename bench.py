@@ -317,9 +317,9 @@ def sharded_line(args, rank, world, dev, peak):
     vocabulary split into contiguous slices over the ranks, sampled through
     ShardedSampler.sample: the default path (shard pass, NCCL all-gather of
     the candidate records, merge kernel), and beside it the fused peer
-    exchange (one streaming kernel that stores each row's record into every
-    rank's buffer over NVLink and merges the rows it completes, then a finish
-    kernel that waits for every row's result).  Strong scaling: the same rows
+    exchange (the streaming kernel stores each row's record and an arrival
+    flag into every rank's buffer over NVLink; the merge kernel waits for
+    each row's flags).  Strong scaling: the same rows
     on every N.  Each phase timed with CUDA events on the launching stream;
     the step time is the max over ranks."""
     import torch
@@ -374,7 +374,8 @@ def sharded_line(args, rank, world, dev, peak):
     if used == "peer":
         line["peer_exchange"] = {
             "value": round(B / (p_step / 1e3), 1), "unit": "rows/s", "ms_per_step": round(p_step, 5),
-            "phase_us": {"fused_shard_exchange_merge": round(p_kernel * 1e3, 2), "finish": round(p_finish * 1e3, 2)},
+            "phase_us": {"shard_pass_with_peer_stores": round(p_kernel * 1e3, 2),
+                         "merge_with_flag_wait": round(p_finish * 1e3, 2)},
             "peer_bytes_per_rank": B * sharded.record_words(50) * 4 * max(world - 1, 0), "rows_flagged": p_flagged}
     else:
         line["peer_exchange"] = {"unavailable": "CUDA IPC mapping of the exchange buffers failed"}

@@ -63,9 +63,9 @@ enum {
                                  full vocabulary (top_k off or above kmax,
                                  a tie block past the candidate buffer, a
                                  non-finite logit); token -1 */
-  MS_ROW_PEER_TIMEOUT = 16    /* fused peer exchange only: the row's result
-                                 had not arrived when ms_exchange_finish
-                                 gave up waiting (a rank missing); token -1 */
+  MS_ROW_PEER_TIMEOUT = 16    /* fused peer exchange only: a rank's record
+                                 of the row had not arrived when
+                                 ms_exchange_merge gave up waiting; token -1 */
 };
 
 /*
@@ -150,34 +150,31 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
                    ms_stream_t stream);
 
 /*
- * Fused peer exchange: steps 1-3 above as one streaming kernel per rank plus
- * a short finish kernel, with no collective call.  Each rank owns an
- * exchange buffer (ms_exchange_words words, zeroed, 16-byte aligned) that
- * every other rank has mapped (ms_ipc_handle / ms_ipc_open); peers: device
- * array [nranks] of the buffers' addresses as seen from this rank
+ * Fused peer exchange: steps 1-3 above without a collective call.  Each rank
+ * owns an exchange buffer (ms_exchange_words words, zeroed, 16-byte aligned)
+ * that every other rank has mapped (ms_ipc_handle / ms_ipc_open); peers:
+ * device array [nranks] of the buffers' addresses as seen from this rank
  * (peers[rank] = its own).  Per call, every rank, same arguments except the
  * slice and rank:
  *
  *   1. ms_shard_exchange: the slice's records (as ms_shard_candidates) are
- *      stored into every rank's buffer over NVLink as each row finishes; the
- *      CTA whose record completes a row's arrival count merges the row (as
- *      ms_shard_merge) and stores the result into every rank's buffer.
- *   2. ms_exchange_finish: waits (at most timeout_ns) until every row's
- *      result has arrived in this rank's buffer, then writes tokens, probs
- *      and statuses; rows missing at the timeout: token -1,
- *      MS_ROW_PEER_TIMEOUT.
+ *      stored into every rank's buffer over NVLink as each row finishes,
+ *      each followed by the row's arrival flag.
+ *   2. ms_exchange_merge: row by row, waits (at most timeout_ns; a stalled
+ *      batch up to about twice that) for every rank's flag of the row, then
+ *      merges it as ms_shard_merge does; rows whose flags did not all
+ *      arrive: token -1, MS_ROW_PEER_TIMEOUT.
  *
  * epoch: the call's number, 1, 2, ... in order on every rank (with a fresh
- * buffer; it may wrap to 1 after an even number); done_target: the sum of B
- * over the calls so far, this one included.  Bcap / kmax_cap: the buffer's
- * capacity (B <= Bcap, kmax <= kmax_cap).  The call's records stay readable
- * in every buffer, at word ms_exchange_records_offset, in the all-gather
- * layout [nranks][B][rec_words] (the distributed nucleus reads them) until
- * the call after next starts.  Rows flagged MS_ROW_UNSUPPORTED /
- * MS_ROW_NONFINITE take the same paths as after ms_shard_merge.
- * nranks * kmax <= 2048, nranks <= 256, B <= 2^20.  Replaces the
- * all-gather + merge of the records (no counterpart in the reference, which
- * samples on one device: miniserve/sampler.py:23-68).
+ * buffer; it may wrap to 1 after an even number).  Bcap / kmax_cap: the
+ * buffer's capacity (B <= Bcap, kmax <= kmax_cap, the same on every rank).
+ * The call's records stay readable in every buffer, at word
+ * ms_exchange_records_offset, in the all-gather layout
+ * [nranks][B][rec_words] (the distributed nucleus reads them) until the call
+ * after next starts.  Rows flagged MS_ROW_UNSUPPORTED / MS_ROW_NONFINITE take
+ * the same paths as after ms_shard_merge.  nranks * kmax <= 2048, nranks <=
+ * 256, B <= 2^20.  Replaces the all-gather of the records (no counterpart in
+ * the reference, which samples on one device: miniserve/sampler.py:23-68).
  */
 int64_t ms_exchange_words(int64_t Bcap, int32_t nranks, int32_t kmax_cap);
 int64_t ms_exchange_records_offset(int64_t Bcap, int32_t nranks, int32_t kmax_cap, uint32_t epoch);
@@ -186,8 +183,10 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
                       const uint32_t *mask, int64_t mask_ld, int32_t kmax, uint32_t *xbuf, uint32_t *const *peers,
                       int32_t rank, int32_t nranks, int64_t Bcap, int32_t kmax_cap, uint32_t epoch,
                       ms_stream_t stream);
-int ms_exchange_finish(const uint32_t *xbuf, int64_t B, int64_t Bcap, uint64_t done_target, uint32_t epoch,
-                       int64_t timeout_ns, int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);
+int ms_exchange_merge(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+                      int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
+                      const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
+                      int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);
 
 /*
  * Device memory for an exchange buffer and its CUDA IPC mapping into the

@@ -281,7 +281,7 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
   a.v0 = v0;
   a.Vg = V;
   a.rows = (int)B;
-  const ms::XArgs x{peers, rank, nranks, epoch, L.cnt, L.out, rec};
+  const ms::XArgs x{peers, rank, nranks, epoch, L.flags, rec};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -291,17 +291,23 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
   return MS_OK;
 }
 
-int ms_exchange_finish(const uint32_t *xbuf, int64_t B, int64_t Bcap, uint64_t done_target, uint32_t epoch,
-                       int64_t timeout_ns, int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
-  if (B < 0 || B > Bcap || Bcap > (1 << 20) || timeout_ns < 0 || epoch == 0u) return MS_E_INVALID;
+int ms_exchange_merge(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+                      int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
+                      const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
+                      int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
+  if (ms_exchange_words(Bcap, nranks, kmax_cap) < 0 || B < 0 || B > Bcap || kmax < 1 || kmax > kmax_cap ||
+      V < 1 || V > 0x7FFFFFFFll - 4096 || timeout_ns < 0 || epoch == 0u)
+    return MS_E_INVALID;
+  if ((int64_t)nranks * kmax > ms::kMgCap) return MS_E_UNSUPPORTED;
   if (B == 0) return MS_OK;
-  if (!xbuf || !tokens || !probs || !row_status) return MS_E_INVALID;
-  if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
+  if (!xbuf || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
+    return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const ms::XLayout L = ms::x_layout(Bcap, 1, 1);  // the counter and entry offsets depend on Bcap only
-  const int grid = (int)((B + ms::kXThreads - 1) / ms::kXThreads);
-  ms::ms_xfinish_kernel<<<dim3((unsigned)(grid < 64 ? grid : 64)), dim3(ms::kXThreads), 0, s>>>(
-      xbuf, L.out, (int)B, (unsigned long long)done_target, epoch, timeout_ns, tokens, probs, row_status);
+  const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
+  const int64_t rec = L.rec0 + (int64_t)(epoch & 1u) * L.half;
+  ms::MergeArgs a{xbuf + rec, nranks, (int)B, kmax, V, temperature, top_k, top_p, uniforms,
+                  tokens, probs, row_status};
+  ms::ms_xmerge_kernel<<<dim3((unsigned)B), dim3(ms::kMgThreads), 0, s>>>(a, xbuf + L.flags, epoch, timeout_ns);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;

@@ -10,9 +10,8 @@
 // largest value has every larger value of the row among the candidates;
 // otherwise the row is flagged MS_ROW_UNSUPPORTED.
 //
-// The row merge (mg_row) runs as its own kernel after an all-gather, or
-// inside the streaming kernel for the fused peer exchange (ms_exchange.cuh),
-// where the results go to every rank's exchange buffer.
+// The row merge (mg_row) runs after an all-gather (ms_merge_kernel) or on
+// the records of the fused peer exchange (ms_xmerge_kernel, ms_exchange.cuh).
 #pragma once
 
 #include "ms_common.cuh"
@@ -38,28 +37,18 @@ struct MergeArgs {
   int64_t *tokens;
   float *probs;
   int32_t *status;
-  // fused peer exchange: the result of row r goes, as one 16-byte entry
-  // {token, prob bits, status, epoch} at word xout + 4 r, to every rank's
-  // exchange buffer instead of tokens / probs / status
-  uint32_t *const *xpeers = nullptr;
-  int64_t xout = 0;
-  uint32_t xepoch = 0;
 };
 
 struct MgShared {
   union {
-    unsigned long long comp[kMgCap + 2];  // (key, ~id) composites per slot r * kmax + i (0: empty), padded
+    unsigned long long comp[kMgCap + 2];  // (key, ~id) composites, padded for paired reads
     double kw[kMgCap];                    // after the ranking: kept weights in index order
   } u;
-  uint32_t key[kMgCap];  // keys: per-rank slots (r * kmax + i) as loaded, in rank order in the nucleus path
-  int id[kMgCap];        // their global ids, likewise
+  uint32_t key[kMgCap];  // candidates in rank order
+  int id[kMgCap];
   int kid[kMgCap];       // kept ids in index order
-  int off[kMgRanks + 1]; // per-rank candidate counts
-  uint32_t tkey[kMgTopK];  // top-k rows: the row's top-k set in rank order
-  int tidx[kMgTopK];
-  double tw[kMgTopK];      // their weights
+  int off[kMgRanks + 1];
   uint32_t st;
-  int n;
   float cut;             // the largest kmax-th value of a full slice
   double redd[33];
   int redi[33];
@@ -67,18 +56,13 @@ struct MgShared {
 };
 
 __device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok, float prob, int32_t st) {
-  if (a.xpeers) {
-    const uint4 e = make_uint4((uint32_t)(int32_t)tok, __float_as_uint(prob), (uint32_t)st, a.xepoch);
-    for (int q = 0; q < a.nranks; ++q) *reinterpret_cast<uint4 *>(a.xpeers[q] + a.xout + 4 * (size_t)r) = e;
-    return;
-  }
   a.tokens[r] = tok;
   a.probs[r] = prob;
   a.status[r] = st;
 }
 
-// Rank r's record of `row`; read through L2 (records written by other GPUs
-// into the fused exchange buffer are never served from a stale L1 line).
+// Rank r's record of `row`; read through L2 (records that other GPUs wrote
+// into a fused exchange buffer are never served from a stale L1 line).
 __device__ __forceinline__ const uint32_t *mg_rec(const MergeArgs &a, int r, int row, size_t rw) {
   return a.records + ((size_t)r * a.B + row) * rw;
 }
@@ -91,19 +75,18 @@ __device__ __forceinline__ uint32_t mg_ld(const uint32_t *p) { return __ldcg(p);
 // kmax-th largest value; the index-order draw over the kept prefix.  The
 // composites of the n candidates are in sh.u.comp.  All threads.
 template <int NT>
-__device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, int ns, size_t rw, double T, double P,
+__device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, size_t rw, double T, double P,
                            double U) {
   const int tid = threadIdx.x;
   if (!(P < 1.0)) {  // the full softmax draw needs every logit
     if (tid == 0) mg_write(a, row, -1, 0.0f, MS_ROW_UNSUPPORTED);
     return;
   }
-  // rank every candidate (all distinct composites; a zero slot is empty)
+  // rank every candidate (all distinct composites)
   const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
-  const int npair = (ns + 1) >> 1;
-  for (int i = tid; i < ns; i += NT) {
+  const int npair = (n + 1) >> 1;
+  for (int i = tid; i < n; i += NT) {
     const unsigned long long ci = sh.u.comp[i];
-    if (ci == 0ull) continue;
     int rank = 0;
     for (int j = 0; j < npair; ++j) {
       const ulonglong2 q = c2[j];
@@ -207,153 +190,47 @@ __device__ void mg_nucleus(const MergeArgs &a, MgShared &sh, int row, int n, int
   }
 }
 
-// Warp-wide exclusive prefix and total of one double per lane.
-__device__ __forceinline__ void mg_warp_scan(double v, double &ex, double &tot) {
-  const int lane = threadIdx.x & 31;
-  double inc = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-    if (lane >= o) inc += t;
-  }
-  tot = __shfl_sync(0xFFFFFFFFu, inc, 31);
-  ex = __shfl_up_sync(0xFFFFFFFFu, inc, 1);
-  if (lane == 0) ex = 0.0;
-}
-
-// A top-k row's finish by one warp (miniserve/sampler.py:35-68): the m
-// entries of sh.tkey / sh.tidx in rank order, float64 weights
-// exp(l/T - max/T), the smallest rank prefix reaching top_p (crossing entry
-// kept), then the index-order inverse CDF over the kept entries.  Each lane
-// takes a contiguous block of ranks (then of index-order positions).
-__device__ __noinline__ void mg_topk_warp(const MergeArgs &a, MgShared &sh, int row, int m, double T, double P,
-                                          double U) {
-  const int lane = threadIdx.x & 31;
-  const double xmax = (double)key_to_float(sh.tkey[0]) / T;
-  const int c = (m + 31) >> 5;
-  const int j0 = min(m, lane * c), j1 = min(m, j0 + c);
-  double s = 0.0;
-  for (int j = j0; j < j1; ++j) {
-    const double w = exp((double)key_to_float(sh.tkey[j]) / T - xmax);
-    sh.tw[j] = w;
-    s += w;
-  }
-  double ex, tot;
-  mg_warp_scan(s, ex, tot);
-  int nkeep = m;
-  if (P < 1.0) {  // sampler.py:49-58: cumsum >= top_p, crossing entry kept
-    const double need = P * tot;
-    int cand = 0x7FFFFFFF;
-    double acc = ex;
-    for (int j = j0; j < j1; ++j) {
-      acc += sh.tw[j];
-      if (acc >= need) {
-        cand = j;
-        break;
-      }
-    }
-    const int first = warp_min_i(cand);
-    if (first != 0x7FFFFFFF) nkeep = first + 1;
-  }
-  __syncwarp();
-  // kept entries in index order (position = kept entries with a smaller id)
-  for (int j = lane; j < nkeep; j += 32) {
-    const int my = sh.tidx[j];
-    int pos = 0;
-    for (int q = 0; q < nkeep; ++q) pos += sh.tidx[q] < my ? 1 : 0;
-    sh.kid[pos] = my;
-    sh.u.kw[pos] = sh.tw[j];
-  }
-  __syncwarp();
-  const int c2 = (nkeep + 31) >> 5;
-  const int q0 = min(nkeep, lane * c2), q1 = min(nkeep, q0 + c2);
-  double s2 = 0.0;
-  for (int j = q0; j < q1; ++j) s2 += sh.u.kw[j];
-  double cx, ktot;
-  mg_warp_scan(s2, cx, ktot);
-  if (!(U > 0.0)) {  // r == 0 stops at index 0
-    if (lane == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / ktot), 0);
-    return;
-  }
-  const double target = U * ktot;  // sampler.py:60-68
-  int who = 0x7FFFFFFF;
-  double acc = cx;
-  for (int j = q0; j < q1; ++j) {
-    acc += sh.u.kw[j];
-    if (sh.u.kw[j] > 0.0 && acc >= target) {
-      who = j;
-      break;
-    }
-  }
-  const int w = warp_min_i(who);
-  if (lane == 0) {
-    if (w == 0x7FFFFFFF) {  // ran past the end
-      const int last = nkeep - 1;
-      mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.u.kw[last] : 0.0) / ktot), 0);
-    } else {
-      mg_write(a, row, sh.kid[w], (float)(sh.u.kw[w] / ktot), 0);
-    }
-  }
-}
-
-// One row's merge: all NT threads of the CTA enter; a top-k row ends in its
-// first warp (the other warps return first).  Rank r's candidate i sits in
-// slot r * kmax + i; every record word of the row is loaded in one wave.
+// One row's merge: all NT threads of the CTA.
 template <int NT>
 __device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row) {
   const int tid = threadIdx.x;
   const size_t rw = (size_t)(4 + 2 * a.kmax);
-  const int N = a.nranks, KM = a.kmax;
-  const int ns = N * KM;  // <= kMgCap
   const double T = a.temperature[row];
   const int k = a.top_k[row];
   const double P = a.top_p[row];
   const double U = a.uniforms[row];
-  if (tid == 0) {
-    sh.st = 0u;
-    sh.n = 0;
+  // per-rank counts -> offsets; statuses OR-ed
+  int m_r = 0;
+  uint32_t st_r = 0u;
+  if (tid < a.nranks) {
+    const uint32_t *rec = mg_rec(a, tid, row, rw);
+    m_r = (int)min(mg_ld(rec), (uint32_t)a.kmax);
+    st_r = mg_ld(rec + 1);
   }
-  uint32_t stv = 0u;
-  if (tid < N) stv = mg_ld(mg_rec(a, tid, row, rw) + 1);
-  constexpr int kPer = (kMgCap + NT - 1) / NT;
-  uint32_t mv[kPer], kv[kPer], iv[kPer];
-#pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int sl = tid + q * NT;
-    if (sl < ns) {
-      const int r = sl / KM, i = sl - r * KM;
-      const uint32_t *rec = mg_rec(a, r, row, rw);
-      mv[q] = mg_ld(rec);
-      kv[q] = mg_ld(rec + 2 + i);
-      iv[q] = mg_ld(rec + 2 + KM + i);
-    }
-  }
-  __syncthreads();  // sh.st / sh.n cleared
-  if (stv) atomicOr(&sh.st, stv);
-#pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int sl = tid + q * NT;
-    if (sl < ns) {
-      const int r = sl / KM, i = sl - r * KM;
-      const int m = (int)min(mv[q], (uint32_t)KM);
-      sh.u.comp[sl] = i < m ? ((unsigned long long)kv[q] << 32) | (unsigned long long)(~iv[q]) : 0ull;
-      if (i == 0) {
-        sh.off[r] = m;
-        atomicAdd(&sh.n, m);
-      }
-    }
-  }
-  if (tid == 0) {
-    sh.u.comp[ns] = 0ull;
-    sh.u.comp[ns + 1] = 0ull;
-  }
+  if (tid == 0) sh.st = 0u;
   __syncthreads();
+  if (st_r) atomicOr(&sh.st, st_r);
+  int ex, inc, n;
+  block_scan<NT, int>(m_r, ex, inc, n, sh.redi);  // ends with a barrier
+  if (tid < a.nranks) sh.off[tid] = ex;
   const uint32_t st = sh.st;
-  const int n = sh.n;
   if (st != 0u) {  // bad temperature, or a slice that needs the full row
     if (tid == 0) mg_write(a, row, -1, 0.0f, (int32_t)st);
     return;
   }
+  __syncthreads();
+  for (int r = 0; r < a.nranks; ++r) {
+    const uint32_t *rec = mg_rec(a, r, row, rw);
+    const int mr = (int)min(mg_ld(rec), (uint32_t)a.kmax);
+    for (int i = tid; i < mr; i += NT)
+      sh.u.comp[sh.off[r] + i] =
+          ((unsigned long long)mg_ld(rec + 2 + i) << 32) | (unsigned long long)(~mg_ld(rec + 2 + a.kmax + i));
+  }
+  if (tid == 0) {
+    sh.u.comp[n] = 0ull;
+    sh.u.comp[n + 1] = 0ull;
+  }
+  __syncthreads();
   if (n == 0) {  // every logit -inf
     if (tid == 0) {
       if (T == 0.0) mg_write(a, row, 0, 1.0f, 0);            // greedy ties at index 0 (sampler.py:33-34)
@@ -363,7 +240,7 @@ __device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row
   }
   if (T == 0.0 || k == 1) {  // the first maximum (sampler.py:33-34, or top-k 1)
     unsigned long long best = 0ull;
-    for (int sl = tid; sl < ns; sl += NT) best = max(best, sh.u.comp[sl]);
+    for (int i = tid; i < n; i += NT) best = max(best, sh.u.comp[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
     if ((tid & 31) == 0) sh.redq[tid >> 5] = best;
@@ -377,29 +254,60 @@ __device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row
     return;
   }
   if (!(k >= 2 && (int64_t)k < a.V)) {  // no top-k: the nucleus from the candidates
-    mg_nucleus<NT>(a, sh, row, n, ns, rw, T, P, U);
+    mg_nucleus<NT>(a, sh, row, n, rw, T, P, U);
     return;
   }
-  // top-k: a candidate's rank is the number of larger composites; the first
-  // min(n, k) ranks are the row's top-k set
+  // top-k: rank every candidate; the best min(n, k) are the row's top-k set
   const int m = min(n, k);
   const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
-  const int npair = (ns + 1) >> 1;
-  for (int sl = tid; sl < ns; sl += NT) {
-    const unsigned long long c = sh.u.comp[sl];
-    if (c == 0ull) continue;
+  const int npair = (n + 1) >> 1;
+  for (int i = tid; i < n; i += NT) {
+    const unsigned long long ci = sh.u.comp[i];
     int rank = 0;
     for (int j = 0; j < npair; ++j) {
       const ulonglong2 q = c2[j];
-      rank += (q.x > c ? 1 : 0) + (q.y > c ? 1 : 0);
+      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
     }
     if (rank < m) {
-      sh.tkey[rank] = (uint32_t)(c >> 32);
-      sh.tidx[rank] = (int)~(uint32_t)c;
+      sh.key[rank] = (uint32_t)(ci >> 32);
+      sh.id[rank] = (int)~(uint32_t)ci;
     }
   }
   __syncthreads();
-  if (tid < 32) mg_topk_warp(a, sh, row, m, T, P, U);
+  // float64 weights over the top-k set (sampler.py:35,45): thread r, rank r
+  const double xmax = (double)key_to_float(sh.key[0]) / T;
+  const double w = tid < m ? exp((double)key_to_float(sh.key[tid]) / T - xmax) : 0.0;
+  double wex, winc, total;
+  block_scan<NT, double>(w, wex, winc, total, sh.redd);
+  int nkeep = m;
+  if (P < 1.0) {  // smallest rank prefix reaching top_p, crossing entry kept (sampler.py:49-58)
+    const int first = block_min_i<NT>((tid < m && winc >= P * total) ? tid : 0x7FFFFFFF, sh.redi);
+    if (first != 0x7FFFFFFF) nkeep = first + 1;
+  }
+  // kept entries in index order
+  if (tid < nkeep) {
+    const int my = sh.id[tid];
+    int pos = 0;
+    for (int j = 0; j < nkeep; ++j) pos += sh.id[j] < my ? 1 : 0;
+    sh.kid[pos] = my;
+    sh.u.kw[pos] = w;
+  }
+  const double tot = block_sum<NT>(tid < nkeep ? w : 0.0, sh.redd);  // ends with a barrier
+  // index-order inverse CDF (sampler.py:60-68)
+  if (!(U > 0.0)) {  // r == 0 stops at index 0
+    if (tid == 0) mg_write(a, row, 0, (float)((sh.kid[0] == 0 ? sh.u.kw[0] : 0.0) / tot), 0);
+    return;
+  }
+  const double target = U * tot;
+  const double kwv = tid < nkeep ? sh.u.kw[tid] : 0.0;
+  double cex, cinc, ctot;
+  block_scan<NT, double>(kwv, cex, cinc, ctot, sh.redd);
+  const int who = block_min_i<NT>((tid < nkeep && kwv > 0.0 && cinc >= target) ? tid : 0x7FFFFFFF, sh.redi);
+  if (tid == 0 && who == 0x7FFFFFFF) {  // ran past the end
+    const int last = nkeep - 1;
+    mg_write(a, row, a.V - 1, (float)((sh.kid[last] == a.V - 1 ? sh.u.kw[last] : 0.0) / tot), 0);
+  }
+  if (tid == who) mg_write(a, row, sh.kid[tid], (float)(kwv / tot), 0);
 }
 
 __global__ void __launch_bounds__(kMgThreads) ms_merge_kernel(MergeArgs a) {

@@ -2607,25 +2607,13 @@ __device__ __forceinline__ void st_row_body(const SampleArgs &a, StShared &sh, i
   });
 }
 
-// The merge of a published row, on the CTA's candidate area (noinline: its
-// registers stay out of the streaming loops).
-__device__ __noinline__ void st_merge_published(MergeArgs m, int row) {
-  extern __shared__ __align__(128) unsigned char st_raw_m[];
-  StShared &sh = *reinterpret_cast<StShared *>(st_raw_m);
-  static_assert(sizeof(MgShared) <= sizeof(sh.w), "merge scratch fits the candidate area");
-  mg_row<kStThreads>(m, *reinterpret_cast<MgShared *>(&sh.w), row);
-}
-
 // Fused peer exchange of vocab-sharded sampling (ms_shard_exchange): after
 // the CTA wrote its record of `row` into this rank's slot of its own buffer,
-// the record is copied into the same slot of every other rank's buffer and
-// counted in the row's arrival counter on the row's home rank (row mod
-// nranks).  The CTA whose arrival completes the count (every rank's record
-// of the row is then in every buffer) merges the row from its own buffer
-// (mg_row) and writes the result entry into every rank's buffer, then counts
-// the row in every rank's done counter (ms_xfinish_kernel waits for it).
-// No wait: every step either stores or reads what has arrived.
-__device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, StShared &sh, int row) {
+// the record is copied into the same slot of every other rank's buffer over
+// NVLink; then one release fence (cumulative over the CTA's stores before
+// the barrier) and the row's arrival flag (the call's epoch) in every
+// buffer.  No wait: the merge kernel on each rank waits for the flags.
+__device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, int row) {
   const int tid = threadIdx.x;
   const int N = x.n, me = x.rank;
   const int W = 4 + 2 * a.kmax;  // even
@@ -2640,23 +2628,9 @@ __device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, 
     __syncthreads();
   }
   if (tid == 0) {
-    // release (cumulative over the CTA's stores before the barrier) and acquire
-    unsigned long long *cnt = reinterpret_cast<unsigned long long *>(x.peers[row % N] + x.cnt) + row;
-    const unsigned long long old = x_atom_add_acq_rel_sys(cnt, 1ull);
-    sh.bcast_i[0] = (old + 1ull) % (unsigned long long)N == 0ull ? 1 : 0;
-  }
-  __syncthreads();
-  if (!sh.bcast_i[0]) return;
-  // every rank's record of the row is in this buffer
-  MergeArgs m{x.peers[me] + x.rec, N, a.rows, a.kmax, a.Vg, a.temperature, a.top_k, a.top_p, a.uniforms,
-              nullptr, nullptr, nullptr};
-  m.xpeers = x.peers;
-  m.xout = x.out;
-  m.xepoch = x.epoch;
-  st_merge_published(m, row);
-  __syncthreads();  // the result entries are stored
-  if (tid == 0) {  // each a release, cumulative over the entries stored before the barrier
-    for (int q = 0; q < N; ++q) x_red_add_release_sys(reinterpret_cast<unsigned long long *>(x.peers[q]), 1ull);
+    x_fence_acq_rel_sys();
+    const int64_t f = x.flags + (int64_t)row * N + me;
+    for (int q = 0; q < N; ++q) x_st_relaxed_sys(x.peers[q] + f, x.epoch);
   }
 }
 
@@ -2676,6 +2650,6 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_xkernel(SampleArgs a,
   StShared &sh = *reinterpret_cast<StShared *>(st_raw);
   int prow = -1;
   st_row_body<DT, true>(a, sh, prow);
-  if (prow >= 0) st_publish(a, x, sh, prow);
+  if (prow >= 0) st_publish(a, x, prow);
 }
 }  // namespace ms

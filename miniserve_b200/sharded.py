@@ -10,12 +10,11 @@ every rank, which finishes each row exactly as miniserve's
 ``Sampler.sample`` (miniserve/sampler.py:23-68) does on the whole vocabulary:
 the row's top-k set is contained in the union of the slices' top-k sets.
 
-With a peer exchange (``PeerExchange``, ``exchange="peer"``) steps 1-3 are
-fused: ``ms_shard_exchange`` stores each row's record into every rank's
-exchange buffer over NVLink as the row finishes, and the CTA whose record
-completes the row merges it in the same kernel and stores the result into
-every rank's buffer; ``ms_exchange_finish`` waits (bounded) for all rows'
-results.  No collective call is made on that path.
+With a peer exchange (``PeerExchange``, ``exchange="peer"``) step 2 is
+fused into step 1: ``ms_shard_exchange`` stores each row's record into every
+rank's exchange buffer over NVLink as the row finishes, with an arrival flag
+per row and rank, and ``ms_exchange_merge`` waits (bounded) for each row's
+flags before merging it.  No collective call is made on that path.
 
 A top-p row without top-k is settled from the records too when its nucleus
 lies among the candidates (the records carry each slice's softmax total);
@@ -126,7 +125,6 @@ class PeerExchange:
         self.local = None
         self._opened = []
         self.epoch = 0
-        self.done = 0
         self.broken = False
         err = None
         handle = b""
@@ -302,8 +300,9 @@ class ShardedSampler:
         of a count decides whether any row needs the full-row path.
         ``events``: optional four CUDA events recorded around the shard pass,
         the all-gather and the merge (for timing the phases); with the peer
-        exchange: before and after the fused kernel and after the finish
-        (the last two events together)."""
+        exchange: before and after the streaming kernel (which also stores the
+        records into every rank's buffer) and after the merge (the last two
+        events together)."""
         torch = _torch()
         if logits_slice.dim() != 2 or not logits_slice.is_cuda:
             raise ValueError("logits_slice must be a [B, Vloc] CUDA tensor")
@@ -346,7 +345,6 @@ class ShardedSampler:
                 cur = torch.cuda.current_stream(dev)
                 stream = cur.cuda_stream
                 x.epoch += 1
-                x.done += B
                 epoch = (x.epoch - 1) % (2 ** 32 - 2) + 1  # parity alternates across the wrap
                 if events is not None:
                     events[0].record(cur)
@@ -357,9 +355,10 @@ class ShardedSampler:
                 _lib.check(rc, "ms_shard_exchange")
                 if events is not None:
                     events[1].record(cur)
-                rc = L.ms_exchange_finish(x.local, B, x.Bcap, x.done % 2 ** 64, epoch, x.timeout_ns,
-                                          tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
-                _lib.check(rc, "ms_exchange_finish")
+                rc = L.ms_exchange_merge(x.local, x.world, B, x.Bcap, kmax, x.kmax_cap, self.V, T.data_ptr(),
+                                         K.data_ptr(), P.data_ptr(), U.data_ptr(), epoch, x.timeout_ns,
+                                         tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
+                _lib.check(rc, "ms_exchange_merge")
                 if events is not None:
                     events[2].record(cur)
                     events[3].record(cur)
@@ -406,7 +405,7 @@ class ShardedSampler:
         n_flagged, n_nuc, n_late = (int(v) for v in torch.stack([flagged.sum(), nuc.sum(), late.sum()]).tolist())
         if n_late:
             x.broken = True
-            raise PeerExchangeError(f"{n_late} rows had no result from the other ranks within "
+            raise PeerExchangeError(f"{n_late} rows missed another rank's record within "
                                     f"{self.peer_timeout_s} s")
         self.last_nucleus_rows = 0
         if (n_nuc and kmax >= 2 and Vloc <= NUCLEUS_MAX_SLICE and self.V <= NUCLEUS_MAX_V

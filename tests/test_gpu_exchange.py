@@ -1,8 +1,8 @@
 """The fused peer exchange of vocab-sharded sampling (ms_shard_exchange +
-ms_exchange_finish) on one GPU.  The ranks are emulated: every rank's
-exchange buffer is a block on this GPU and the ranks' kernels run one after
-another on one stream (no kernel of this path waits, so launch order does not
-matter: the last rank's CTAs find every row's count complete and merge).
+ms_exchange_merge) on one GPU.  The ranks are emulated: every rank's
+exchange buffer is a block on this GPU and the ranks' streaming kernels run
+one after another on one stream before any merge (the streaming kernels do
+not wait; each merge finds every flag already set).
 Tokens must equal the all-gather path (ms_shard_candidates + ms_shard_merge)
 bit for bit and the oracle on the full rows.  With two GPUs the same path
 runs under torchrun (tests/mp_sharded.py).  Needs a B200."""
@@ -40,7 +40,6 @@ class Buffers:
             self.ptrs.append(p.value)
         self.peers = torch.tensor(self.ptrs, dtype=torch.int64, device="cuda")
         self.epoch = 0
-        self.done = 0
 
     def close(self):
         for p in self.ptrs:
@@ -65,7 +64,6 @@ def run_exchange(torch, bufs, xt, T, K, P, U, kmax, bf16=False, mask=None, ranks
     Ut = torch.tensor(U, dtype=torch.float64, device=dev)
     s = torch.cuda.current_stream().cuda_stream
     bufs.epoch += 1
-    bufs.done += B
     world = bufs.world
     for r in (range(world) if ranks is None else ranks):
         v0, v1 = sharded.shard_bounds(V, world, r)
@@ -82,8 +80,9 @@ def run_exchange(torch, bufs, xt, T, K, P, U, kmax, bf16=False, mask=None, ranks
         tok = torch.empty(B, dtype=torch.int64, device=dev)
         prob = torch.empty(B, dtype=torch.float32, device=dev)
         st = torch.empty(B, dtype=torch.int32, device=dev)
-        rc = L.ms_exchange_finish(bufs.ptrs[r], B, bufs.Bcap, bufs.done, bufs.epoch, timeout_ns, tok.data_ptr(),
-                                  prob.data_ptr(), st.data_ptr(), s)
+        rc = L.ms_exchange_merge(bufs.ptrs[r], world, B, bufs.Bcap, kmax, bufs.kmax_cap, V, Tt.data_ptr(),
+                                 Kt.data_ptr(), Pt.data_ptr(), Ut.data_ptr(), bufs.epoch, timeout_ns, tok.data_ptr(),
+                                 prob.data_ptr(), st.data_ptr(), s)
         assert rc == 0, rc
         torch.cuda.synchronize()
         out.append((tok.cpu().numpy(), prob.cpu().numpy(), st.cpu().numpy()))
@@ -136,10 +135,10 @@ def _mixed(seed=9, B=48, V=65536):
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
 def test_exchange_equals_gather_path(torch, world):
-    """Three calls in a row on the same buffers (both record areas, growing
-    counters): every rank's tokens equal the all-gather path's bit for bit,
-    the records sit in every buffer in the all-gather layout, and the exact
-    rows equal the oracle."""
+    """Three calls in a row on the same buffers (both record areas, the flags
+    of earlier calls in place): every rank's tokens equal the all-gather
+    path's bit for bit, the records sit in every buffer in the all-gather
+    layout, and the exact rows equal the oracle."""
     from miniserve_b200 import sharded
     x, T, K, P, U = _mixed(seed=world)
     kmax = sharded.choose_kmax(list(K), list(T), list(P), x.shape[1])
@@ -178,7 +177,7 @@ def test_exchange_equals_gather_path(torch, world):
 
 def test_exchange_bf16_mask_and_batch_sizes(torch):
     """bf16 slices with a mask, and calls of different batch sizes on one
-    buffer (the done counter grows by each call's rows)."""
+    buffer (rows past a call's batch keep older flags)."""
     from miniserve_b200 import sharded
     x, T, K, P, U = _mixed(seed=10)
     xb = ((x.view(np.uint32) >> 16).astype(np.uint32) << 16).view(np.float32)
@@ -199,9 +198,9 @@ def test_exchange_bf16_mask_and_batch_sizes(torch):
         bufs.close()
 
 
-def test_exchange_finish_times_out_without_peer(torch):
-    """A rank that never runs its kernel: the others' rows never complete, so
-    the finish waits its limit (2 ms here) and returns MS_ROW_PEER_TIMEOUT
+def test_exchange_merge_times_out_without_peer(torch):
+    """A rank that never runs its streaming kernel: its flags never arrive, so
+    each merge waits its limit (2 ms here) and returns MS_ROW_PEER_TIMEOUT
     rows with token -1; the device stays usable."""
     x, T, K, P, U = _mixed(seed=12, B=16)
     K[:] = 20
