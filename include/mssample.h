@@ -158,12 +158,13 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
  * slice and rank:
  *
  *   1. ms_shard_exchange: the slice's records (as ms_shard_candidates) are
- *      stored into every rank's buffer over NVLink as each row finishes,
- *      each followed by the row's arrival flag.
+ *      stored into every other rank's buffer over NVLink as each row
+ *      finishes, every word tagged with the call's epoch in one 8-byte
+ *      store (no fence, no wait).
  *   2. ms_exchange_merge: row by row, waits (at most timeout_ns; a stalled
- *      batch up to about twice that) for every rank's flag of the row, then
- *      merges it as ms_shard_merge does; rows whose flags did not all
- *      arrive: token -1, MS_ROW_PEER_TIMEOUT.
+ *      batch up to about twice that) until every other rank's words of the
+ *      row carry the epoch, then merges it as ms_shard_merge does; rows with
+ *      a word missing: token -1, MS_ROW_PEER_TIMEOUT.
  *
  * epoch: the call's number, 1, 2, ... in order on every rank (with a fresh
  * buffer; it may wrap to 1 after an even number).  Bcap / kmax_cap: the
@@ -183,7 +184,7 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
                       const uint32_t *mask, int64_t mask_ld, int32_t kmax, uint32_t *xbuf, uint32_t *const *peers,
                       int32_t rank, int32_t nranks, int64_t Bcap, int32_t kmax_cap, uint32_t epoch,
                       ms_stream_t stream);
-int ms_exchange_merge(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+int ms_exchange_merge(uint32_t *xbuf, int32_t rank, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
                       int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
                       const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);

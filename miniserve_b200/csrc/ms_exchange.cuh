@@ -4,18 +4,21 @@
 // into the other ranks by CUDA IPC), in place of an all-gather between the
 // streaming kernel and the merge.
 //
+// Every 8-byte store carries one record word and the call's epoch (high
+// half): an aligned 8-byte store is seen whole or not at all, so a reader
+// that finds the epoch finds the word, and the writer needs no fence and
+// never waits.  The merge on each rank waits (bounded) for the epochs of
+// the row's words from every other rank.
+//
 // Exchange buffer layout (32-bit words; Bcap rows, nranks ranks, records of
 // at most Wcap = 4 + 2 kmax_cap words; the same in every rank's buffer):
-//   [flags, +Bcap*nranks)  arrival flags [row][rank]: the epoch of the last
-//                          call whose record of that row from that rank is
-//                          in this buffer
-//   [rec0, +2 half)        two record areas, [nranks][B][W] each (the layout
-//                          of an all-gather of ms_shard_candidates' records);
-//                          call `epoch` uses area (epoch & 1)
-// A rank stores its record of a row into every buffer, then (one release
-// fence later) its flag of that row in every buffer.  The merge on each rank
-// waits, row by row and for a bounded time, until the row's flags from
-// every rank carry the call's epoch.
+//   [rec0, +2 half)   two plain record areas, [nranks][B][W] each (the
+//                     layout of an all-gather of ms_shard_candidates'
+//                     records): this rank's own records from the streaming
+//                     kernel, the other ranks' unpacked by the merge
+//   [ll0, +2 llhalf)  two areas of tagged words (8 bytes each), [B][nranks][W]
+//                     the other ranks store into
+// Call `epoch` uses the areas (epoch & 1).
 #pragma once
 
 #include <cstdint>
@@ -26,41 +29,40 @@
 namespace ms {
 
 // One call of the fused exchange on one rank: peers[q] is rank q's exchange
-// buffer (peers[rank] this rank's own); flags and rec are word offsets, the
-// same in every buffer (rec: the call's record area).
+// buffer (peers[rank] this rank's own); ll: word offset of the call's tagged
+// area, the same in every buffer.
 struct XArgs {
   uint32_t *const *peers;
   int rank;
   int n;
   uint32_t epoch;
-  int64_t flags;
-  int64_t rec;
+  int64_t ll;
 };
 
 struct XLayout {
-  int64_t flags, rec0, half, total;
+  int64_t rec0, half, ll0, llhalf, total;
 };
 
 __host__ __device__ inline int64_t x_round32(int64_t w) { return (w + 31) / 32 * 32; }
 
 __host__ __device__ inline XLayout x_layout(int64_t Bcap, int nranks, int kmax_cap) {
   XLayout L;
-  L.flags = 0;
-  L.rec0 = x_round32(Bcap * nranks);
-  L.half = x_round32((int64_t)nranks * Bcap * (4 + 2 * (int64_t)kmax_cap));
-  L.total = L.rec0 + 2 * L.half;
+  const int64_t words = (int64_t)nranks * Bcap * (4 + 2 * (int64_t)kmax_cap);
+  L.rec0 = 0;
+  L.half = x_round32(words);
+  L.ll0 = 2 * L.half;
+  L.llhalf = x_round32(2 * words);
+  L.total = L.ll0 + 2 * L.llhalf;
   return L;
 }
 
-__device__ __forceinline__ void x_fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-__device__ __forceinline__ void x_st_relaxed_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void x_st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t x_ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long x_ld_relaxed_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -70,27 +72,34 @@ __device__ __forceinline__ uint64_t x_now_ns() {
   return t;
 }
 
-// The merge on every rank, one CTA per row: thread q waits (at most
-// timeout_ns) for rank q's flag of the row, then the row is merged from this
-// buffer's records as ms_merge_kernel does.  A row whose flags are not all
-// there at the timeout: token -1, MS_ROW_PEER_TIMEOUT.  Only other GPUs'
-// kernels can still be writing while it waits: this rank's own streaming
-// kernel ran to completion before it on the stream.
-__global__ void __launch_bounds__(kMgThreads) ms_xmerge_kernel(MergeArgs a, const uint32_t *flags, uint32_t epoch,
+// The merge on every rank, one CTA per row: the other ranks' tagged words
+// of the row are waited for (each at most timeout_ns after the CTA starts),
+// unpacked into the plain record area (`plain`, the call's [nranks][B][W]),
+// and the row is merged as ms_merge_kernel does.  A row with a word missing
+// at the timeout: token -1, MS_ROW_PEER_TIMEOUT.  Only other GPUs' kernels
+// can still be storing while it waits: this rank's own streaming kernel ran
+// to completion before it on the stream.
+__global__ void __launch_bounds__(kMgThreads) ms_xmerge_kernel(MergeArgs a, uint32_t *plain,
+                                                              const unsigned long long *ll, int me, uint32_t epoch,
                                                               int64_t timeout_ns) {
   __shared__ MgShared sh;
-  const int row = blockIdx.x;
+  const int row = blockIdx.x, N = a.nranks, W = 4 + 2 * a.kmax;
+  const unsigned long long *src = ll + (size_t)row * N * W;
   int ok = 1;
-  if ((int)threadIdx.x < a.nranks) {
-    const uint32_t *f = flags + (size_t)row * a.nranks + threadIdx.x;
-    const uint64_t t0 = x_now_ns();
-    while (x_ld_acquire_sys(f) != epoch) {
+  const uint64_t t0 = x_now_ns();
+  for (int j = threadIdx.x; j < N * W && ok; j += kMgThreads) {
+    const int r = j / W;
+    if (r == me) continue;
+    unsigned long long v = x_ld_relaxed_sys(src + j);
+    while ((uint32_t)(v >> 32) != epoch) {
       if ((int64_t)(x_now_ns() - t0) > timeout_ns) {
         ok = 0;
         break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
+      v = x_ld_relaxed_sys(src + j);
     }
+    plain[((size_t)r * a.B + row) * W + (j - r * W)] = (uint32_t)v;
   }
   if (!__syncthreads_and(ok)) {
     if (threadIdx.x == 0) mg_write(a, row, -1, 0.0f, MS_ROW_PEER_TIMEOUT);

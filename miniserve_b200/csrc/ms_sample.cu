@@ -281,7 +281,7 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
   a.v0 = v0;
   a.Vg = V;
   a.rows = (int)B;
-  const ms::XArgs x{peers, rank, nranks, epoch, L.flags, rec};
+  const ms::XArgs x{peers, rank, nranks, epoch, L.ll0 + (int64_t)(epoch & 1u) * L.llhalf};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -291,23 +291,27 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
   return MS_OK;
 }
 
-int ms_exchange_merge(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+int ms_exchange_merge(uint32_t *xbuf, int32_t rank, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
                       int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
                       const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
   if (ms_exchange_words(Bcap, nranks, kmax_cap) < 0 || B < 0 || B > Bcap || kmax < 1 || kmax > kmax_cap ||
-      V < 1 || V > 0x7FFFFFFFll - 4096 || timeout_ns < 0 || epoch == 0u)
+      V < 1 || V > 0x7FFFFFFFll - 4096 || timeout_ns < 0 || epoch == 0u || rank < 0 || rank >= nranks)
     return MS_E_INVALID;
   if ((int64_t)nranks * kmax > ms::kMgCap) return MS_E_UNSUPPORTED;
   if (B == 0) return MS_OK;
   if (!xbuf || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
     return MS_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
   const int64_t rec = L.rec0 + (int64_t)(epoch & 1u) * L.half;
   ms::MergeArgs a{xbuf + rec, nranks, (int)B, kmax, V, temperature, top_k, top_p, uniforms,
                   tokens, probs, row_status};
-  ms::ms_xmerge_kernel<<<dim3((unsigned)B), dim3(ms::kMgThreads), 0, s>>>(a, xbuf + L.flags, epoch, timeout_ns);
+  const unsigned long long *ll =
+      reinterpret_cast<const unsigned long long *>(xbuf + L.ll0 + (int64_t)(epoch & 1u) * L.llhalf);
+  ms::ms_xmerge_kernel<<<dim3((unsigned)B), dim3(ms::kMgThreads), 0, s>>>(a, xbuf + rec, ll, rank, epoch,
+                                                                         timeout_ns);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;

@@ -2608,29 +2608,22 @@ __device__ __forceinline__ void st_row_body(const SampleArgs &a, StShared &sh, i
 }
 
 // Fused peer exchange of vocab-sharded sampling (ms_shard_exchange): after
-// the CTA wrote its record of `row` into this rank's slot of its own buffer,
-// the record is copied into the same slot of every other rank's buffer over
-// NVLink; then one release fence (cumulative over the CTA's stores before
-// the barrier) and the row's arrival flag (the call's epoch) in every
-// buffer.  No wait: the merge kernel on each rank waits for the flags.
+// the CTA wrote its record of `row` into its own buffer's plain area, every
+// word goes to every other rank's tagged area over NVLink, as one 8-byte
+// store of (epoch, word).  No fence and no wait: the merge kernel on each
+// rank checks the epochs.
 __device__ __forceinline__ void st_publish(const SampleArgs &a, const XArgs &x, int row) {
   const int tid = threadIdx.x;
   const int N = x.n, me = x.rank;
-  const int W = 4 + 2 * a.kmax;  // even
-  const int64_t roff = x.rec + ((int64_t)me * a.rows + row) * W;
+  const int W = 4 + 2 * a.kmax;
   __syncthreads();  // the record is written
-  if (N > 1) {
-    const uint2 *src = reinterpret_cast<const uint2 *>(x.peers[me] + roff);
-    for (int q = 1; q < N; ++q) {
-      uint2 *dst = reinterpret_cast<uint2 *>(x.peers[(me + q) % N] + roff);
-      for (int i = tid; i < W / 2; i += kStThreads) dst[i] = src[i];
-    }
-    __syncthreads();
-  }
-  if (tid == 0) {
-    x_fence_acq_rel_sys();
-    const int64_t f = x.flags + (int64_t)row * N + me;
-    for (int q = 0; q < N; ++q) x_st_relaxed_sys(x.peers[q] + f, x.epoch);
+  const uint32_t *src = st_record(a, row);
+  const int64_t slot = ((int64_t)row * N + me) * W;
+  const unsigned long long tag = (unsigned long long)x.epoch << 32;
+  for (int i = tid; i < W; i += kStThreads) {
+    const unsigned long long v = tag | src[i];
+    for (int q = 1; q < N; ++q)
+      x_st_relaxed_sys(reinterpret_cast<unsigned long long *>(x.peers[(me + q) % N] + x.ll) + slot + i, v);
   }
 }
 
@@ -2650,6 +2643,6 @@ __global__ void __launch_bounds__(kStThreads, 2) ms_stream_xkernel(SampleArgs a,
   StShared &sh = *reinterpret_cast<StShared *>(st_raw);
   int prow = -1;
   st_row_body<DT, true>(a, sh, prow);
-  if (prow >= 0) st_publish(a, x, prow);
+  if (prow >= 0 && x.n > 1) st_publish(a, x, prow);
 }
 }  // namespace ms

@@ -12,9 +12,10 @@ the row's top-k set is contained in the union of the slices' top-k sets.
 
 With a peer exchange (``PeerExchange``, ``exchange="peer"``) step 2 is
 fused into step 1: ``ms_shard_exchange`` stores each row's record into every
-rank's exchange buffer over NVLink as the row finishes, with an arrival flag
-per row and rank, and ``ms_exchange_merge`` waits (bounded) for each row's
-flags before merging it.  No collective call is made on that path.
+other rank's exchange buffer over NVLink as the row finishes (every word
+tagged with the call's epoch in one 8-byte store), and ``ms_exchange_merge``
+waits (bounded) until a row's words from every rank carry the epoch before
+merging it.  No collective call is made on that path.
 
 A top-p row without top-k is settled from the records too when its nucleus
 lies among the candidates (the records carry each slice's softmax total);
@@ -355,7 +356,7 @@ class ShardedSampler:
                 _lib.check(rc, "ms_shard_exchange")
                 if events is not None:
                     events[1].record(cur)
-                rc = L.ms_exchange_merge(x.local, x.world, B, x.Bcap, kmax, x.kmax_cap, self.V, T.data_ptr(),
+                rc = L.ms_exchange_merge(x.local, x.rank, x.world, B, x.Bcap, kmax, x.kmax_cap, self.V, T.data_ptr(),
                                          K.data_ptr(), P.data_ptr(), U.data_ptr(), epoch, x.timeout_ns,
                                          tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
                 _lib.check(rc, "ms_exchange_merge")

@@ -80,7 +80,7 @@ def run_exchange(torch, bufs, xt, T, K, P, U, kmax, bf16=False, mask=None, ranks
         tok = torch.empty(B, dtype=torch.int64, device=dev)
         prob = torch.empty(B, dtype=torch.float32, device=dev)
         st = torch.empty(B, dtype=torch.int32, device=dev)
-        rc = L.ms_exchange_merge(bufs.ptrs[r], world, B, bufs.Bcap, kmax, bufs.kmax_cap, V, Tt.data_ptr(),
+        rc = L.ms_exchange_merge(bufs.ptrs[r], r, world, B, bufs.Bcap, kmax, bufs.kmax_cap, V, Tt.data_ptr(),
                                  Kt.data_ptr(), Pt.data_ptr(), Ut.data_ptr(), bufs.epoch, timeout_ns, tok.data_ptr(),
                                  prob.data_ptr(), st.data_ptr(), s)
         assert rc == 0, rc
@@ -199,17 +199,17 @@ def test_exchange_bf16_mask_and_batch_sizes(torch):
 
 
 def test_exchange_merge_times_out_without_peer(torch):
-    """A rank that never runs its streaming kernel: its flags never arrive, so
-    each merge waits its limit (2 ms here) and returns MS_ROW_PEER_TIMEOUT
-    rows with token -1; the device stays usable."""
+    """A rank that never runs its streaming kernel: its records never arrive,
+    so rank 0's merge waits its limit (2 ms here) and returns
+    MS_ROW_PEER_TIMEOUT rows with token -1; the device stays usable."""
     x, T, K, P, U = _mixed(seed=12, B=16)
     K[:] = 20
     xt = torch.from_numpy(x).cuda()
     bufs = Buffers(torch, 2, 16, 64)
     try:
         outs = run_exchange(torch, bufs, xt, T, K, P, U, 20, ranks=[0], timeout_ns=2_000_000)
-        for tok, prob, st in outs:
-            assert np.all(st == 16) and np.all(tok == -1)
+        tok, prob, st = outs[0]
+        assert np.all(st == 16) and np.all(tok == -1)
         assert float(torch.ones(4, device="cuda").sum()) == 4.0
     finally:
         bufs.close()
