@@ -315,11 +315,11 @@ def run_ours(args, rank, world, local_rank):
 def sharded_line(args, rank, world, dev, peak):
     """Config 5 (1024 x 256000 fp32, top_k 50, top_p 0.95, T 0.9) with the
     vocabulary split into contiguous slices over the ranks, sampled through
-    ShardedSampler.sample: the default path (shard pass, NCCL all-gather of
-    the candidate records, merge kernel), and beside it the fused peer
-    exchange (the streaming kernel stores each row's record and an arrival
-    flag into every rank's buffer over NVLink; the merge kernel waits for
-    each row's flags).  Strong scaling: the same rows
+    ShardedSampler.sample: the default path, the fused peer exchange (the
+    streaming kernel stores each row's record, every word tagged with the
+    call's epoch, into every other rank's buffer over NVLink; the merge
+    kernel waits for each row's tags), and beside it the all-gather path
+    (shard pass, NCCL all-gather of the candidate records, merge kernel).  Strong scaling: the same rows
     on every N.  Each phase timed with CUDA events on the launching stream;
     the step time is the max over ranks."""
     import torch
@@ -356,29 +356,34 @@ def sharded_line(args, rank, world, dev, peak):
             dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         return used, [float(v) for v in stats.tolist()], int((st != 0).sum())
 
-    _, (step_ms, shard_ms, gather_ms, merge_ms), flagged = run("nccl")
-    used, (p_step, p_kernel, p_finish, _), p_flagged = run("auto")
+    used, (step_ms, k_ms, m_ms, _), flagged = run("auto")
+    _, (g_step, g_shard, g_gather, g_merge), g_flagged = run("nccl")
     alg = B * ((v1 - v0) * 4 + 52)  # this rank's logits slice and per-row parameters
+    gather = {"value": round(B / (g_step / 1e3), 1), "unit": "rows/s", "ms_per_step": round(g_step, 5),
+              "phase_us": {"shard_pass": round(g_shard * 1e3, 2), "all_gather": round(g_gather * 1e3, 2),
+                           "merge": round(g_merge * 1e3, 2)},
+              "gather_bytes_per_rank": B * sharded.record_words(50) * 4, "rows_flagged": g_flagged}
     line = {
         "workload": "config5: 1024x256000 fp32, vocab sliced over the GPUs, top_k 50, top_p 0.95, T 0.9",
-        "api": "miniserve_b200.sharded.ShardedSampler.sample", "scaling": "strong", "nccl_ranks": world,
+        "api": "miniserve_b200.sharded.ShardedSampler.sample", "scaling": "strong", "ranks": world,
+        "exchange": used,
         "value": round(B / (step_ms / 1e3), 1), "unit": "rows/s", "ms_per_step": round(step_ms, 5),
-        "phase_us": {"shard_pass": round(shard_ms * 1e3, 2), "all_gather": round(gather_ms * 1e3, 2),
-                     "merge": round(merge_ms * 1e3, 2)},
-        "gather_bytes_per_rank": B * sharded.record_words(50) * 4,
-        "per_gpu_hbm": {"achieved": round(alg / (shard_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(alg / (shard_ms / 1e3) / 1e9 / peak, 4), "kernel": "shard pass"},
         "rows_flagged": flagged, "steps": steps,
         "timing": "CUDA events per phase on the launching stream, max over ranks; device time",
     }
     if used == "peer":
-        line["peer_exchange"] = {
-            "value": round(B / (p_step / 1e3), 1), "unit": "rows/s", "ms_per_step": round(p_step, 5),
-            "phase_us": {"shard_pass_with_peer_stores": round(p_kernel * 1e3, 2),
-                         "merge_with_flag_wait": round(p_finish * 1e3, 2)},
-            "peer_bytes_per_rank": B * sharded.record_words(50) * 4 * max(world - 1, 0), "rows_flagged": p_flagged}
+        line["phase_us"] = {"shard_pass_with_peer_stores": round(k_ms * 1e3, 2),
+                            "merge_with_tag_wait": round(m_ms * 1e3, 2)}
+        line["peer_bytes_per_rank"] = B * sharded.record_words(50) * 8 * max(world - 1, 0)
+        kernel_ms, kname = k_ms, "shard pass with peer stores"
+        line["all_gather_path"] = gather
     else:
+        line["phase_us"] = gather["phase_us"]
+        line["gather_bytes_per_rank"] = gather["gather_bytes_per_rank"]
+        kernel_ms, kname = g_shard, "shard pass"
         line["peer_exchange"] = {"unavailable": "CUDA IPC mapping of the exchange buffers failed"}
+    line["per_gpu_hbm"] = {"achieved": round(alg / (kernel_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                           "frac": round(alg / (kernel_ms / 1e3) / 1e9 / peak, 4), "kernel": kname}
     return line
 
 

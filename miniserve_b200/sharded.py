@@ -10,7 +10,7 @@ every rank, which finishes each row exactly as miniserve's
 ``Sampler.sample`` (miniserve/sampler.py:23-68) does on the whole vocabulary:
 the row's top-k set is contained in the union of the slices' top-k sets.
 
-With a peer exchange (``PeerExchange``, ``exchange="peer"``) step 2 is
+With a peer exchange (``PeerExchange``, the default) step 2 is
 fused into step 1: ``ms_shard_exchange`` stores each row's record into every
 other rank's exchange buffer over NVLink as the row finishes (every word
 tagged with the call's epoch in one 8-byte store), and ``ms_exchange_merge``
@@ -241,11 +241,11 @@ def gather_rows(logits_slice, rows, V: int, group=None):
 class ShardedSampler:
     """Sample [B, V] rows whose vocabulary is split across the ranks of `group`."""
 
-    def __init__(self, V: int, group=None, exchange: str = "nccl", peer_timeout_s: float = 10.0) -> None:
-        """``exchange``: "nccl" (all-gather of the records and a merge
-        kernel), "peer" (the fused peer exchange; PeerExchangeError if CUDA
-        IPC is unavailable) or "auto" (peer when available, else nccl; the
-        choice is the same on every rank)."""
+    def __init__(self, V: int, group=None, exchange: str = "auto", peer_timeout_s: float = 10.0) -> None:
+        """``exchange``: "auto" (the fused peer exchange when CUDA IPC maps
+        every rank's buffer, else nccl; the choice is the same on every
+        rank), "peer" (PeerExchangeError if CUDA IPC is unavailable) or
+        "nccl" (all-gather of the records and a merge kernel)."""
         if exchange not in ("auto", "peer", "nccl"):
             raise ValueError("exchange must be 'auto', 'peer' or 'nccl'")
         self.V = int(V)
