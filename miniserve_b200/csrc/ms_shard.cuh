@@ -259,18 +259,46 @@ __device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row
   }
   // top-k: rank every candidate; the best min(n, k) are the row's top-k set
   const int m = min(n, k);
-  const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
-  const int npair = (n + 1) >> 1;
-  for (int i = tid; i < n; i += NT) {
-    const unsigned long long ci = sh.u.comp[i];
-    int rank = 0;
-    for (int j = 0; j < npair; ++j) {
-      const ulonglong2 q = c2[j];
-      rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
+  if (a.nranks >= 4) {
+    // many ranks: each rank's run comp[off[r], off[r+1]) is sorted (value
+    // descending, id ascending), so a candidate's rank is its place in its
+    // own run plus a binary search in every other run
+    const int N = a.nranks;
+    for (int i = tid; i < n; i += NT) {
+      int r = 0;
+      while (r + 1 < N && sh.off[r + 1] <= i) ++r;
+      const unsigned long long ci = sh.u.comp[i];
+      int rank = i - sh.off[r];
+      for (int r2 = 0; r2 < N && rank < m; ++r2) {
+        if (r2 == r) continue;
+        const int base = sh.off[r2];
+        int lo = base, hi = r2 + 1 < N ? sh.off[r2 + 1] : n;
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (sh.u.comp[mid] > ci) lo = mid + 1;
+          else hi = mid;
+        }
+        rank += lo - base;
+      }
+      if (rank < m) {
+        sh.key[rank] = (uint32_t)(ci >> 32);
+        sh.id[rank] = (int)~(uint32_t)ci;
+      }
     }
-    if (rank < m) {
-      sh.key[rank] = (uint32_t)(ci >> 32);
-      sh.id[rank] = (int)~(uint32_t)ci;
+  } else {
+    const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(sh.u.comp);
+    const int npair = (n + 1) >> 1;
+    for (int i = tid; i < n; i += NT) {
+      const unsigned long long ci = sh.u.comp[i];
+      int rank = 0;
+      for (int j = 0; j < npair; ++j) {
+        const ulonglong2 q = c2[j];
+        rank += (q.x > ci ? 1 : 0) + (q.y > ci ? 1 : 0);
+      }
+      if (rank < m) {
+        sh.key[rank] = (uint32_t)(ci >> 32);
+        sh.id[rank] = (int)~(uint32_t)ci;
+      }
     }
   }
   __syncthreads();
