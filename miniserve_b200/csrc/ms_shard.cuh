@@ -48,6 +48,7 @@ struct MgShared {
   int id[kMgCap];
   int kid[kMgCap];       // kept ids in index order
   int off[kMgRanks + 1];
+  int cnt[kMgRanks];     // per-rank candidate counts
   uint32_t st;
   float cut;             // the largest kmax-th value of a full slice
   double redd[33];
@@ -212,19 +213,26 @@ __device__ __forceinline__ void mg_row(const MergeArgs &a, MgShared &sh, int row
   if (st_r) atomicOr(&sh.st, st_r);
   int ex, inc, n;
   block_scan<NT, int>(m_r, ex, inc, n, sh.redi);  // ends with a barrier
-  if (tid < a.nranks) sh.off[tid] = ex;
+  if (tid < a.nranks) {
+    sh.off[tid] = ex;
+    sh.cnt[tid] = m_r;
+  }
   const uint32_t st = sh.st;
   if (st != 0u) {  // bad temperature, or a slice that needs the full row
     if (tid == 0) mg_write(a, row, -1, 0.0f, (int32_t)st);
     return;
   }
   __syncthreads();
-  for (int r = 0; r < a.nranks; ++r) {
-    const uint32_t *rec = mg_rec(a, r, row, rw);
-    const int mr = (int)min(mg_ld(rec), (uint32_t)a.kmax);
-    for (int i = tid; i < mr; i += NT)
+  // every (rank, slot) pair at once: the loads of all ranks' records in flight together
+  const int KM = a.kmax;
+#pragma unroll 4
+  for (int j = tid; j < a.nranks * KM; j += NT) {
+    const int r = j / KM, i = j - r * KM;
+    if (i < sh.cnt[r]) {
+      const uint32_t *rec = mg_rec(a, r, row, rw);
       sh.u.comp[sh.off[r] + i] =
-          ((unsigned long long)mg_ld(rec + 2 + i) << 32) | (unsigned long long)(~mg_ld(rec + 2 + a.kmax + i));
+          ((unsigned long long)mg_ld(rec + 2 + i) << 32) | (unsigned long long)(~mg_ld(rec + 2 + KM + i));
+    }
   }
   if (tid == 0) {
     sh.u.comp[n] = 0ull;
