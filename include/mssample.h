@@ -163,8 +163,13 @@ int ms_shard_merge(const uint32_t *records, int32_t nranks, int64_t B, int32_t k
  *      store (no fence, no wait).
  *   2. ms_exchange_merge: row by row, waits (at most timeout_ns; a stalled
  *      batch up to about twice that) until every other rank's words of the
- *      row carry the epoch, then merges it as ms_shard_merge does; rows with
- *      a word missing: token -1, MS_ROW_PEER_TIMEOUT.
+ *      row carry the epoch; row r is then merged (as ms_shard_merge does) on
+ *      rank r mod nranks, which stores the result into every rank's buffer,
+ *      tagged the same way (with one rank: straight into the outputs).
+ *   3. ms_exchange_results: waits (at most timeout_ns) for every row's
+ *      result and writes tokens, probs and statuses (nothing to do with one
+ *      rank).  A row with a word or result missing: token -1,
+ *      MS_ROW_PEER_TIMEOUT.
  *
  * epoch: the call's number, 1, 2, ... in order on every rank (with a fresh
  * buffer; it may wrap to 1 after an even number).  Bcap / kmax_cap: the
@@ -184,10 +189,14 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
                       const uint32_t *mask, int64_t mask_ld, int32_t kmax, uint32_t *xbuf, uint32_t *const *peers,
                       int32_t rank, int32_t nranks, int64_t Bcap, int32_t kmax_cap, uint32_t epoch,
                       ms_stream_t stream);
-int ms_exchange_merge(uint32_t *xbuf, int32_t rank, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+int ms_exchange_merge(uint32_t *xbuf, uint32_t *const *peers, int32_t rank, int32_t nranks, int64_t B,
+                      int64_t Bcap, int32_t kmax,
                       int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
                       const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream);
+int ms_exchange_results(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax_cap,
+                        uint32_t epoch, int64_t timeout_ns, int64_t *tokens, float *probs, int32_t *row_status,
+                        ms_stream_t stream);
 
 /*
  * Device memory for an exchange buffer and its CUDA IPC mapping into the

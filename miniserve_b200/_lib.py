@@ -60,9 +60,11 @@ SIGNATURES = {
     "ms_shard_exchange": (ctypes.c_int, [_P, ctypes.c_int, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P,
                                          _I64, ctypes.c_int32, _P, _P, ctypes.c_int32, ctypes.c_int32, _I64,
                                          ctypes.c_int32, ctypes.c_uint32, _P]),
-    "ms_exchange_merge": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _I64, _I64, ctypes.c_int32,
+    "ms_exchange_merge": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, _I64, _I64, ctypes.c_int32,
                                          ctypes.c_int32, _I64, _P, _P, _P, _P, ctypes.c_uint32, _I64, _P, _P, _P,
                                          _P]),
+    "ms_exchange_results": (ctypes.c_int, [_P, ctypes.c_int32, _I64, _I64, ctypes.c_int32, ctypes.c_uint32, _I64,
+                                           _P, _P, _P, _P]),
     "ms_device_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
     "ms_device_free": (ctypes.c_int, [_P]),
     "ms_ipc_handle": (ctypes.c_int, [_P, ctypes.c_char_p]),

@@ -291,7 +291,8 @@ int ms_shard_exchange(const void *logits, int dtype, int64_t B, int64_t Vloc, in
   return MS_OK;
 }
 
-int ms_exchange_merge(uint32_t *xbuf, int32_t rank, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax,
+int ms_exchange_merge(uint32_t *xbuf, uint32_t *const *peers, int32_t rank, int32_t nranks, int64_t B,
+                      int64_t Bcap, int32_t kmax,
                       int32_t kmax_cap, int64_t V, const double *temperature, const int32_t *top_k,
                       const double *top_p, const double *uniforms, uint32_t epoch, int64_t timeout_ns,
                       int64_t *tokens, float *probs, int32_t *row_status, ms_stream_t stream) {
@@ -300,18 +301,44 @@ int ms_exchange_merge(uint32_t *xbuf, int32_t rank, int32_t nranks, int64_t B, i
     return MS_E_INVALID;
   if ((int64_t)nranks * kmax > ms::kMgCap) return MS_E_UNSUPPORTED;
   if (B == 0) return MS_OK;
-  if (!xbuf || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
+  if (!xbuf || !peers || !temperature || !top_k || !top_p || !uniforms || !tokens || !probs || !row_status)
     return MS_E_INVALID;
   if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
+  const int64_t res = L.res0 + (int64_t)(epoch & 1u) * L.reshalf;
   const int64_t rec = L.rec0 + (int64_t)(epoch & 1u) * L.half;
   ms::MergeArgs a{xbuf + rec, nranks, (int)B, kmax, V, temperature, top_k, top_p, uniforms,
                   tokens, probs, row_status};
+  if (nranks > 1) {  // each row merged on its owner, the result stored into every rank's buffer
+    a.xpeers = peers;
+    a.xres = res;
+    a.xepoch = epoch;
+  }
   const unsigned long long *ll =
       reinterpret_cast<const unsigned long long *>(xbuf + L.ll0 + (int64_t)(epoch & 1u) * L.llhalf);
   ms::ms_xmerge_kernel<<<dim3((unsigned)B), dim3(ms::kMgThreads), 0, s>>>(a, xbuf + rec, ll, rank, epoch,
                                                                          timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e);
+  return MS_OK;
+}
+
+int ms_exchange_results(const uint32_t *xbuf, int32_t nranks, int64_t B, int64_t Bcap, int32_t kmax_cap,
+                        uint32_t epoch, int64_t timeout_ns, int64_t *tokens, float *probs, int32_t *row_status,
+                        ms_stream_t stream) {
+  if (ms_exchange_words(Bcap, nranks, kmax_cap) < 0 || B < 0 || B > Bcap || timeout_ns < 0 || epoch == 0u)
+    return MS_E_INVALID;
+  if (B == 0 || nranks == 1) return MS_OK;  // one rank: the merge wrote the outputs
+  if (!xbuf || !tokens || !probs || !row_status) return MS_E_INVALID;
+  if ((reinterpret_cast<uintptr_t>(xbuf) & 15u) != 0) return MS_E_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const ms::XLayout L = ms::x_layout(Bcap, nranks, kmax_cap);
+  const int64_t res = L.res0 + (int64_t)(epoch & 1u) * L.reshalf;
+  const unsigned grid = (unsigned)((B + ms::kXThreads - 1) / ms::kXThreads);
+  ms::ms_xresult_kernel<<<dim3(grid), dim3(ms::kXThreads), 0, s>>>(
+      reinterpret_cast<const unsigned long long *>(xbuf + res), (int)B, epoch, timeout_ns, tokens, probs,
+      row_status);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e);
   return MS_OK;

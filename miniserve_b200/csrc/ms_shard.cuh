@@ -37,7 +37,18 @@ struct MergeArgs {
   int64_t *tokens;
   float *probs;
   int32_t *status;
+  // fused peer exchange with more than one rank: the result of row r goes to
+  // every rank's buffer instead, as three 8-byte stores tagged with the
+  // call's epoch (token, prob bits, status) at 8-byte slot 4 r of word
+  // offset xres
+  uint32_t *const *xpeers = nullptr;
+  int64_t xres = 0;
+  uint32_t xepoch = 0;
 };
+
+__device__ __forceinline__ void mg_st_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 struct MgShared {
   union {
@@ -57,6 +68,16 @@ struct MgShared {
 };
 
 __device__ __forceinline__ void mg_write(const MergeArgs &a, int r, int64_t tok, float prob, int32_t st) {
+  if (a.xpeers) {
+    const unsigned long long tag = (unsigned long long)a.xepoch << 32;
+    for (int q = 0; q < a.nranks; ++q) {
+      unsigned long long *e = reinterpret_cast<unsigned long long *>(a.xpeers[q] + a.xres) + 4 * (size_t)r;
+      mg_st_sys(e, tag | (uint32_t)(int32_t)tok);
+      mg_st_sys(e + 1, tag | __float_as_uint(prob));
+      mg_st_sys(e + 2, tag | (uint32_t)st);
+    }
+    return;
+  }
   a.tokens[r] = tok;
   a.probs[r] = prob;
   a.status[r] = st;

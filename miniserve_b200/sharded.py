@@ -13,9 +13,11 @@ the row's top-k set is contained in the union of the slices' top-k sets.
 With a peer exchange (``PeerExchange``, the default) step 2 is
 fused into step 1: ``ms_shard_exchange`` stores each row's record into every
 other rank's exchange buffer over NVLink as the row finishes (every word
-tagged with the call's epoch in one 8-byte store), and ``ms_exchange_merge``
-waits (bounded) until a row's words from every rank carry the epoch before
-merging it.  No collective call is made on that path.
+tagged with the call's epoch in one 8-byte store); ``ms_exchange_merge``
+waits (bounded) until a row's words from every rank carry the epoch, and the
+row's owner (row mod world) merges it and stores the result into every
+rank's buffer the same way; ``ms_exchange_results`` collects them (bounded).
+No collective call is made on that path.
 
 A top-p row without top-k is settled from the records too when its nucleus
 lies among the candidates (the records carry each slice's softmax total);
@@ -356,10 +358,13 @@ class ShardedSampler:
                 _lib.check(rc, "ms_shard_exchange")
                 if events is not None:
                     events[1].record(cur)
-                rc = L.ms_exchange_merge(x.local, x.rank, x.world, B, x.Bcap, kmax, x.kmax_cap, self.V, T.data_ptr(),
+                rc = L.ms_exchange_merge(x.local, x.peers.data_ptr(), x.rank, x.world, B, x.Bcap, kmax, x.kmax_cap, self.V, T.data_ptr(),
                                          K.data_ptr(), P.data_ptr(), U.data_ptr(), epoch, x.timeout_ns,
                                          tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
                 _lib.check(rc, "ms_exchange_merge")
+                rc = L.ms_exchange_results(x.local, x.world, B, x.Bcap, x.kmax_cap, epoch, x.timeout_ns,
+                                           tokens.data_ptr(), probs.data_ptr(), status.data_ptr(), stream)
+                _lib.check(rc, "ms_exchange_results")
                 if events is not None:
                     events[2].record(cur)
                     events[3].record(cur)

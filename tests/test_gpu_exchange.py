@@ -1,8 +1,8 @@
 """The fused peer exchange of vocab-sharded sampling (ms_shard_exchange +
 ms_exchange_merge) on one GPU.  The ranks are emulated: every rank's
-exchange buffer is a block on this GPU and the ranks' streaming kernels run
-one after another on one stream before any merge (the streaming kernels do
-not wait; each merge finds every flag already set).
+exchange buffer is a block on this GPU, and every rank's streaming kernel
+runs before any merge, every merge before any result collection (a step that
+waits finds what it waits for already stored).
 Tokens must equal the all-gather path (ms_shard_candidates + ms_shard_merge)
 bit for bit and the oracle on the full rows.  With two GPUs the same path
 runs under torchrun (tests/mp_sharded.py).  Needs a B200."""
@@ -52,8 +52,9 @@ def _slice_mask(torch, mask, v0, v1):
 
 
 def run_exchange(torch, bufs, xt, T, K, P, U, kmax, bf16=False, mask=None, ranks=None, timeout_ns=10**9):
-    """One call of every emulated rank (or of `ranks` only); returns each
-    rank's (tokens, probs, status) as numpy arrays."""
+    """One call of every emulated rank (or of `ranks` only, the others
+    missing); returns each of those ranks' (tokens, probs, status) as numpy
+    arrays."""
     from miniserve_b200 import sharded
     L = bufs.L
     B, V = xt.shape
@@ -76,17 +77,24 @@ def run_exchange(torch, bufs, xt, T, K, P, U, kmax, bf16=False, mask=None, ranks
         assert rc == 0, rc
         torch.cuda.synchronize()
     out = []
-    for r in range(world):
+    for r in (range(world) if ranks is None else ranks):
         tok = torch.empty(B, dtype=torch.int64, device=dev)
         prob = torch.empty(B, dtype=torch.float32, device=dev)
         st = torch.empty(B, dtype=torch.int32, device=dev)
-        rc = L.ms_exchange_merge(bufs.ptrs[r], r, world, B, bufs.Bcap, kmax, bufs.kmax_cap, V, Tt.data_ptr(),
+        out.append((tok, prob, st))
+        rc = L.ms_exchange_merge(bufs.ptrs[r], bufs.peers.data_ptr(), r, world, B, bufs.Bcap, kmax, bufs.kmax_cap, V, Tt.data_ptr(),
                                  Kt.data_ptr(), Pt.data_ptr(), Ut.data_ptr(), bufs.epoch, timeout_ns, tok.data_ptr(),
                                  prob.data_ptr(), st.data_ptr(), s)
         assert rc == 0, rc
         torch.cuda.synchronize()
-        out.append((tok.cpu().numpy(), prob.cpu().numpy(), st.cpu().numpy()))
-    return out
+    # every rank's merges ran before any rank collects the results (a
+    # collection waits for other ranks' merges)
+    for r, (tok, prob, st) in zip(range(world) if ranks is None else ranks, out):
+        rc = L.ms_exchange_results(bufs.ptrs[r], world, B, bufs.Bcap, bufs.kmax_cap, bufs.epoch, timeout_ns,
+                                   tok.data_ptr(), prob.data_ptr(), st.data_ptr(), s)
+        assert rc == 0, rc
+        torch.cuda.synchronize()
+    return [(tok.cpu().numpy(), prob.cpu().numpy(), st.cpu().numpy()) for tok, prob, st in out]
 
 
 def gathered(torch, xt, T, K, P, U, world, kmax, bf16=False, mask=None):
@@ -200,8 +208,9 @@ def test_exchange_bf16_mask_and_batch_sizes(torch):
 
 def test_exchange_merge_times_out_without_peer(torch):
     """A rank that never runs its streaming kernel: its records never arrive,
-    so rank 0's merge waits its limit (2 ms here) and returns
-    MS_ROW_PEER_TIMEOUT rows with token -1; the device stays usable."""
+    so rank 0's merges wait their limit (2 ms here) and its rows come back
+    MS_ROW_PEER_TIMEOUT with token -1, and so do the rows rank 1 would have
+    merged (their results never arrive); the device stays usable."""
     x, T, K, P, U = _mixed(seed=12, B=16)
     K[:] = 20
     xt = torch.from_numpy(x).cuda()
