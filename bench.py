@@ -356,8 +356,14 @@ def sharded_line(args, rank, world, dev, peak):
             dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         return used, [float(v) for v in stats.tolist()], int((st != 0).sum())
 
-    used, (step_ms, k_ms, m_ms, _), flagged = run("auto")
+    try:
+        used, (step_ms, k_ms, m_ms, _), flagged = run("auto")
+        peer_error = None
+    except sharded.PeerExchangeError as e:  # every rank raises it (bounded waits that ran out)
+        used, peer_error = "nccl", str(e)
     _, (g_step, g_shard, g_gather, g_merge), g_flagged = run("nccl")
+    if peer_error is not None:
+        step_ms, flagged = g_step, g_flagged
     alg = B * ((v1 - v0) * 4 + 52)  # this rank's logits slice and per-row parameters
     gather = {"value": round(B / (g_step / 1e3), 1), "unit": "rows/s", "ms_per_step": round(g_step, 5),
               "phase_us": {"shard_pass": round(g_shard * 1e3, 2), "all_gather": round(g_gather * 1e3, 2),
@@ -381,7 +387,7 @@ def sharded_line(args, rank, world, dev, peak):
         line["phase_us"] = gather["phase_us"]
         line["gather_bytes_per_rank"] = gather["gather_bytes_per_rank"]
         kernel_ms, kname = g_shard, "shard pass"
-        line["peer_exchange"] = {"unavailable": "CUDA IPC mapping of the exchange buffers failed"}
+        line["peer_exchange"] = {"unavailable": peer_error or "CUDA IPC mapping of the exchange buffers failed"}
     line["per_gpu_hbm"] = {"achieved": round(alg / (kernel_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                            "frac": round(alg / (kernel_ms / 1e3) / 1e9 / peak, 4), "kernel": kname}
     return line
